@@ -1,0 +1,1232 @@
+// gguf_cuda.cu -- libgguf_cuda.so: the C ABI declared in include/gguf_cuda.h.
+//
+// One translation unit holds the context, the quant.rs entry points, device
+// tensors and the LlamaModel forward / Engine greedy loop.  Kernels live in the
+// included .cuh files.  Built with -fmad=false so that the dequantisers' f32
+// arithmetic is never contracted into FMAs (bit-exact with the reference).
+#include <cmath>
+#include <cstdarg>
+#include <cstdlib>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include <nccl.h>
+
+#include "common.cuh"
+#include "dequant.cuh"
+#include "planes.cuh"
+#include "gemv.cuh"
+#include "attention.cuh"
+
+using namespace ggc;
+
+// ===========================================================================
+// errors
+// ===========================================================================
+namespace ggc {
+ggc_error_info& tls_error() {
+    static thread_local ggc_error_info e;
+    return e;
+}
+int set_error(int status, const char* fmt, ...) {
+    ggc_error_info& e = tls_error();
+    memset(&e, 0, sizeof(e));
+    e.status = status;
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(e.message, sizeof(e.message), fmt, ap);
+    va_end(ap);
+    return status;
+}
+int set_dequant_error(int dtype, uint64_t expected, uint64_t actual, const char* what) {
+    set_error(GGC_ERR_DEQUANT, "DequantError { dtype: %s, expected: %llu, actual: %llu } (%s)", dtype_name(dtype),
+              (unsigned long long)expected, (unsigned long long)actual, what);
+    ggc_error_info& e = tls_error();
+    snprintf(e.dtype, sizeof(e.dtype), "%s", dtype_name(dtype));
+    e.expected = expected;
+    e.actual = actual;
+    return GGC_ERR_DEQUANT;
+}
+int set_shape_error(uint64_t elements, uint64_t block, const char* what) {
+    set_error(GGC_ERR_INVALID_TENSOR_SHAPE, "InvalidTensorShape { elements: %llu, block: %llu } (%s)",
+              (unsigned long long)elements, (unsigned long long)block, what);
+    tls_error().elements = elements;
+    tls_error().block = block;
+    return GGC_ERR_INVALID_TENSOR_SHAPE;
+}
+}  // namespace ggc
+
+// ===========================================================================
+// context
+// ===========================================================================
+struct ggc_ctx {
+    int device = 0;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;
+    int rank = 0, world = 1;
+    ncclComm_t comm = nullptr;
+    uint64_t launches = 0;
+    // staging buffers for host arguments
+    void* stage[3] = {nullptr, nullptr, nullptr};
+    size_t stage_cap[3] = {0, 0, 0};
+};
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+bool is_device_ptr(const void* p) {
+    if (!p) return false;
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
+}
+
+int ensure_stage(ggc_ctx* ctx, int i, size_t bytes) {
+    if (ctx->stage_cap[i] >= bytes) return GGC_OK;
+    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    if (ctx->stage[i]) cudaFree(ctx->stage[i]);
+    ctx->stage[i] = nullptr;
+    ctx->stage_cap[i] = 0;
+    size_t cap = bytes < 4096 ? 4096 : bytes;
+    GGC_CUDA_TRY(cudaMalloc(&ctx->stage[i], cap));
+    ctx->stage_cap[i] = cap;
+    return GGC_OK;
+}
+
+// Device view of a caller argument: device pointers pass through, host data is
+// copied into staging buffer `i`.
+int dev_in(ggc_ctx* ctx, int i, const void* p, size_t bytes, const void** out) {
+    if (is_device_ptr(p) || bytes == 0) { *out = p; return GGC_OK; }
+    GGC_TRY(ensure_stage(ctx, i, bytes));
+    GGC_CUDA_TRY(cudaMemcpyAsync(ctx->stage[i], p, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    *out = ctx->stage[i];
+    return GGC_OK;
+}
+int dev_out(ggc_ctx* ctx, int i, void* p, size_t bytes, void** out, bool* staged) {
+    *staged = !is_device_ptr(p);
+    if (!*staged) { *out = p; return GGC_OK; }
+    GGC_TRY(ensure_stage(ctx, i, bytes));
+    *out = ctx->stage[i];
+    return GGC_OK;
+}
+
+// Launch with programmatic stream serialization (PDL): the next kernel may be
+// scheduled while this one drains; every kernel calls griddepcontrol.wait.
+template <class... KArgs, class... Args>
+cudaError_t launch(ggc_ctx* ctx, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    ctx->launches++;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+int host_threads() {
+    unsigned h = std::thread::hardware_concurrency();
+    return h ? (int)(h > 32 ? 32 : h) : 4;
+}
+
+}  // namespace
+
+// ===========================================================================
+// quant.rs entry points
+// ===========================================================================
+namespace {
+
+template <int DT>
+struct RunDequant {
+    static void run(ggc_ctx* ctx, const uint8_t* raw, uint64_t n, float* out, cudaError_t* err) {
+        uint64_t blocks = cdiv<uint64_t>(n, 256);
+        unsigned grid = (unsigned)(blocks < (uint64_t)ctx->num_sms * 16 ? blocks : (uint64_t)ctx->num_sms * 16);
+        if (grid == 0) grid = 1;
+        *err = launch(ctx, k_dequantize<DT>, dim3(grid), dim3(256), 0, raw, n, out);
+    }
+};
+
+template <int DT>
+struct RunMatvecRaw {
+    static void run(ggc_ctx* ctx, const uint8_t* w, uint64_t rows, uint64_t cols, const float* x, float* y,
+                    cudaError_t* err) {
+        uint64_t ctas = cdiv<uint64_t>(rows, 8);
+        unsigned grid = (unsigned)(ctas < (uint64_t)ctx->num_sms * 8 ? ctas : (uint64_t)ctx->num_sms * 8);
+        if (grid == 0) grid = 1;
+        *err = launch(ctx, k_matvec_raw<DT>, dim3(grid), dim3(256), 0, w, rows, cols, x, y);
+    }
+};
+
+}  // namespace
+
+extern "C" int ggc_last_error(ggc_error_info* out) {
+    if (out) *out = tls_error();
+    return tls_error().status;
+}
+
+extern "C" int64_t ggc_block_size(int dtype) { return block_size_of(dtype); }
+extern "C" int64_t ggc_block_bytes(int dtype) { return block_bytes_of(dtype); }
+
+extern "C" int ggc_nccl_unique_id(void* out128) {
+    if (!out128) return set_error(GGC_ERR_INVALID_ARG, "null id buffer");
+    ncclUniqueId id;
+    ncclResult_t r = ncclGetUniqueId(&id);
+    if (r != ncclSuccess) return set_error(GGC_ERR_NCCL, "ncclGetUniqueId: %s", ncclGetErrorString(r));
+    memcpy(out128, &id, sizeof(id));
+    return GGC_OK;
+}
+
+static int ctx_init(ggc_ctx* c, int device) {
+    int n = 0;
+    GGC_CUDA_TRY(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n) return set_error(GGC_ERR_INVALID_ARG, "device %d out of range (%d GPUs)", device, n);
+    c->device = device;
+    DeviceGuard g(device);
+    GGC_CUDA_TRY(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device));
+    GGC_CUDA_TRY(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    return GGC_OK;
+}
+
+extern "C" int ggc_ctx_create(int device, ggc_ctx** out) {
+    if (!out) return set_error(GGC_ERR_INVALID_ARG, "null out");
+    std::unique_ptr<ggc_ctx> c(new ggc_ctx());
+    GGC_TRY(ctx_init(c.get(), device));
+    *out = c.release();
+    return GGC_OK;
+}
+
+extern "C" int ggc_ctx_create_tp(int device, int rank, int world, const void* nccl_id, ggc_ctx** out) {
+    if (!out || !nccl_id || world < 1 || rank < 0 || rank >= world)
+        return set_error(GGC_ERR_INVALID_ARG, "bad tensor-parallel arguments");
+    std::unique_ptr<ggc_ctx> c(new ggc_ctx());
+    GGC_TRY(ctx_init(c.get(), device));
+    c->rank = rank;
+    c->world = world;
+    if (world > 1) {
+        DeviceGuard g(device);
+        ncclUniqueId id;
+        memcpy(&id, nccl_id, sizeof(id));
+        ncclResult_t r = ncclCommInitRank(&c->comm, world, id, rank);
+        if (r != ncclSuccess) return set_error(GGC_ERR_NCCL, "ncclCommInitRank: %s", ncclGetErrorString(r));
+    }
+    *out = c.release();
+    return GGC_OK;
+}
+
+extern "C" int ggc_ctx_destroy(ggc_ctx* ctx) {
+    if (!ctx) return GGC_OK;
+    {
+        DeviceGuard g(ctx->device);
+        cudaStreamSynchronize(ctx->stream);
+        for (int i = 0; i < 3; ++i)
+            if (ctx->stage[i]) cudaFree(ctx->stage[i]);
+        if (ctx->comm) ncclCommDestroy(ctx->comm);
+        cudaStreamDestroy(ctx->stream);
+    }
+    delete ctx;
+    return GGC_OK;
+}
+
+extern "C" void* ggc_ctx_stream(ggc_ctx* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
+extern "C" uint64_t ggc_ctx_kernel_launches(ggc_ctx* ctx) { return ctx ? ctx->launches : 0; }
+
+extern "C" int ggc_ctx_synchronize(ggc_ctx* ctx) {
+    if (!ctx) return set_error(GGC_ERR_INVALID_ARG, "null ctx");
+    DeviceGuard g(ctx->device);
+    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    return GGC_OK;
+}
+
+// quant.rs:403-448
+extern "C" int ggc_dequantize(ggc_ctx* ctx, int dtype, const void* raw, uint64_t raw_len, uint64_t n, float* out) {
+    const int bs = block_size_of(dtype);
+    if (bs < 0) return set_dequant_error(dtype, 0, 0, "unsupported dtype");
+    if (n % (uint64_t)bs != 0) return set_shape_error(n, (uint64_t)bs, "dequantize");
+    const uint64_t need = n / bs * (uint64_t)block_bytes_of(dtype);
+    if (raw_len < need) return set_dequant_error(dtype, need, raw_len, "data shorter than tensor");
+    if (n == 0) return GGC_OK;
+    if (!ctx) return set_error(GGC_ERR_INVALID_ARG, "null ctx");
+    if (!raw || !out) return set_error(GGC_ERR_INVALID_ARG, "null buffer");
+    DeviceGuard g(ctx->device);
+    const void* draw;
+    void* dout;
+    bool staged;
+    GGC_TRY(dev_in(ctx, 0, raw, need, &draw));
+    GGC_TRY(dev_out(ctx, 1, out, n * sizeof(float), &dout, &staged));
+    cudaError_t err = cudaSuccess;
+    dispatch_dtype<RunDequant>(dtype, ctx, (const uint8_t*)draw, n, (float*)dout, &err);
+    GGC_CUDA_TRY(err);
+    if (staged) {
+        GGC_CUDA_TRY(cudaMemcpyAsync(out, dout, n * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+        GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    }
+    return GGC_OK;
+}
+
+// quant.rs:526-570 (checks in the order of :534-555)
+extern "C" int ggc_quant_matvec(ggc_ctx* ctx, int dtype, const void* w, uint64_t w_len, uint64_t rows, uint64_t cols,
+                                const float* x, uint64_t x_len, float* y, uint64_t y_len) {
+    const int bs = block_size_of(dtype), bb = block_bytes_of(dtype);
+    if (bs < 0 || bb < 0) return set_dequant_error(dtype, 0, 0, "unsupported dtype");
+    if (cols % (uint64_t)bs != 0) return set_shape_error(cols, (uint64_t)bs, "row_bytes");
+    const uint64_t rb = cols / bs * (uint64_t)bb;
+    if (x_len != cols) return set_dequant_error(dtype, cols, x_len, "x length != cols");
+    if (y_len != rows) return set_dequant_error(dtype, rows, y_len, "y length != rows");
+    if (rows * rb > w_len) return set_dequant_error(dtype, rows * rb, w_len, "w shorter than rows*row_bytes");
+    if (rows == 0) return GGC_OK;
+    if (!ctx) return set_error(GGC_ERR_INVALID_ARG, "null ctx");
+    if (!w || !y || (!x && cols)) return set_error(GGC_ERR_INVALID_ARG, "null buffer");
+    DeviceGuard g(ctx->device);
+    const void *dw, *dx;
+    void* dy;
+    bool staged;
+    GGC_TRY(dev_in(ctx, 0, w, rows * rb, &dw));
+    GGC_TRY(dev_in(ctx, 1, x, cols * sizeof(float), &dx));
+    GGC_TRY(dev_out(ctx, 2, y, rows * sizeof(float), &dy, &staged));
+    cudaError_t err = cudaSuccess;
+    dispatch_dtype<RunMatvecRaw>(dtype, ctx, (const uint8_t*)dw, rows, cols, (const float*)dx, (float*)dy, &err);
+    GGC_CUDA_TRY(err);
+    if (staged) {
+        GGC_CUDA_TRY(cudaMemcpyAsync(y, dy, rows * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+        GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    }
+    return GGC_OK;
+}
+
+// model/llama.rs:656-710
+extern "C" int ggc_infer_k_quant_dtype(uint64_t span, uint64_t n, int marked) {
+    switch (marked) {
+        case GGC_Q4_0: case GGC_Q4_1: case GGC_Q5_0: case GGC_Q5_1: case GGC_Q8_0: case GGC_Q2_K:
+        case GGC_Q3_K_S: case GGC_Q3_K_M: case GGC_Q3_K_L: case GGC_Q4_K: case GGC_Q5_K:
+        case GGC_Q6_K: case GGC_Q8_K: break;
+        default: return -1;
+    }
+    if (n == 0) return -1;
+    const int bs = block_size_of(marked);
+    const uint64_t blocks = bs == 32 ? n / 32 : n / 256;
+    if (blocks == 0) return -1;
+    const uint64_t per256 = bs == 32 ? span * 8 / blocks : span / blocks;
+    if (span % blocks > 256) return -1;
+    static const struct { uint64_t b; int dt; } table[] = {{84, GGC_Q2_K}, {110, GGC_Q3_K_S}, {114, GGC_Q3_K_M},
+                                                            {144, GGC_Q4_K}, {176, GGC_Q5_K}, {210, GGC_Q6_K},
+                                                            {292, GGC_Q8_K}};
+    for (auto& e : table)
+        if (e.b == per256) return e.dt;
+    return -1;
+}
+
+// ===========================================================================
+// device tensors in plane layout
+// ===========================================================================
+struct DevMat {
+    int dtype = -1;
+    uint32_t rows = 0, cols = 0;      // cols padded to the chunk width for float formats
+    uint32_t xcols = 0;               // logical cols
+    uint8_t* base = nullptr;          // one allocation holding all planes
+    QMat q{};
+    uint64_t bytes = 0;
+};
+
+namespace {
+
+void free_mat(DevMat& m) {
+    if (m.base) cudaFree(m.base);
+    m.base = nullptr;
+}
+
+int chunk_elems(int dt) { return plane_spec(dt).chunk_elems; }
+
+// Splits raw rows into planes on the host and uploads them.
+int upload_mat(ggc_ctx* ctx, const void* raw, uint64_t raw_bytes, int dt, uint64_t rows, uint64_t cols,
+               const uint32_t* row_src, DevMat& out) {
+    const int bs = block_size_of(dt), bb = block_bytes_of(dt);
+    PlaneSpec ps = plane_spec(dt);
+    if (bs < 0 || ps.n == 0) return set_dequant_error(dt, 0, 0, "unsupported dtype");
+    if (cols % (uint64_t)bs != 0) return set_shape_error(cols, bs, "matrix columns");
+    const uint64_t E = (uint64_t)chunk_elems(dt);
+    uint64_t pcols = cols;
+    if (cols % E != 0) {
+        if (bs != 1) return set_shape_error(cols, E, "matrix columns (chunk)");
+        pcols = (cols + E - 1) / E * E;
+    }
+    const uint64_t row_bytes = cols / bs * (uint64_t)bb;
+    if (raw_bytes < rows * row_bytes) return set_dequant_error(dt, rows * row_bytes, raw_bytes, "tensor data too short");
+    if (rows == 0 || rows > 0xFFFFFFFFull || pcols > 0xFFFFFFFFull) return set_error(GGC_ERR_INVALID_ARG, "matrix shape");
+    uint64_t pitch[4] = {0, 0, 0, 0}, off[4] = {0, 0, 0, 0}, total = 0;
+    for (int p = 0; p < ps.n; ++p) {
+        pitch[p] = plane_pitch(dt, p, pcols);
+        off[p] = total;
+        total += (rows * pitch[p] + 255) / 256 * 256;
+    }
+    std::vector<uint8_t> host(total, 0);
+    uint8_t* planes[4] = {nullptr, nullptr, nullptr, nullptr};
+    for (int p = 0; p < ps.n; ++p) planes[p] = host.data() + off[p];
+    if (bs == 1) {   // float formats: rows copied as-is, zero padded to pcols
+        for (uint64_t r = 0; r < rows; ++r)
+            memcpy(planes[0] + r * pitch[0], (const uint8_t*)raw + (uint64_t)(row_src ? row_src[r] : r) * row_bytes, row_bytes);
+    } else {
+        repack_rows_host(dt, (const uint8_t*)raw, rows, cols, row_src, planes, host_threads());
+    }
+    DevMat m;
+    m.dtype = dt;
+    m.rows = (uint32_t)rows;
+    m.cols = (uint32_t)pcols;
+    m.xcols = (uint32_t)cols;
+    m.bytes = total;
+    GGC_CUDA_TRY(cudaMalloc(&m.base, total));
+    cudaError_t e = cudaMemcpyAsync(m.base, host.data(), total, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) {
+        cudaFree(m.base);
+        return set_error(GGC_ERR_CUDA, "upload: %s", cudaGetErrorString(e));
+    }
+    for (int p = 0; p < 4; ++p) {
+        m.q.p[p] = p < ps.n ? m.base + off[p] : nullptr;
+        m.q.pitch[p] = (uint32_t)pitch[p];
+    }
+    m.q.rows = (uint32_t)rows;
+    m.q.cols = (uint32_t)pcols;
+    out = m;
+    return GGC_OK;
+}
+
+template <int DT>
+struct SetGemvSmem {
+    static void run(int* ok) {
+        if (cudaFuncSetAttribute(k_gemv<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess) *ok = 0;
+    }
+};
+
+int init_kernel_attrs() {
+    static std::once_flag once;
+    static int ok = 1;
+    std::call_once(once, [] {
+        const int dts[] = {GGC_F32, GGC_F16, GGC_BF16, GGC_Q4_0, GGC_Q4_1, GGC_Q5_0, GGC_Q5_1, GGC_Q8_0,
+                           GGC_Q2_K, GGC_Q3_K_S, GGC_Q3_K_M, GGC_Q3_K_L, GGC_Q4_K, GGC_Q5_K, GGC_Q6_K, GGC_Q8_K};
+        for (int dt : dts) dispatch_dtype<SetGemvSmem>(dt, &ok);
+        if (cudaFuncSetAttribute(k_attn_av, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024) != cudaSuccess) ok = 0;
+    });
+    if (!ok) return set_error(GGC_ERR_CUDA, "cudaFuncSetAttribute failed");
+    return GGC_OK;
+}
+
+// One k_gemv launch over up to three same-dtype segments.
+struct GemvLaunch {
+    GemvArgs a{};
+    int dtype = -1;
+    uint32_t xcols = 0;
+};
+
+template <int DT>
+struct RunGemv {
+    static void run(ggc_ctx* ctx, const GemvArgs* a, cudaError_t* err) {
+        uint32_t total = 0;
+        for (int i = 0; i < a->nseg; ++i) total += a->seg[i].groups;
+        uint32_t ctas = cdiv<uint32_t>(total, GEMV_WARPS);
+        uint32_t cap = (uint32_t)ctx->num_sms * 2;
+        if (ctas > cap) ctas = cap;
+        if (ctas == 0) ctas = 1;
+        *err = launch(ctx, k_gemv<DT>, dim3(ctas), dim3(GEMV_WARPS * 32), gemv_smem_bytes<DT>(a->cols), *a);
+    }
+};
+
+int run_gemv(ggc_ctx* ctx, int dt, const GemvArgs& a) {
+    cudaError_t err = cudaSuccess;
+    if (!dispatch_dtype<RunGemv>(dt, ctx, &a, &err)) return set_dequant_error(dt, 0, 0, "gemv dtype");
+    GGC_CUDA_TRY(err);
+    return GGC_OK;
+}
+
+Seg make_seg(const DevMat& m, int epi, float* out, void* cache, const float* bias) {
+    Seg s{};
+    s.m = m.q;
+    s.epi = epi;
+    s.out = out;
+    s.cache = cache;
+    s.bias = bias;
+    s.groups = cdiv<uint32_t>(m.rows, GEMV_R);
+    return s;
+}
+
+}  // namespace
+
+struct ggc_tensor {
+    ggc_ctx* ctx = nullptr;
+    int dtype = -1;
+    uint64_t ne[4] = {1, 1, 1, 1};
+    int ndim = 0;
+    bool repacked = false;
+    DevMat mat;               // repacked planes
+    uint8_t* raw = nullptr;   // raw bytes when not repacked
+    uint64_t raw_bytes = 0;
+    uint64_t n_elements = 0;
+};
+
+extern "C" int ggc_tensor_upload(ggc_ctx* ctx, const void* raw, uint64_t bytes, int dtype, const uint64_t* ne, int ndim,
+                                 int repack, ggc_tensor** out) {
+    if (!ctx || !raw || !ne || !out || ndim < 1 || ndim > 4) return set_error(GGC_ERR_INVALID_ARG, "bad upload arguments");
+    const int bs = block_size_of(dtype), bb = block_bytes_of(dtype);
+    if (bs < 0) return set_dequant_error(dtype, 0, 0, "unsupported dtype");
+    DeviceGuard g(ctx->device);
+    GGC_TRY(init_kernel_attrs());
+    std::unique_ptr<ggc_tensor> t(new ggc_tensor());
+    t->ctx = ctx;
+    t->dtype = dtype;
+    t->ndim = ndim;
+    uint64_t n = 1;
+    for (int i = 0; i < ndim; ++i) { t->ne[i] = ne[i]; n *= ne[i]; }
+    t->n_elements = n;
+    if (n % (uint64_t)bs != 0) return set_shape_error(n, bs, "tensor elements");
+    const uint64_t need = n / bs * (uint64_t)bb;
+    if (bytes < need) return set_dequant_error(dtype, need, bytes, "tensor data too short");
+    const uint64_t cols = ne[0], rows = n / (cols ? cols : 1);
+    if (repack) {
+        GGC_TRY(upload_mat(ctx, raw, bytes, dtype, rows, cols, nullptr, t->mat));
+        t->repacked = true;
+    } else {
+        GGC_CUDA_TRY(cudaMalloc(&t->raw, need));
+        GGC_CUDA_TRY(cudaMemcpy(t->raw, raw, need, cudaMemcpyHostToDevice));
+        t->raw_bytes = need;
+    }
+    *out = t.release();
+    return GGC_OK;
+}
+
+extern "C" int ggc_tensor_free(ggc_tensor* t) {
+    if (!t) return GGC_OK;
+    DeviceGuard g(t->ctx->device);
+    cudaStreamSynchronize(t->ctx->stream);
+    free_mat(t->mat);
+    if (t->raw) cudaFree(t->raw);
+    delete t;
+    return GGC_OK;
+}
+
+extern "C" int ggc_tensor_matvec(ggc_ctx* ctx, const ggc_tensor* t, const float* x, float* y) {
+    if (!ctx || !t || !x || !y) return set_error(GGC_ERR_INVALID_ARG, "null argument");
+    DeviceGuard g(ctx->device);
+    const uint64_t cols = t->ne[0], rows = t->n_elements / (cols ? cols : 1);
+    const void* dx;
+    void* dy;
+    bool staged;
+    GGC_TRY(dev_in(ctx, 1, x, cols * sizeof(float), &dx));
+    GGC_TRY(dev_out(ctx, 2, y, rows * sizeof(float), &dy, &staged));
+    if (t->repacked) {
+        GemvArgs a{};
+        a.seg[0] = make_seg(t->mat, EPI_STORE, (float*)dy, nullptr, nullptr);
+        a.nseg = 1;
+        a.pro = PRO_PLAIN;
+        a.x = (const float*)dx;
+        a.cols = t->mat.cols;
+        a.xcols = t->mat.xcols;
+        GGC_TRY(run_gemv(ctx, t->dtype, a));
+    } else {
+        cudaError_t err = cudaSuccess;
+        dispatch_dtype<RunMatvecRaw>(t->dtype, ctx, (const uint8_t*)t->raw, rows, cols, (const float*)dx, (float*)dy, &err);
+        GGC_CUDA_TRY(err);
+    }
+    if (staged) {
+        GGC_CUDA_TRY(cudaMemcpyAsync(y, dy, rows * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+        GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    }
+    return GGC_OK;
+}
+
+extern "C" int ggc_tensor_dequantize(ggc_ctx* ctx, const ggc_tensor* t, float* out) {
+    if (!ctx || !t || !out) return set_error(GGC_ERR_INVALID_ARG, "null argument");
+    if (t->repacked) return set_error(GGC_ERR_INVALID_ARG, "tensor was uploaded in plane layout; upload with repack=0");
+    return ggc_dequantize(ctx, t->dtype, t->raw, t->raw_bytes, t->n_elements, out);
+}
+
+// ===========================================================================
+// LlamaModel
+// ===========================================================================
+namespace ggc {
+// Device-side state of the token loop (Engine::generate, engine.rs:89-138).
+struct StepState {
+    int32_t in_idx;     // next prompt token to consume
+    int32_t n_in;       // prompt tokens of this run
+    int32_t max_new;    // sampling budget (max_tokens)
+    int32_t eos;        // < 0: none
+    int32_t n_out;      // tokens generated in this run
+    int32_t done;       // run finished (EOS, budget, or error)
+    uint32_t tok;       // token of the current step
+    uint32_t slot;      // KV cache length before this step (= write index)
+    int64_t pos;        // position of the current step
+    int64_t next_pos;
+    uint32_t next_tok;
+    uint32_t max_ctx;
+};
+}  // namespace ggc
+
+namespace {
+
+__global__ void k_step_begin(StepState* st, const uint32_t* in_tok, const int64_t* in_pos,
+                             unsigned long long* argmax_key, int* errf) {
+    pdl_trigger();
+    pdl_wait();
+    if (threadIdx.x != 0 || st->done) return;
+    if (st->in_idx < st->n_in) {
+        st->tok = in_tok[st->in_idx];
+        st->pos = in_pos[st->in_idx];
+        st->in_idx += 1;
+    } else {
+        st->tok = st->next_tok;
+        st->pos = st->next_pos;
+    }
+    *argmax_key = 0ull;
+    if (st->slot >= st->max_ctx) {   // KvCacheOverflow (error.rs:46-51)
+        errf[ERRF_KV_OVERFLOW] = (int)st->slot + 1;
+        st->done = 1;
+    } else if (st->pos < 0 || st->pos >= (int64_t)st->max_ctx) {
+        errf[ERRF_BAD_POS] = 1;
+        st->done = 1;
+    }
+}
+
+__global__ void k_step_end(StepState* st, const unsigned long long* argmax_key, uint32_t* out_ids, int* errf) {
+    pdl_trigger();
+    pdl_wait();
+    if (threadIdx.x != 0 || st->done) return;
+    st->slot += 1;   // this step's K/V were appended
+    for (int i = 0; i < ERRF_COUNT; ++i)
+        if (errf[i]) { st->done = 1; return; }
+    if (st->in_idx < st->n_in) return;          // inside the prompt: logits not sampled
+    if (st->n_out >= st->max_new) { st->done = 1; return; }
+    const uint32_t id = (uint32_t)(*argmax_key & 0xFFFFFFFFull);   // Sampler greedy (sampler.rs:113-123)
+    if (st->eos >= 0 && (int64_t)id == (int64_t)st->eos) { st->done = 1; return; }
+    out_ids[st->n_out] = id;
+    st->n_out += 1;
+    st->next_tok = id;
+    st->next_pos = st->pos + 1;
+}
+
+// Greedy-samples the last forward's logits to start a decode continuation
+// (the first `sample` of the engine.rs:104-138 loop).
+__global__ void k_decode_start(StepState* st, const unsigned long long* argmax_key, uint32_t* out_ids, int* errf) {
+    pdl_trigger();
+    pdl_wait();
+    if (threadIdx.x != 0 || st->done) return;
+    if (st->max_new <= 0 || errf[ERRF_NAN_LOGITS]) { st->done = 1; return; }
+    const uint32_t id = (uint32_t)(*argmax_key & 0xFFFFFFFFull);
+    if (st->eos >= 0 && (int64_t)id == (int64_t)st->eos) { st->done = 1; return; }
+    out_ids[0] = id;
+    st->n_out = 1;
+    st->next_tok = id;
+    st->next_pos = st->pos + 1;
+}
+
+template <int DT>
+__global__ void __launch_bounds__(256) k_embed(const uint8_t* __restrict__ raw, uint64_t n_rows, uint32_t d,
+                                               StepState* st, float* __restrict__ hidden, int* __restrict__ errf) {
+    constexpr int BS = block_size_of(DT), BB = block_bytes_of(DT);
+    pdl_trigger();
+    pdl_wait();
+    if (st->done) return;
+    const uint32_t tok = st->tok;
+    if ((uint64_t)tok >= n_rows) {   // llama.rs:374-379 embed out of bounds
+        if (threadIdx.x == 0 && blockIdx.x == 0) { errf[ERRF_EMBED_OOB] = (int)tok + 1; }
+        return;
+    }
+    const uint64_t row_bytes = (uint64_t)(d / BS) * BB;
+    const uint8_t* row = raw + (uint64_t)tok * row_bytes;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < d; i += gridDim.x * blockDim.x) {
+        const uint32_t blk = i / BS;
+        hidden[i] = deq_elem<DT>(row + (uint64_t)blk * BB, (int)(i - blk * BS));
+    }
+}
+
+template <int DT>
+struct RunEmbed {
+    static void run(ggc_ctx* ctx, const uint8_t* raw, uint64_t rows, uint32_t d, StepState* st, float* hidden, int* errf,
+                    cudaError_t* err) {
+        unsigned grid = cdiv<uint32_t>(d, 256);
+        *err = launch(ctx, k_embed<DT>, dim3(grid), dim3(256), 0, raw, rows, d, st, hidden, errf);
+    }
+};
+
+}  // namespace
+
+struct ModelLayer {
+    float* attn_norm = nullptr;
+    float* ffn_norm = nullptr;
+    float* bq = nullptr;
+    float* bk = nullptr;
+    float* bv = nullptr;
+    DevMat wq, wk, wv, wo, up, gate, down;
+};
+
+struct ggc_model {
+    ggc_ctx* ctx = nullptr;
+    ggc_hparams hp{};
+    uint32_t hd = 0, qdim = 0, kvdim = 0, nsplit = 1;
+    int embd_dtype = -1;
+    uint8_t* embd = nullptr;
+    uint64_t embd_rows = 0;
+    float* output_norm = nullptr;
+    DevMat output;
+    std::vector<ModelLayer> layers;
+    void* kcache = nullptr;
+    void* vcache = nullptr;
+    size_t kv_elem = 4;
+    float2* rope = nullptr;
+    // activations / scratch
+    float *hidden = nullptr, *q = nullptr, *o = nullptr, *ubuf = nullptr, *gbuf = nullptr, *logits = nullptr;
+    float *scores = nullptr, *pmax = nullptr, *opart = nullptr;
+    float2* stats = nullptr;
+    unsigned* tickets = nullptr;
+    unsigned long long* argmax_key = nullptr;
+    int* errf = nullptr;
+    StepState* st = nullptr;
+    uint32_t* in_tok = nullptr;
+    int64_t* in_pos = nullptr;
+    uint32_t* out_ids = nullptr;
+    // pinned host mirror for readback
+    struct Readback {
+        int32_t ctl[6];
+        StepState st;
+        int errf[ERRF_COUNT];
+        unsigned long long key;
+    }* rb = nullptr;
+    cudaGraphExec_t graph = nullptr;
+    uint64_t launches_per_step = 0;
+    uint64_t cache_len = 0;
+    std::vector<void*> allocs;
+};
+
+namespace {
+
+template <class T>
+int dalloc(ggc_model* m, T** p, size_t count) {
+    void* q = nullptr;
+    GGC_CUDA_TRY(cudaMalloc(&q, count * sizeof(T) + 16));
+    GGC_CUDA_TRY(cudaMemset(q, 0, count * sizeof(T) + 16));
+    m->allocs.push_back(q);
+    *p = (T*)q;
+    return GGC_OK;
+}
+
+// dequantises a (norm / bias) tensor to an f32 device vector (LlamaModel::materialize)
+int upload_vec(ggc_model* m, const ggc_tensor_desc& t, uint64_t expect, float** out, const char* what) {
+    *out = nullptr;
+    if (!t.data) return GGC_OK;
+    const int bs = block_size_of(t.dtype), bb = block_bytes_of(t.dtype);
+    if (bs < 0) return set_dequant_error(t.dtype, 0, 0, what);
+    const uint64_t elements = t.nbytes / (uint64_t)bb * (uint64_t)bs;   // llama.rs:765-767
+    if (elements != t.n_elements)
+        return set_error(GGC_ERR_INFERENCE, "materialize(%s): dequantized length %llu != num_elements %llu", what,
+                         (unsigned long long)elements, (unsigned long long)t.n_elements);
+    if (expect && elements != expect)
+        return set_error(GGC_ERR_INFERENCE, "%s: %llu elements, expected %llu", what, (unsigned long long)elements,
+                         (unsigned long long)expect);
+    float* d = nullptr;
+    GGC_TRY(dalloc(m, &d, elements));
+    GGC_TRY(ggc_dequantize(m->ctx, t.dtype, t.data, t.nbytes, elements, d));
+    GGC_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    *out = d;
+    return GGC_OK;
+}
+
+int upload_weight(ggc_model* m, const ggc_tensor_desc& t, uint64_t rows, uint64_t cols, const uint32_t* row_src,
+                  DevMat& out, const char* what) {
+    if (!t.data) return set_error(GGC_ERR_MISSING_TENSOR, "MissingTensor { name: %s, kind: tensor }", what);
+    if (t.n_elements != rows * cols)
+        return set_dequant_error(GGC_F32, rows * cols, t.n_elements, what);   // matvec_colmajor_trans size check
+    return upload_mat(m->ctx, t.data, t.nbytes, t.dtype, rows, cols, row_src, out);
+}
+
+// RoPE pair order: plane row 2m / 2m+1 = logical rows h hd + j / h hd + j + hd/2
+std::vector<uint32_t> rope_row_order(uint32_t heads, uint32_t hd) {
+    std::vector<uint32_t> v((size_t)heads * hd);
+    const uint32_t half = hd / 2;
+    for (uint32_t h = 0; h < heads; ++h)
+        for (uint32_t j = 0; j < half; ++j) {
+            const uint32_t mm = h * half + j;
+            v[2 * mm] = h * hd + j;
+            v[2 * mm + 1] = h * hd + j + half;
+        }
+    return v;
+}
+
+// Group segments by dtype into as few k_gemv launches as possible.
+int run_segments(ggc_model* m, std::vector<std::pair<int, Seg>> segs, int pro, const float* x, const float* x2,
+                 uint32_t cols, uint32_t xcols, const GemvArgs& tmpl) {
+    while (!segs.empty()) {
+        const int dt = segs.front().first;
+        GemvArgs a = tmpl;
+        a.nseg = 0;
+        std::vector<std::pair<int, Seg>> rest;
+        for (auto& s : segs) {
+            if (s.first == dt && a.nseg < 3) a.seg[a.nseg++] = s.second;
+            else rest.push_back(s);
+        }
+        a.pro = pro;
+        a.x = x;
+        a.x2 = x2;
+        a.cols = cols;
+        a.xcols = xcols;
+        GGC_TRY(run_gemv(m->ctx, dt, a));
+        segs.swap(rest);
+    }
+    return GGC_OK;
+}
+
+// Enqueues one decode step (one token through every layer) on the context stream.
+int enqueue_step(ggc_model* m) {
+    ggc_ctx* ctx = m->ctx;
+    const ggc_hparams& hp = m->hp;
+    const uint32_t d = hp.embed_dim, f = hp.ffn_dim;
+    GGC_CUDA_TRY(launch(ctx, k_step_begin, dim3(1), dim3(32), 0, m->st, (const uint32_t*)m->in_tok,
+                        (const int64_t*)m->in_pos, m->argmax_key, m->errf));
+    cudaError_t err = cudaSuccess;
+    dispatch_dtype<RunEmbed>(m->embd_dtype, ctx, (const uint8_t*)m->embd, m->embd_rows, d, m->st, m->hidden, m->errf, &err);
+    GGC_CUDA_TRY(err);
+    GemvArgs base{};
+    base.st_done = &m->st->done;
+    base.slot = &m->st->slot;
+    base.pos = &m->st->pos;
+    base.rope = m->rope;
+    base.hd = m->hd;
+    base.kv_f16 = hp.kv_f16 ? 1 : 0;
+    base.errf = m->errf;
+    base.argmax_key = m->argmax_key;
+    const size_t layer_kv = (size_t)hp.max_ctx * m->kvdim * m->kv_elem;
+    for (uint32_t l = 0; l < hp.n_layers; ++l) {
+        ModelLayer& L = m->layers[l];
+        void* kc = (uint8_t*)m->kcache + l * layer_kv;
+        void* vc = (uint8_t*)m->vcache + l * layer_kv;
+        // attention_block (llama.rs:417-495): rmsnorm -> q/k/v (+bias, RoPE, cache append)
+        GGC_TRY(run_segments(m,
+                             {{L.wq.dtype, make_seg(L.wq, EPI_ROPE_Q, m->q, nullptr, L.bq)},
+                              {L.wk.dtype, make_seg(L.wk, EPI_ROPE_KC, nullptr, kc, L.bk)},
+                              {L.wv.dtype, make_seg(L.wv, EPI_VC, nullptr, vc, L.bv)}},
+                             PRO_RMSNORM, m->hidden, L.attn_norm, L.wq.cols, d, base));
+        AttnArgs aa{};
+        aa.q = m->q;
+        aa.kc = kc;
+        aa.vc = vc;
+        aa.scores = m->scores;
+        aa.pmax = m->pmax;
+        aa.stats = m->stats;
+        aa.opart = m->opart;
+        aa.o = m->o;
+        aa.tickets = m->tickets;
+        aa.slot = &m->st->slot;
+        aa.pos = &m->st->pos;
+        aa.done = &m->st->done;
+        aa.n_heads = hp.n_heads;
+        aa.kvh = hp.n_kv_heads;
+        aa.hd = m->hd;
+        aa.max_ctx = hp.max_ctx;
+        aa.nsplit = m->nsplit;
+        aa.inv = 1.0f / sqrtf((float)m->hd);
+        aa.kv_f16 = base.kv_f16;
+        GGC_CUDA_TRY(launch(ctx, k_attn_scores, dim3(hp.n_kv_heads, m->nsplit), dim3(ATTN_WARPS * 32), 0, aa));
+        GGC_CUDA_TRY(launch(ctx, k_attn_av, dim3(hp.n_kv_heads, m->nsplit), dim3(ATTN_WARPS * 32),
+                            attn_av_smem(hp.n_heads / hp.n_kv_heads, m->hd), aa));
+        // output projection + residual (llama.rs:485, :309-311), NaN guard (:300-307)
+        GemvArgs ro = base;
+        ro.err_slot = ERRF_NAN_ATTN;
+        ro.err_val = (int)l + 1;
+        GGC_TRY(run_segments(m, {{L.wo.dtype, make_seg(L.wo, EPI_RESID, m->hidden, nullptr, nullptr)}}, PRO_PLAIN, m->o,
+                             nullptr, L.wo.cols, L.wo.xcols, ro));
+        // ffn_block (llama.rs:547-580): rmsnorm -> up, gate -> silu(gate)*up -> down + residual
+        GGC_TRY(run_segments(m,
+                             {{L.up.dtype, make_seg(L.up, EPI_STORE, m->ubuf, nullptr, nullptr)},
+                              {L.gate.dtype, make_seg(L.gate, EPI_STORE, m->gbuf, nullptr, nullptr)}},
+                             PRO_RMSNORM, m->hidden, L.ffn_norm, L.up.cols, d, base));
+        GemvArgs rd = base;
+        rd.err_slot = ERRF_NAN_FFN;
+        rd.err_val = (int)l + 1;
+        GGC_TRY(run_segments(m, {{L.down.dtype, make_seg(L.down, EPI_RESID, m->hidden, nullptr, nullptr)}}, PRO_SWIGLU,
+                             m->gbuf, m->ubuf, L.down.cols, f, rd));
+    }
+    // final norm + lm_head for the last token only (llama.rs:333, :582-616) + greedy argmax
+    GemvArgs lh = base;
+    lh.st_skip = &m->st->in_idx;   // skip while in_idx < n_in (a prompt token that is not the last)
+    GGC_TRY(run_segments(m, {{m->output.dtype, make_seg(m->output, EPI_LOGITS, m->logits, nullptr, nullptr)}},
+                         PRO_RMSNORM, m->hidden, m->output_norm, m->output.cols, d, lh));
+    GGC_CUDA_TRY(launch(ctx, k_step_end, dim3(1), dim3(32), 0, m->st, (const unsigned long long*)m->argmax_key,
+                        m->out_ids, m->errf));
+    return GGC_OK;
+}
+
+int build_graph(ggc_model* m) {
+    ggc_ctx* ctx = m->ctx;
+    uint64_t before = ctx->launches;
+    cudaGraph_t g = nullptr;
+    GGC_CUDA_TRY(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+    int st = enqueue_step(m);
+    cudaError_t e = cudaStreamEndCapture(ctx->stream, &g);
+    if (st != GGC_OK) {
+        if (g) cudaGraphDestroy(g);
+        return st;
+    }
+    GGC_CUDA_TRY(e);
+    e = cudaGraphInstantiate(&m->graph, g, 0);
+    cudaGraphDestroy(g);
+    GGC_CUDA_TRY(e);
+    m->launches_per_step = ctx->launches - before;
+    ctx->launches = before;
+    return GGC_OK;
+}
+
+void destroy_model(ggc_model* m) {
+    if (!m) return;
+    DeviceGuard g(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    if (m->graph) cudaGraphExecDestroy(m->graph);
+    for (auto& L : m->layers) {
+        free_mat(L.wq); free_mat(L.wk); free_mat(L.wv); free_mat(L.wo);
+        free_mat(L.up); free_mat(L.gate); free_mat(L.down);
+    }
+    free_mat(m->output);
+    for (void* p : m->allocs) cudaFree(p);
+    if (m->rb) cudaFreeHost(m->rb);
+    delete m;
+}
+
+}  // namespace
+
+extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const ggc_tensor_desc* t, uint64_t n_tensors,
+                                ggc_model** out) {
+    if (!ctx || !hp_in || !t || !out) return set_error(GGC_ERR_INVALID_ARG, "null argument");
+    const ggc_hparams hp = *hp_in;
+    if (n_tensors != 3 + 12ull * hp.n_layers)
+        return set_error(GGC_ERR_MISSING_TENSOR, "expected %llu tensors, got %llu",
+                         (unsigned long long)(3 + 12ull * hp.n_layers), (unsigned long long)n_tensors);
+    if (hp.n_heads == 0 || hp.n_kv_heads == 0 || hp.embed_dim % hp.n_heads != 0 || hp.n_heads % hp.n_kv_heads != 0)
+        return set_error(GGC_ERR_INFERENCE, "unsupported head configuration");
+    if (ctx->world > 1) return set_error(GGC_ERR_INVALID_ARG, "tensor-parallel model: use ggc_model_create on a TP context (not yet built)");
+    const uint32_t hd = hp.embed_dim / hp.n_heads;
+    if (hd % 2 != 0 || hd > 256 || hp.n_heads / hp.n_kv_heads > ATTN_MAX_G)
+        return set_error(GGC_ERR_INFERENCE, "head_dim %u / GQA group %u not supported", hd, hp.n_heads / hp.n_kv_heads);
+    if (hp.max_ctx == 0) return set_error(GGC_ERR_INVALID_ARG, "max_ctx must be > 0");
+    DeviceGuard g(ctx->device);
+    GGC_TRY(init_kernel_attrs());
+    std::unique_ptr<ggc_model, void (*)(ggc_model*)> m(new ggc_model(), destroy_model);
+    m->ctx = ctx;
+    m->hp = hp;
+    m->hd = hd;
+    m->qdim = hp.n_heads * hd;
+    m->kvdim = hp.n_kv_heads * hd;
+    m->kv_elem = hp.kv_f16 ? 2 : 4;
+    const uint32_t d = hp.embed_dim, f = hp.ffn_dim;
+    // token_embd: kept raw, one row dequantised per token
+    {
+        const ggc_tensor_desc& e = t[0];
+        if (!e.data) return set_error(GGC_ERR_MISSING_TENSOR, "MissingTensor { name: token_embd, kind: tensor }");
+        const int bs = block_size_of(e.dtype), bb = block_bytes_of(e.dtype);
+        if (bs < 0) return set_dequant_error(e.dtype, 0, 0, "token_embd");
+        if (d % bs != 0) return set_shape_error(d, bs, "token_embd row");
+        const uint64_t row_bytes = (uint64_t)d / bs * bb;
+        m->embd_rows = e.nbytes / row_bytes;
+        m->embd_dtype = e.dtype;
+        GGC_TRY(dalloc(m.get(), &m->embd, m->embd_rows * row_bytes));
+        GGC_CUDA_TRY(cudaMemcpy(m->embd, e.data, m->embd_rows * row_bytes, cudaMemcpyHostToDevice));
+    }
+    GGC_TRY(upload_vec(m.get(), t[1], d, &m->output_norm, "output_norm"));
+    if (!m->output_norm) return set_error(GGC_ERR_MISSING_TENSOR, "MissingTensor { name: output_norm, kind: tensor }");
+    GGC_TRY(upload_weight(m.get(), t[2], hp.vocab_size, d, nullptr, m->output, "output"));
+    const std::vector<uint32_t> qorder = rope_row_order(hp.n_heads, hd), korder = rope_row_order(hp.n_kv_heads, hd);
+    m->layers.resize(hp.n_layers);
+    for (uint32_t l = 0; l < hp.n_layers; ++l) {
+        const ggc_tensor_desc* L = t + 3 + 12 * l;
+        ModelLayer& ML = m->layers[l];
+        GGC_TRY(upload_vec(m.get(), L[0], d, &ML.attn_norm, "attn_norm"));
+        if (!ML.attn_norm) return set_error(GGC_ERR_MISSING_TENSOR, "MissingTensor { name: blk.%u.attn_norm, kind: tensor }", l);
+        GGC_TRY(upload_weight(m.get(), L[1], m->qdim, d, qorder.data(), ML.wq, "attn_q"));
+        GGC_TRY(upload_vec(m.get(), L[2], m->qdim, &ML.bq, "attn_q.bias"));
+        GGC_TRY(upload_weight(m.get(), L[3], m->kvdim, d, korder.data(), ML.wk, "attn_k"));
+        GGC_TRY(upload_vec(m.get(), L[4], m->kvdim, &ML.bk, "attn_k.bias"));
+        GGC_TRY(upload_weight(m.get(), L[5], m->kvdim, d, nullptr, ML.wv, "attn_v"));
+        GGC_TRY(upload_vec(m.get(), L[6], m->kvdim, &ML.bv, "attn_v.bias"));
+        GGC_TRY(upload_weight(m.get(), L[7], d, m->qdim, nullptr, ML.wo, "attn_output"));
+        GGC_TRY(upload_vec(m.get(), L[8], d, &ML.ffn_norm, "ffn_norm"));
+        if (!ML.ffn_norm) return set_error(GGC_ERR_MISSING_TENSOR, "MissingTensor { name: blk.%u.ffn_norm, kind: tensor }", l);
+        GGC_TRY(upload_weight(m.get(), L[9], f, d, nullptr, ML.up, "ffn_up"));
+        GGC_TRY(upload_weight(m.get(), L[10], f, d, nullptr, ML.gate, "ffn_gate"));
+        GGC_TRY(upload_weight(m.get(), L[11], d, f, nullptr, ML.down, "ffn_down"));
+    }
+    // KV cache resident in HBM: [layer][max_ctx][n_kv][hd]
+    const size_t kv_bytes = (size_t)hp.n_layers * hp.max_ctx * m->kvdim * m->kv_elem;
+    GGC_TRY(dalloc(m.get(), (uint8_t**)&m->kcache, kv_bytes));
+    GGC_TRY(dalloc(m.get(), (uint8_t**)&m->vcache, kv_bytes));
+    // RoPE table with the reference's f32 arithmetic (ops.rs:326-330, llama.rs:778-782)
+    {
+        const uint32_t half = hd / 2;
+        std::vector<float> inv(half);
+        for (uint32_t i = 0; i < half; ++i) inv[i] = (float)std::pow(hp.rope_freq_base, -2.0 * (double)i / (double)hd);
+        std::vector<float2> tab((size_t)hp.max_ctx * half);
+        for (uint32_t p = 0; p < hp.max_ctx; ++p)
+            for (uint32_t i = 0; i < half; ++i) {
+                const float angle = (float)p * inv[i];
+                tab[(size_t)p * half + i] = make_float2(cosf(angle), sinf(angle));
+            }
+        GGC_TRY(dalloc(m.get(), &m->rope, tab.size()));
+        GGC_CUDA_TRY(cudaMemcpy(m->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    }
+    uint32_t ns = cdiv<uint32_t>((uint32_t)ctx->num_sms * 2, hp.n_kv_heads);
+    m->nsplit = ns < 1 ? 1 : (ns > 64 ? 64 : ns);
+    GGC_TRY(dalloc(m.get(), &m->hidden, d));
+    GGC_TRY(dalloc(m.get(), &m->q, m->qdim));
+    GGC_TRY(dalloc(m.get(), &m->o, m->qdim));
+    GGC_TRY(dalloc(m.get(), &m->ubuf, f));
+    GGC_TRY(dalloc(m.get(), &m->gbuf, f));
+    GGC_TRY(dalloc(m.get(), &m->logits, hp.vocab_size));
+    GGC_TRY(dalloc(m.get(), &m->scores, (size_t)hp.n_heads * hp.max_ctx));
+    GGC_TRY(dalloc(m.get(), &m->pmax, (size_t)hp.n_heads * m->nsplit));
+    GGC_TRY(dalloc(m.get(), &m->stats, hp.n_heads));
+    GGC_TRY(dalloc(m.get(), &m->opart, (size_t)m->nsplit * m->qdim));
+    GGC_TRY(dalloc(m.get(), &m->tickets, 2 * hp.n_kv_heads));
+    GGC_TRY(dalloc(m.get(), &m->argmax_key, 1));
+    GGC_TRY(dalloc(m.get(), &m->errf, ERRF_COUNT));
+    GGC_TRY(dalloc(m.get(), &m->st, 1));
+    GGC_TRY(dalloc(m.get(), &m->in_tok, hp.max_ctx));
+    GGC_TRY(dalloc(m.get(), &m->in_pos, hp.max_ctx));
+    GGC_TRY(dalloc(m.get(), &m->out_ids, hp.max_ctx));
+    GGC_CUDA_TRY(cudaMallocHost((void**)&m->rb, sizeof(*m->rb)));
+    StepState s0{};
+    s0.done = 1;
+    s0.max_ctx = hp.max_ctx;
+    GGC_CUDA_TRY(cudaMemcpy(m->st, &s0, sizeof(s0), cudaMemcpyHostToDevice));
+    GGC_TRY(build_graph(m.get()));
+    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    *out = m.release();
+    return GGC_OK;
+}
+
+extern "C" int ggc_model_destroy(ggc_model* m) {
+    destroy_model(m);
+    return GGC_OK;
+}
+
+namespace {
+
+// Runs `steps` graph replays after setting the control block, then reads back.
+int run_steps(ggc_model* m, uint64_t n_in, uint64_t max_new, int64_t eos, uint64_t steps) {
+    ggc_ctx* ctx = m->ctx;
+    int32_t ctl[6] = {0, (int32_t)n_in, (int32_t)max_new, (int32_t)(eos < 0 ? -1 : eos), 0, 0};
+    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));   // the pinned control block may still be in flight
+    memcpy(&m->rb->ctl, ctl, sizeof(ctl));
+    GGC_CUDA_TRY(cudaMemcpyAsync(m->st, &m->rb->ctl, sizeof(ctl), cudaMemcpyHostToDevice, ctx->stream));
+    for (uint64_t i = 0; i < steps; ++i) {
+        GGC_CUDA_TRY(cudaGraphLaunch(m->graph, ctx->stream));
+        ctx->launches += m->launches_per_step;
+    }
+    GGC_CUDA_TRY(cudaMemcpyAsync(&m->rb->st, m->st, sizeof(StepState), cudaMemcpyDeviceToHost, ctx->stream));
+    GGC_CUDA_TRY(cudaMemcpyAsync(m->rb->errf, m->errf, sizeof(int) * ERRF_COUNT, cudaMemcpyDeviceToHost, ctx->stream));
+    GGC_CUDA_TRY(cudaMemcpyAsync(&m->rb->key, m->argmax_key, sizeof(unsigned long long), cudaMemcpyDeviceToHost, ctx->stream));
+    return GGC_OK;
+}
+
+int check_run(ggc_model* m) {
+    const int* e = m->rb->errf;
+    m->cache_len = m->rb->st.slot;
+    int status = GGC_OK;
+    if (e[ERRF_EMBED_OOB]) status = set_error(GGC_ERR_INFERENCE, "embed out of bounds: tok=%d", e[ERRF_EMBED_OOB] - 1);
+    else if (e[ERRF_NAN_ATTN]) status = set_error(GGC_ERR_INFERENCE, "NaN after layer %d attention", e[ERRF_NAN_ATTN] - 1);
+    else if (e[ERRF_NAN_FFN]) status = set_error(GGC_ERR_INFERENCE, "NaN after layer %d ffn", e[ERRF_NAN_FFN] - 1);
+    else if (e[ERRF_NAN_LOGITS]) status = set_error(GGC_ERR_INFERENCE, "NaN in logits");
+    else if (e[ERRF_KV_OVERFLOW]) {
+        status = set_error(GGC_ERR_KV_CACHE_OVERFLOW, "KvCacheOverflow { seq_len: %d, max_seq: %u }", e[ERRF_KV_OVERFLOW] - 1,
+                           m->hp.max_ctx);
+    } else if (e[ERRF_BAD_POS]) status = set_error(GGC_ERR_INFERENCE, "position outside [0, %u)", m->hp.max_ctx);
+    if (status != GGC_OK) {
+        cudaMemsetAsync(m->errf, 0, sizeof(int) * ERRF_COUNT, m->ctx->stream);
+        cudaStreamSynchronize(m->ctx->stream);
+    }
+    return status;
+}
+
+}  // namespace
+
+// LlamaModel::forward (llama.rs:214-224, :266-350)
+extern "C" int ggc_model_forward(ggc_model* m, const uint32_t* tokens, const int64_t* positions, uint64_t n, float* logits,
+                                 uint32_t* argmax) {
+    if (!m) return set_error(GGC_ERR_INVALID_ARG, "null model");
+    if (n == 0) return set_error(GGC_ERR_INFERENCE, "empty input");
+    if (!tokens || !positions) return set_error(GGC_ERR_INVALID_ARG, "null tokens/positions");
+    ggc_ctx* ctx = m->ctx;
+    DeviceGuard g(ctx->device);
+    if (m->cache_len + n > m->hp.max_ctx)
+        return set_error(GGC_ERR_KV_CACHE_OVERFLOW, "KvCacheOverflow { seq_len: %llu, max_seq: %u }",
+                         (unsigned long long)(m->cache_len + n), m->hp.max_ctx);
+    const cudaMemcpyKind k1 = is_device_ptr(tokens) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    const cudaMemcpyKind k2 = is_device_ptr(positions) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    GGC_CUDA_TRY(cudaMemcpyAsync(m->in_tok, tokens, n * sizeof(uint32_t), k1, ctx->stream));
+    GGC_CUDA_TRY(cudaMemcpyAsync(m->in_pos, positions, n * sizeof(int64_t), k2, ctx->stream));
+    GGC_TRY(run_steps(m, n, 0, -1, n));
+    if (logits) {
+        const cudaMemcpyKind k = is_device_ptr(logits) ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
+        GGC_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, (size_t)m->hp.vocab_size * sizeof(float), k, ctx->stream));
+    }
+    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    GGC_TRY(check_run(m));
+    if (argmax) {
+        const uint32_t id = (uint32_t)(m->rb->key & 0xFFFFFFFFull);
+        if (is_device_ptr(argmax)) GGC_CUDA_TRY(cudaMemcpy(argmax, &id, sizeof(id), cudaMemcpyHostToDevice));
+        else *argmax = id;
+    }
+    return GGC_OK;
+}
+
+extern "C" int ggc_model_generate_greedy(ggc_model* m, const uint32_t* prompt, uint64_t n_prompt, int64_t start_pos,
+                                         uint64_t max_tokens, int64_t eos, uint32_t* out_ids, uint64_t* n_out) {
+    if (!m || !n_out) return set_error(GGC_ERR_INVALID_ARG, "null argument");
+    *n_out = 0;
+    if (n_prompt == 0) return set_error(GGC_ERR_INFERENCE, "prompt tokenize empty");
+    if (!prompt || (max_tokens && !out_ids)) return set_error(GGC_ERR_INVALID_ARG, "null buffer");
+    ggc_ctx* ctx = m->ctx;
+    DeviceGuard g(ctx->device);
+    if (m->cache_len + n_prompt + max_tokens > m->hp.max_ctx)
+        return set_error(GGC_ERR_KV_CACHE_OVERFLOW, "KvCacheOverflow { seq_len: %llu, max_seq: %u }",
+                         (unsigned long long)(m->cache_len + n_prompt + max_tokens), m->hp.max_ctx);
+    std::vector<int64_t> pos(n_prompt);
+    for (uint64_t i = 0; i < n_prompt; ++i) pos[i] = start_pos + (int64_t)i;
+    const cudaMemcpyKind k1 = is_device_ptr(prompt) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    GGC_CUDA_TRY(cudaMemcpyAsync(m->in_tok, prompt, n_prompt * sizeof(uint32_t), k1, ctx->stream));
+    GGC_CUDA_TRY(cudaMemcpyAsync(m->in_pos, pos.data(), n_prompt * sizeof(int64_t), cudaMemcpyHostToDevice, ctx->stream));
+    GGC_TRY(run_steps(m, n_prompt, max_tokens, eos, n_prompt + max_tokens));
+    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    const uint64_t got = (uint64_t)m->rb->st.n_out;
+    if (got) GGC_CUDA_TRY(cudaMemcpy(out_ids, m->out_ids, got * sizeof(uint32_t), cudaMemcpyDeviceToHost));
+    *n_out = got;
+    return check_run(m);
+}
+
+extern "C" int ggc_model_wait(ggc_model* m, uint32_t* out_ids, uint64_t* n_out);
+
+// Continues greedy decoding from the last forward's logits: `steps` iterations of
+// sample -> forward(1 token), all on the device (no host round trip per token).
+extern "C" int ggc_model_decode(ggc_model* m, uint64_t steps, int64_t eos, int sync, uint32_t* out_ids, uint64_t* n_out) {
+    if (!m) return set_error(GGC_ERR_INVALID_ARG, "null model");
+    if (n_out) *n_out = 0;
+    if (m->cache_len == 0) return set_error(GGC_ERR_INFERENCE, "decode needs a previous forward");
+    if (m->cache_len + steps > m->hp.max_ctx)
+        return set_error(GGC_ERR_KV_CACHE_OVERFLOW, "KvCacheOverflow { seq_len: %llu, max_seq: %u }",
+                         (unsigned long long)(m->cache_len + steps), m->hp.max_ctx);
+    if (steps == 0) return GGC_OK;
+    ggc_ctx* ctx = m->ctx;
+    DeviceGuard g(ctx->device);
+    int32_t ctl[6] = {0, 0, (int32_t)steps, (int32_t)(eos < 0 ? -1 : eos), 0, 0};
+    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));   // the pinned control block may still be in flight
+    memcpy(&m->rb->ctl, ctl, sizeof(ctl));
+    GGC_CUDA_TRY(cudaMemcpyAsync(m->st, &m->rb->ctl, sizeof(ctl), cudaMemcpyHostToDevice, ctx->stream));
+    GGC_CUDA_TRY(launch(ctx, k_decode_start, dim3(1), dim3(32), 0, m->st, (const unsigned long long*)m->argmax_key,
+                        m->out_ids, m->errf));
+    for (uint64_t i = 0; i < steps; ++i) {
+        GGC_CUDA_TRY(cudaGraphLaunch(m->graph, ctx->stream));
+        ctx->launches += m->launches_per_step;
+    }
+    m->cache_len += steps;   // provisional; corrected by the readback below / ggc_model_wait
+    if (!sync) return GGC_OK;
+    return ggc_model_wait(m, out_ids, n_out);
+}
+
+// Waits for the model's queued work, validates it and returns the generated ids.
+extern "C" int ggc_model_wait(ggc_model* m, uint32_t* out_ids, uint64_t* n_out) {
+    if (!m) return set_error(GGC_ERR_INVALID_ARG, "null model");
+    ggc_ctx* ctx = m->ctx;
+    DeviceGuard g(ctx->device);
+    GGC_CUDA_TRY(cudaMemcpyAsync(&m->rb->st, m->st, sizeof(StepState), cudaMemcpyDeviceToHost, ctx->stream));
+    GGC_CUDA_TRY(cudaMemcpyAsync(m->rb->errf, m->errf, sizeof(int) * ERRF_COUNT, cudaMemcpyDeviceToHost, ctx->stream));
+    GGC_CUDA_TRY(cudaMemcpyAsync(&m->rb->key, m->argmax_key, sizeof(unsigned long long), cudaMemcpyDeviceToHost, ctx->stream));
+    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    const uint64_t got = (uint64_t)m->rb->st.n_out;
+    if (out_ids && got) GGC_CUDA_TRY(cudaMemcpy(out_ids, m->out_ids, got * sizeof(uint32_t), cudaMemcpyDeviceToHost));
+    if (n_out) *n_out = got;
+    return check_run(m);
+}
+
+extern "C" uint64_t ggc_model_cache_len(const ggc_model* m) { return m ? m->cache_len : 0; }
+
+extern "C" int ggc_model_truncate(ggc_model* m, uint64_t new_len) {
+    if (!m) return set_error(GGC_ERR_INVALID_ARG, "null model");
+    if (new_len >= m->cache_len) return GGC_OK;   // cache.rs:86-93 only shrinks
+    DeviceGuard g(m->ctx->device);
+    const uint32_t slot = (uint32_t)new_len;
+    GGC_CUDA_TRY(cudaMemcpyAsync(&m->st->slot, &slot, sizeof(slot), cudaMemcpyHostToDevice, m->ctx->stream));
+    GGC_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    m->cache_len = new_len;
+    return GGC_OK;
+}
+
+extern "C" int ggc_model_reset_cache(ggc_model* m) { return ggc_model_truncate(m, 0); }
+
+extern "C" int ggc_model_cache_append(ggc_model* m, uint32_t layer, const float* k, const float* v, uint64_t seq) {
+    if (!m || !k || !v) return set_error(GGC_ERR_INVALID_ARG, "null argument");
+    if (layer >= m->hp.n_layers) return set_error(GGC_ERR_INVALID_ARG, "layer %u out of range", layer);
+    // every layer must hold the same number of tokens; the slot advances when the last layer is appended
+    const uint64_t base = m->cache_len;
+    if (base + seq > m->hp.max_ctx)
+        return set_error(GGC_ERR_KV_CACHE_OVERFLOW, "KvCacheOverflow { seq_len: %llu, max_seq: %u }",
+                         (unsigned long long)(base + seq), m->hp.max_ctx);
+    DeviceGuard g(m->ctx->device);
+    const size_t layer_kv = (size_t)m->hp.max_ctx * m->kvdim * m->kv_elem;
+    const size_t n = (size_t)seq * m->kvdim;
+    uint8_t* kd = (uint8_t*)m->kcache + layer * layer_kv + base * m->kvdim * m->kv_elem;
+    uint8_t* vd = (uint8_t*)m->vcache + layer * layer_kv + base * m->kvdim * m->kv_elem;
+    if (m->hp.kv_f16) {
+        std::vector<__half> hk(n), hv(n);
+        std::vector<float> fk(n), fv(n);
+        GGC_CUDA_TRY(cudaMemcpy(fk.data(), k, n * 4, is_device_ptr(k) ? cudaMemcpyDeviceToHost : cudaMemcpyHostToHost));
+        GGC_CUDA_TRY(cudaMemcpy(fv.data(), v, n * 4, is_device_ptr(v) ? cudaMemcpyDeviceToHost : cudaMemcpyHostToHost));
+        for (size_t i = 0; i < n; ++i) { hk[i] = __float2half_rn(fk[i]); hv[i] = __float2half_rn(fv[i]); }
+        GGC_CUDA_TRY(cudaMemcpy(kd, hk.data(), n * 2, cudaMemcpyHostToDevice));
+        GGC_CUDA_TRY(cudaMemcpy(vd, hv.data(), n * 2, cudaMemcpyHostToDevice));
+    } else {
+        GGC_CUDA_TRY(cudaMemcpy(kd, k, n * 4, cudaMemcpyDefault));
+        GGC_CUDA_TRY(cudaMemcpy(vd, v, n * 4, cudaMemcpyDefault));
+    }
+    if (layer == m->hp.n_layers - 1) {
+        const uint32_t slot = (uint32_t)(base + seq);
+        GGC_CUDA_TRY(cudaMemcpy(&m->st->slot, &slot, sizeof(slot), cudaMemcpyHostToDevice));
+        m->cache_len = base + seq;
+    }
+    return GGC_OK;
+}
+
+extern "C" int ggc_model_cache_read(ggc_model* m, uint32_t layer, float* k, float* v) {
+    if (!m || !k || !v) return set_error(GGC_ERR_INVALID_ARG, "null argument");
+    if (layer >= m->hp.n_layers) return set_error(GGC_ERR_INVALID_ARG, "layer %u out of range", layer);
+    DeviceGuard g(m->ctx->device);
+    GGC_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    const size_t layer_kv = (size_t)m->hp.max_ctx * m->kvdim * m->kv_elem;
+    const size_t n = (size_t)m->cache_len * m->kvdim;
+    const uint8_t* kd = (const uint8_t*)m->kcache + layer * layer_kv;
+    const uint8_t* vd = (const uint8_t*)m->vcache + layer * layer_kv;
+    if (m->hp.kv_f16) {
+        std::vector<__half> hk(n), hv(n);
+        GGC_CUDA_TRY(cudaMemcpy(hk.data(), kd, n * 2, cudaMemcpyDeviceToHost));
+        GGC_CUDA_TRY(cudaMemcpy(hv.data(), vd, n * 2, cudaMemcpyDeviceToHost));
+        std::vector<float> fk(n), fv(n);
+        for (size_t i = 0; i < n; ++i) { fk[i] = __half2float(hk[i]); fv[i] = __half2float(hv[i]); }
+        GGC_CUDA_TRY(cudaMemcpy(k, fk.data(), n * 4, cudaMemcpyDefault));
+        GGC_CUDA_TRY(cudaMemcpy(v, fv.data(), n * 4, cudaMemcpyDefault));
+    } else {
+        GGC_CUDA_TRY(cudaMemcpy(k, kd, n * 4, cudaMemcpyDefault));
+        GGC_CUDA_TRY(cudaMemcpy(v, vd, n * 4, cudaMemcpyDefault));
+    }
+    return GGC_OK;
+}

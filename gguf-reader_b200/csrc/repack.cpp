@@ -1,0 +1,145 @@
+// repack.cpp -- host-side split of raw GGUF rows into the plane layout
+// (see planes.cuh).  Runs once per weight at model load.
+#include <cstring>
+#include <thread>
+#include <vector>
+
+#include "planes.cuh"
+
+namespace ggc {
+namespace {
+
+inline uint32_t rd32(const uint8_t* p) {
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+inline void wr32(uint8_t* p, uint32_t v) {
+    p[0] = (uint8_t)v; p[1] = (uint8_t)(v >> 8); p[2] = (uint8_t)(v >> 16); p[3] = (uint8_t)(v >> 24);
+}
+
+// Q5_0 / Q5_1 qh: element i (i<16) uses bit i, element 16+i uses bit 16+i.
+// Plane bit 8k+w   <- qh bit 4w+k      (low nibbles of chunk word w, byte k)
+// Plane bit 8k+4+w <- qh bit 16+4w+k   (high nibbles of chunk word w, byte k)
+uint32_t permute_q5_qh(uint32_t qh) {
+    uint32_t o = 0;
+    for (int w = 0; w < 4; ++w)
+        for (int k = 0; k < 4; ++k) {
+            o |= ((qh >> (4 * w + k)) & 1u) << (8 * k + w);
+            o |= ((qh >> (16 + 4 * w + k)) & 1u) << (8 * k + 4 + w);
+        }
+    return o;
+}
+
+void repack_block(int dt, const uint8_t* b, uint64_t blk, uint8_t* const pl[4]) {
+    switch (dt) {
+        case GGC_Q4_0:
+            std::memcpy(pl[0] + blk * 16, b + 2, 16);
+            std::memcpy(pl[1] + blk * 2, b, 2);
+            break;
+        case GGC_Q4_1:
+            std::memcpy(pl[0] + blk * 16, b + 4, 16);
+            std::memcpy(pl[1] + blk * 4, b, 4);
+            break;
+        case GGC_Q5_0:
+            std::memcpy(pl[0] + blk * 16, b + 6, 16);
+            wr32(pl[1] + blk * 4, permute_q5_qh(rd32(b + 2)));
+            std::memcpy(pl[2] + blk * 2, b, 2);
+            break;
+        case GGC_Q5_1:
+            std::memcpy(pl[0] + blk * 16, b + 8, 16);
+            wr32(pl[1] + blk * 4, permute_q5_qh(rd32(b + 4)));
+            std::memcpy(pl[2] + blk * 4, b, 4);
+            break;
+        case GGC_Q8_0:
+            std::memcpy(pl[0] + blk * 32, b + 2, 32);
+            std::memcpy(pl[1] + blk * 2, b, 2);
+            break;
+        case GGC_Q2_K:
+            std::memcpy(pl[0] + blk * 64, b + 16, 64);
+            std::memcpy(pl[1] + blk * 16, b, 16);
+            std::memcpy(pl[2] + blk * 4, b + 80, 4);
+            break;
+        case GGC_Q3_K_S: case GGC_Q3_K_L: case GGC_Q3_K_M: {
+            std::memcpy(pl[0] + blk * 64, b + 32, 64);
+            // hmask: element e uses bit e%8 of byte e/8.  Chunk p covers elements
+            // 64p + 16w + 4k + s; plane word (2p + w/2), bit 8k + s + 4(w%2).
+            uint32_t words[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            for (int e = 0; e < 256; ++e) {
+                uint32_t bit = (b[e / 8] >> (e % 8)) & 1u;
+                int p = e / 64, r = e % 64, w = r / 16, k = (r % 16) / 4, s = r % 4;
+                words[2 * p + w / 2] |= bit << (8 * k + s + 4 * (w % 2));
+            }
+            for (int i = 0; i < 8; ++i) wr32(pl[1] + blk * 32 + 4 * i, words[i]);
+            std::memcpy(pl[2] + blk * 12, b + 96, 12);
+            std::memcpy(pl[3] + blk * 2, b + (dt == GGC_Q3_K_M ? 112 : 108), 2);
+            break;
+        }
+        case GGC_Q4_K:
+            std::memcpy(pl[0] + blk * 128, b + 16, 128);
+            std::memcpy(pl[1] + blk * 16, b, 16);
+            break;
+        case GGC_Q5_K: {
+            std::memcpy(pl[0] + blk * 128, b + 48, 128);
+            // qs byte B (0..127) takes its 5th bit from bit B%8 of qh[B/8] (only
+            // qh[0..16) is read).  Chunk p = bytes 16p + 4w + k -> plane word p/2,
+            // bit 8k + w + 4(p%2).
+            uint32_t words[4] = {0, 0, 0, 0};
+            for (int B = 0; B < 128; ++B) {
+                uint32_t bit = (b[16 + B / 8] >> (B % 8)) & 1u;
+                int p = B / 16, i = B % 16, w = i / 4, k = i % 4;
+                words[p / 2] |= bit << (8 * k + w + 4 * (p % 2));
+            }
+            for (int i = 0; i < 4; ++i) wr32(pl[1] + blk * 16 + 4 * i, words[i]);
+            std::memcpy(pl[2] + blk * 16, b, 16);
+            break;
+        }
+        case GGC_Q6_K:
+            std::memcpy(pl[0] + blk * 128, b, 128);
+            std::memcpy(pl[1] + blk * 64, b + 128, 64);
+            std::memcpy(pl[2] + blk * 16, b + 192, 16);
+            std::memcpy(pl[3] + blk * 2, b + 208, 2);
+            break;
+        case GGC_Q8_K:
+            std::memcpy(pl[0] + blk * 256, b + 4, 256);
+            std::memcpy(pl[1] + blk * 4, b, 4);
+            break;
+        case GGC_F16: case GGC_BF16:
+            std::memcpy(pl[0] + blk * 2, b, 2);
+            break;
+        case GGC_F32:
+            std::memcpy(pl[0] + blk * 4, b, 4);
+            break;
+        default:
+            break;
+    }
+}
+
+}  // namespace
+
+void repack_rows_host(int dt, const uint8_t* raw, uint64_t rows, uint64_t cols, const uint32_t* row_src,
+                      uint8_t* const planes[4], int nthreads) {
+    PlaneSpec s = plane_spec(dt);
+    const uint64_t bs = (uint64_t)block_size_of(dt), bb = (uint64_t)block_bytes_of(dt);
+    const uint64_t nb = cols / bs, row_bytes = nb * bb;
+    uint64_t pitch[4] = {0, 0, 0, 0};
+    for (int p = 0; p < s.n; ++p) pitch[p] = plane_pitch(dt, p, cols);
+    auto work = [&](uint64_t r0, uint64_t r1) {
+        for (uint64_t r = r0; r < r1; ++r) {
+            const uint8_t* src = raw + (uint64_t)(row_src ? row_src[r] : r) * row_bytes;
+            uint8_t* pl[4] = {nullptr, nullptr, nullptr, nullptr};
+            for (int p = 0; p < s.n; ++p) pl[p] = planes[p] + r * pitch[p];
+            for (uint64_t k = 0; k < nb; ++k) repack_block(dt, src + k * bb, k, pl);
+        }
+    };
+    if (nthreads <= 1 || rows < 64) {
+        work(0, rows);
+        return;
+    }
+    std::vector<std::thread> pool;
+    for (int t = 0; t < nthreads; ++t) {
+        uint64_t r0 = rows * t / nthreads, r1 = rows * (t + 1) / nthreads;
+        pool.emplace_back(work, r0, r1);
+    }
+    for (auto& th : pool) th.join();
+}
+
+}  // namespace ggc

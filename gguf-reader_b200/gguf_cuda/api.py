@@ -1,0 +1,265 @@
+"""Host-side mirror of gguf-reader's infer API over libgguf_cuda.
+
+Names, argument meanings and errors follow the Rust crate:
+  quant::dequantize / quant::quant_matvec       (src/infer/quant.rs:403, :526)
+  LlamaModel::{forward, forward_cached, cache_len, reset_cache}  (model/llama.rs:214-239)
+  Engine greedy generate loop                   (src/infer/engine.rs:74-148)
+Arrays are numpy (host) or torch CUDA tensors (device); results come back in the
+same kind of memory the caller passed.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import _lib as L
+from ._lib import check, lib
+
+
+def _ptr(a):
+    """(address, nbytes) of a numpy array or a torch tensor."""
+    if a is None:
+        return None, 0
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data, a.nbytes
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr(), a.numel() * a.element_size()
+    raise TypeError(f"unsupported buffer type {type(a)}")
+
+
+def _as_bytes(data) -> np.ndarray:
+    if isinstance(data, (bytes, bytearray, memoryview)):
+        return np.frombuffer(data, dtype=np.uint8)
+    if isinstance(data, np.ndarray):
+        return np.ascontiguousarray(data).view(np.uint8).reshape(-1)
+    return data   # torch tensor (device bytes)
+
+
+class Context:
+    """One CUDA stream on one GPU (ggc_ctx)."""
+
+    def __init__(self, device: int = 0, rank: int = 0, world: int = 1, nccl_id: bytes | None = None):
+        h = C.c_void_p()
+        if world > 1:
+            buf = C.create_string_buffer(bytes(nccl_id), 128)
+            check(lib().ggc_ctx_create_tp(device, rank, world, C.cast(buf, C.c_void_p), C.byref(h)))
+        else:
+            check(lib().ggc_ctx_create(device, C.byref(h)))
+        self.h = h
+        self.device = device
+
+    @staticmethod
+    def nccl_unique_id() -> bytes:
+        buf = C.create_string_buffer(128)
+        check(lib().ggc_nccl_unique_id(C.cast(buf, C.c_void_p)))
+        return buf.raw
+
+    @property
+    def stream(self) -> int:
+        return lib().ggc_ctx_stream(self.h) or 0
+
+    def synchronize(self):
+        check(lib().ggc_ctx_synchronize(self.h))
+
+    def kernel_launches(self) -> int:
+        return int(lib().ggc_ctx_kernel_launches(self.h))
+
+    def close(self):
+        if getattr(self, "h", None) is not None and self.h.value:
+            lib().ggc_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+_default_ctx: Context | None = None
+
+
+def default_context() -> Context:
+    global _default_ctx
+    if _default_ctx is None:
+        _default_ctx = Context(0)
+    return _default_ctx
+
+
+# ---- quant.rs ----------------------------------------------------------------
+def block_size(dtype: int):
+    v = lib().ggc_block_size(dtype)
+    return None if v < 0 else v
+
+
+def block_bytes(dtype: int):
+    v = lib().ggc_block_bytes(dtype)
+    return None if v < 0 else v
+
+
+def dequantize(data, dtype: int, n: int, out=None, ctx: Context | None = None):
+    """quant::dequantize: n elements of `dtype` -> f32 (bit-exact with the reference)."""
+    ctx = ctx or default_context()
+    raw = _as_bytes(data)
+    rp, rn = _ptr(raw)
+    if out is None:
+        out = np.empty(n, dtype=np.float32)
+    op, _ = _ptr(out)
+    check(lib().ggc_dequantize(ctx.h, dtype, rp if rn else None, rn, n, op))
+    return out
+
+
+def quant_matvec(w, dtype: int, rows: int, cols: int, x, y=None, ctx: Context | None = None):
+    """quant::quant_matvec: y[r] = sum_c W[r, c] x[c] over raw GGUF rows."""
+    ctx = ctx or default_context()
+    wb = _as_bytes(w)
+    if isinstance(x, np.ndarray):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+    if y is None:
+        y = np.zeros(rows, dtype=np.float32)
+    wp, wn = _ptr(wb)
+    xp, xn = _ptr(x)
+    yp, yn = _ptr(y)
+    check(lib().ggc_quant_matvec(ctx.h, dtype, wp, wn, rows, cols, xp, xn // 4, yp, yn // 4))
+    return y
+
+
+def infer_k_quant_dtype(span: int, n: int, marked: int):
+    v = lib().ggc_infer_k_quant_dtype(span, n, marked)
+    return None if v < 0 else v
+
+
+class Tensor:
+    """A GGUF tensor resident in HBM (plane layout when repack=True)."""
+
+    def __init__(self, raw, dtype: int, ne, repack: bool = True, ctx: Context | None = None):
+        self.ctx = ctx or default_context()
+        raw = _as_bytes(raw)
+        ne_arr = (C.c_uint64 * len(ne))(*ne)
+        h = C.c_void_p()
+        rp, rn = _ptr(raw)
+        check(lib().ggc_tensor_upload(self.ctx.h, rp, rn, dtype, ne_arr, len(ne), 1 if repack else 0, C.byref(h)))
+        self.h, self.dtype, self.ne = h, dtype, tuple(ne)
+        self.rows = int(np.prod(ne[1:])) if len(ne) > 1 else 1
+        self.cols = ne[0]
+
+    def matvec(self, x, y=None):
+        if isinstance(x, np.ndarray):
+            x = np.ascontiguousarray(x, dtype=np.float32)
+        if y is None:
+            y = np.zeros(self.rows, dtype=np.float32)
+        check(lib().ggc_tensor_matvec(self.ctx.h, self.h, _ptr(x)[0], _ptr(y)[0]))
+        return y
+
+    def dequantize(self, out=None):
+        if out is None:
+            out = np.empty(self.rows * self.cols, dtype=np.float32)
+        check(lib().ggc_tensor_dequantize(self.ctx.h, self.h, _ptr(out)[0]))
+        return out
+
+    def free(self):
+        if getattr(self, "h", None) is not None and self.h.value:
+            lib().ggc_tensor_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+# ---- model/llama.rs ------------------------------------------------------------
+class LlamaModel:
+    """LlamaModel over tensors given in role order (see synth.TENSOR_ROLES)."""
+
+    def __init__(self, hp: dict, tensors: list, max_ctx: int = 2048, kv_f16: bool = False,
+                 ctx: Context | None = None):
+        self.ctx = ctx or default_context()
+        descs = (L.TensorDesc * len(tensors))()
+        keep = []
+        for i, t in enumerate(tensors):
+            if t is None:
+                descs[i] = L.TensorDesc(None, 0, 0, 0)
+                continue
+            raw = _as_bytes(t["raw"])
+            keep.append(raw)
+            descs[i] = L.TensorDesc(raw.ctypes.data, raw.nbytes, t["dtype"], t["n_elements"])
+        self.hp = L.HParams(hp["vocab_size"], hp["embed_dim"], hp["n_heads"], hp["n_kv_heads"], hp["ffn_dim"],
+                            hp["n_layers"], float(hp["rope_freq_base"]), max_ctx, 1 if kv_f16 else 0)
+        h = C.c_void_p()
+        check(lib().ggc_model_create(self.ctx.h, C.byref(self.hp), descs, len(tensors), C.byref(h)))
+        self.h = h
+        self.vocab = hp["vocab_size"]
+        self.kv_dim = hp["n_kv_heads"] * (hp["embed_dim"] // hp["n_heads"])
+
+    def forward(self, tokens, positions, logits=None, want_logits=True):
+        """LlamaModel::forward: logits (vocab f32) of the last token; appends K/V."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32) if not hasattr(tokens, "data_ptr") else tokens
+        p = np.ascontiguousarray(positions, dtype=np.int64) if not hasattr(positions, "data_ptr") else positions
+        n = t.size if isinstance(t, np.ndarray) else t.numel()
+        if want_logits and logits is None:
+            logits = np.zeros(self.vocab, dtype=np.float32)
+        am = np.zeros(1, dtype=np.uint32)
+        check(lib().ggc_model_forward(self.h, _ptr(t)[0], _ptr(p)[0], n, _ptr(logits)[0] if want_logits else None,
+                                      am.ctypes.data))
+        self.last_argmax = int(am[0])
+        return logits if want_logits else self.last_argmax
+
+    forward_cached = forward
+
+    def cache_len(self) -> int:
+        return int(lib().ggc_model_cache_len(self.h))
+
+    def reset_cache(self):
+        check(lib().ggc_model_reset_cache(self.h))
+
+    def truncate(self, new_len: int):
+        check(lib().ggc_model_truncate(self.h, new_len))
+
+    def cache_append(self, layer: int, k, v):
+        k = np.ascontiguousarray(k, dtype=np.float32)
+        v = np.ascontiguousarray(v, dtype=np.float32)
+        check(lib().ggc_model_cache_append(self.h, layer, k.ctypes.data, v.ctypes.data, k.size // self.kv_dim))
+
+    def cache_read(self, layer: int):
+        n = self.cache_len() * self.kv_dim
+        k = np.zeros(n, dtype=np.float32)
+        v = np.zeros(n, dtype=np.float32)
+        check(lib().ggc_model_cache_read(self.h, layer, k.ctypes.data, v.ctypes.data))
+        return k, v
+
+    def generate_greedy(self, prompt, max_tokens: int, eos: int = -1, start_pos: int = 0) -> list:
+        """Engine::generate's loop with the greedy sampler, run on the device."""
+        p = np.ascontiguousarray(prompt, dtype=np.uint32)
+        out = np.zeros(max(max_tokens, 1), dtype=np.uint32)
+        n = C.c_uint64(0)
+        check(lib().ggc_model_generate_greedy(self.h, p.ctypes.data, p.size, start_pos, max_tokens, eos,
+                                              out.ctypes.data, C.byref(n)))
+        return out[: n.value].tolist()
+
+    def decode(self, steps: int, eos: int = -1, sync: bool = True):
+        """Continues greedy decoding from the last forward's logits (sample -> forward, on the device)."""
+        out = np.zeros(max(steps, 1), dtype=np.uint32)
+        n = C.c_uint64(0)
+        check(lib().ggc_model_decode(self.h, steps, eos, 1 if sync else 0, out.ctypes.data if sync else None,
+                                     C.byref(n)))
+        return out[: n.value].tolist() if sync else None
+
+    def wait(self, max_ids: int = 0) -> list:
+        out = np.zeros(max(max_ids, 1), dtype=np.uint32)
+        n = C.c_uint64(0)
+        check(lib().ggc_model_wait(self.h, out.ctypes.data if max_ids else None, C.byref(n)))
+        return out[: min(n.value, max_ids)].tolist()
+
+    def close(self):
+        if getattr(self, "h", None) is not None and self.h.value:
+            lib().ggc_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
