@@ -257,9 +257,11 @@ def run_ours(args, rank, world, local_rank):
         barrier()
         l0 = ctx.kernel_launches()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("timed")
         e0.record(stream)
         model.decode(K, sync=False)
         e1.record(stream)
+        torch.cuda.nvtx.range_pop()
         e1.synchronize()
         launches = ctx.kernel_launches() - l0
         ids = model.wait(K)

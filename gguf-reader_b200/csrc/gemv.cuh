@@ -485,7 +485,7 @@ __device__ __forceinline__ unsigned long long argmax_key_of(float v, uint32_t id
 }
 
 template <int DT>
-__global__ void __launch_bounds__(GEMV_WARPS * 32) k_gemv(const GemvArgs a) {
+__global__ void __launch_bounds__(GEMV_WARPS * 32, 2) k_gemv(const GemvArgs a) {
     using D = Dec<DT>;
     constexpr int R = GEMV_R;
     extern __shared__ float4 smem4[];
@@ -519,26 +519,30 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) k_gemv(const GemvArgs a) {
         __syncthreads();
     }
     const float scale = (a.pro == PRO_RMSNORM) ? s_scale : 0.f;
-    float* xsf = reinterpret_cast<float*>(xs);
-    for (int s = tid; s < D::T * nch * 4; s += nthr) {
-        const int j = s & 3, c = (s >> 2) % nch, t = (s >> 2) / nch;
-        const int e = D::elem(c, t, j);
-        float v;
-        if ((uint32_t)e >= a.xcols) {
-            v = 0.f;
-        } else if (a.pro == PRO_RMSNORM) {
-            v = __fmul_rn(__fmul_rn(a.x[e], scale), a.x2[e]);
-        } else if (a.pro == PRO_SWIGLU) {
-            // ops::silu (ops.rs:237-247) then gate *= up (llama.rs:564-567)
-            const float g = a.x[e];
-            float sig;
-            if (g >= 0.0f) sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
-            else { const float ex = expf(g); sig = __fdiv_rn(ex, __fadd_rn(1.0f, ex)); }
-            v = __fmul_rn(__fmul_rn(g, sig), a.x2[e]);
-        } else {
-            v = a.x[e];
+#pragma unroll 1
+    for (int t = 0; t < D::T; ++t) {
+        for (int c = tid; c < nch; c += nthr) {
+            float v[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int e = D::elem(c, t, j);
+                if ((uint32_t)e >= a.xcols) {
+                    v[j] = 0.f;
+                } else if (a.pro == PRO_RMSNORM) {
+                    v[j] = __fmul_rn(__fmul_rn(a.x[e], scale), a.x2[e]);
+                } else if (a.pro == PRO_SWIGLU) {
+                    // ops::silu (ops.rs:237-247) then gate *= up (llama.rs:564-567)
+                    const float g = a.x[e];
+                    float sig;
+                    if (g >= 0.0f) sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
+                    else { const float ex = expf(g); sig = __fdiv_rn(ex, __fadd_rn(1.0f, ex)); }
+                    v[j] = __fmul_rn(__fmul_rn(g, sig), a.x2[e]);
+                } else {
+                    v[j] = a.x[e];
+                }
+            }
+            xs[t * nch + c] = make_float4(v[0], v[1], v[2], v[3]);
         }
-        xsf[s] = v;
     }
     __syncthreads();
     if constexpr (D::G > 0) {
@@ -558,8 +562,11 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) k_gemv(const GemvArgs a) {
     // ---- main loop over row groups ----------------------------------------
     const int lane = tid & 31;
     const uint32_t total_groups = a.seg[0].groups + (a.nseg > 1 ? a.seg[1].groups : 0) + (a.nseg > 2 ? a.seg[2].groups : 0);
-    const uint32_t gwarps = gridDim.x * GEMV_WARPS;
-    for (uint32_t g = blockIdx.x * GEMV_WARPS + (tid >> 5); g < total_groups; g += gwarps) {
+    // balanced contiguous ranges of row groups per warp (they differ by at most one group)
+    const uint32_t gwarps = gridDim.x * GEMV_WARPS, wid = blockIdx.x * GEMV_WARPS + (tid >> 5);
+    const uint32_t g_begin = (uint32_t)((uint64_t)total_groups * wid / gwarps);
+    const uint32_t g_end = (uint32_t)((uint64_t)total_groups * (wid + 1) / gwarps);
+    for (uint32_t g = g_begin; g < g_end; ++g) {
         int si = 0;
         uint32_t lg = g;
         while (si + 1 < a.nseg && lg >= a.seg[si].groups) { lg -= a.seg[si].groups; ++si; }

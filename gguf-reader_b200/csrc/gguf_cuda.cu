@@ -13,6 +13,7 @@
 #include <thread>
 #include <vector>
 
+#include <dlfcn.h>
 #include <nccl.h>
 
 #include "common.cuh"
@@ -58,6 +59,49 @@ int set_shape_error(uint64_t elements, uint64_t block, const char* what) {
     return GGC_ERR_INVALID_TENSOR_SHAPE;
 }
 }  // namespace ggc
+
+// ===========================================================================
+// NCCL, loaded on first use (no link-time dependency): the library then shares
+// whichever libnccl.so.2 the process already has (e.g. PyTorch's).
+// ===========================================================================
+namespace {
+struct NcclApi {
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+    const char* (*GetErrorString)(ncclResult_t) = nullptr;
+    ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    bool ok = false;
+};
+
+NcclApi& nccl() {
+    static NcclApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return;
+        api.GetUniqueId = (decltype(api.GetUniqueId))dlsym(h, "ncclGetUniqueId");
+        api.CommInitRank = (decltype(api.CommInitRank))dlsym(h, "ncclCommInitRank");
+        api.CommDestroy = (decltype(api.CommDestroy))dlsym(h, "ncclCommDestroy");
+        api.CommAbort = (decltype(api.CommAbort))dlsym(h, "ncclCommAbort");
+        api.CommGetAsyncError = (decltype(api.CommGetAsyncError))dlsym(h, "ncclCommGetAsyncError");
+        api.GetErrorString = (decltype(api.GetErrorString))dlsym(h, "ncclGetErrorString");
+        api.AllReduce = (decltype(api.AllReduce))dlsym(h, "ncclAllReduce");
+        api.AllGather = (decltype(api.AllGather))dlsym(h, "ncclAllGather");
+        api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.AllReduce && api.AllGather &&
+                 api.GetErrorString;
+    });
+    return api;
+}
+
+int nccl_error(const char* what, ncclResult_t r) {
+    return set_error(GGC_ERR_NCCL, "%s: %s", what, nccl().GetErrorString ? nccl().GetErrorString(r) : "?");
+}
+}  // namespace
 
 // ===========================================================================
 // context
@@ -189,9 +233,10 @@ extern "C" int64_t ggc_block_bytes(int dtype) { return block_bytes_of(dtype); }
 
 extern "C" int ggc_nccl_unique_id(void* out128) {
     if (!out128) return set_error(GGC_ERR_INVALID_ARG, "null id buffer");
+    if (!nccl().ok) return set_error(GGC_ERR_NCCL, "libnccl.so.2 not loadable");
     ncclUniqueId id;
-    ncclResult_t r = ncclGetUniqueId(&id);
-    if (r != ncclSuccess) return set_error(GGC_ERR_NCCL, "ncclGetUniqueId: %s", ncclGetErrorString(r));
+    ncclResult_t r = nccl().GetUniqueId(&id);
+    if (r != ncclSuccess) return nccl_error("ncclGetUniqueId", r);
     memcpy(out128, &id, sizeof(id));
     return GGC_OK;
 }
@@ -224,10 +269,11 @@ extern "C" int ggc_ctx_create_tp(int device, int rank, int world, const void* nc
     c->world = world;
     if (world > 1) {
         DeviceGuard g(device);
+        if (!nccl().ok) return set_error(GGC_ERR_NCCL, "libnccl.so.2 not loadable");
         ncclUniqueId id;
         memcpy(&id, nccl_id, sizeof(id));
-        ncclResult_t r = ncclCommInitRank(&c->comm, world, id, rank);
-        if (r != ncclSuccess) return set_error(GGC_ERR_NCCL, "ncclCommInitRank: %s", ncclGetErrorString(r));
+        ncclResult_t r = nccl().CommInitRank(&c->comm, world, id, rank);
+        if (r != ncclSuccess) return nccl_error("ncclCommInitRank", r);
     }
     *out = c.release();
     return GGC_OK;
@@ -240,7 +286,7 @@ extern "C" int ggc_ctx_destroy(ggc_ctx* ctx) {
         cudaStreamSynchronize(ctx->stream);
         for (int i = 0; i < 3; ++i)
             if (ctx->stage[i]) cudaFree(ctx->stage[i]);
-        if (ctx->comm) ncclCommDestroy(ctx->comm);
+        if (ctx->comm) nccl().CommDestroy(ctx->comm);
         cudaStreamDestroy(ctx->stream);
     }
     delete ctx;
