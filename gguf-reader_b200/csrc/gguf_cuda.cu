@@ -418,21 +418,16 @@ int upload_mat(ggc_ctx* ctx, const void* raw, uint64_t raw_bytes, int dt, uint64
     const uint64_t row_bytes = cols / bs * (uint64_t)bb;
     if (raw_bytes < rows * row_bytes) return set_dequant_error(dt, rows * row_bytes, raw_bytes, "tensor data too short");
     if (rows == 0 || rows > 0xFFFFFFFFull || pcols > 0xFFFFFFFFull) return set_error(GGC_ERR_INVALID_ARG, "matrix shape");
-    uint64_t pitch[4] = {0, 0, 0, 0}, off[4] = {0, 0, 0, 0}, total = 0;
+    const TileLayout L = make_layout(dt, (uint32_t)rows, (uint32_t)pcols);
+    uint64_t off[4] = {0, 0, 0, 0}, total = 0;
     for (int p = 0; p < ps.n; ++p) {
-        pitch[p] = plane_pitch(dt, p, pcols);
         off[p] = total;
-        total += (rows * pitch[p] + 255) / 256 * 256;
+        total += ((uint64_t)L.nrb * L.rb_bytes[p] + 255) / 256 * 256;
     }
     std::vector<uint8_t> host(total, 0);
     uint8_t* planes[4] = {nullptr, nullptr, nullptr, nullptr};
     for (int p = 0; p < ps.n; ++p) planes[p] = host.data() + off[p];
-    if (bs == 1) {   // float formats: rows copied as-is, zero padded to pcols
-        for (uint64_t r = 0; r < rows; ++r)
-            memcpy(planes[0] + r * pitch[0], (const uint8_t*)raw + (uint64_t)(row_src ? row_src[r] : r) * row_bytes, row_bytes);
-    } else {
-        repack_rows_host(dt, (const uint8_t*)raw, rows, cols, row_src, planes, host_threads());
-    }
+    repack_rows_host(dt, (const uint8_t*)raw, rows, cols, row_src, L, planes, host_threads());
     DevMat m;
     m.dtype = dt;
     m.rows = (uint32_t)rows;
@@ -446,20 +441,19 @@ int upload_mat(ggc_ctx* ctx, const void* raw, uint64_t raw_bytes, int dt, uint64
         cudaFree(m.base);
         return set_error(GGC_ERR_CUDA, "upload: %s", cudaGetErrorString(e));
     }
-    for (int p = 0; p < 4; ++p) {
-        m.q.p[p] = p < ps.n ? m.base + off[p] : nullptr;
-        m.q.pitch[p] = (uint32_t)pitch[p];
-    }
-    m.q.rows = (uint32_t)rows;
-    m.q.cols = (uint32_t)pcols;
+    for (int p = 0; p < 4; ++p) m.q.p[p] = p < ps.n ? m.base + off[p] : nullptr;
+    m.q.L = L;
     out = m;
     return GGC_OK;
 }
 
+constexpr size_t GEMV_SMEM_LIMIT = 227 * 1024 - 4096;   // dynamic shared bytes per CTA (static use < 4 KB)
+
 template <int DT>
 struct SetGemvSmem {
     static void run(int* ok) {
-        if (cudaFuncSetAttribute(k_gemv<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess) *ok = 0;
+        if (cudaFuncSetAttribute(k_gemv<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMV_SMEM_LIMIT) != cudaSuccess)
+            *ok = 0;
     }
 };
 
@@ -486,13 +480,13 @@ struct GemvLaunch {
 template <int DT>
 struct RunGemv {
     static void run(ggc_ctx* ctx, const GemvArgs* a, cudaError_t* err) {
-        uint32_t total = 0;
-        for (int i = 0; i < a->nseg; ++i) total += a->seg[i].groups;
-        uint32_t ctas = cdiv<uint32_t>(total, GEMV_WARPS);
-        uint32_t cap = (uint32_t)ctx->num_sms * 2;
-        if (ctas > cap) ctas = cap;
+        uint32_t total_rb = 0;
+        for (int i = 0; i < a->nseg; ++i) total_rb += a->seg[i].m.L.nrb;
+        const TileCfg tc = make_tile_cfg<DT>(a->cols, GEMV_SMEM_LIMIT);
+        if (tc.stages < 2) { *err = cudaErrorInvalidConfiguration; return; }
+        uint32_t ctas = total_rb < (uint32_t)ctx->num_sms ? total_rb : (uint32_t)ctx->num_sms;
         if (ctas == 0) ctas = 1;
-        *err = launch(ctx, k_gemv<DT>, dim3(ctas), dim3(GEMV_WARPS * 32), gemv_smem_bytes<DT>(a->cols), *a);
+        *err = launch(ctx, k_gemv<DT>, dim3(ctas), dim3(GEMV_THREADS), gemv_smem_bytes(tc), *a, tc);
     }
 };
 
@@ -510,7 +504,6 @@ Seg make_seg(const DevMat& m, int epi, float* out, void* cache, const float* bia
     s.out = out;
     s.cache = cache;
     s.bias = bias;
-    s.groups = cdiv<uint32_t>(m.rows, GEMV_R);
     return s;
 }
 

@@ -1,29 +1,39 @@
-// planes.cuh -- the coalesced "plane" layout of uploaded weight tensors.
+// planes.cuh -- the tiled "plane" layout of uploaded weight tensors.
 //
 // A raw GGUF tensor stores each block's scale fields and quant bits together
 // (e.g. Q4_K: d, dmin, scales[12], qs[128] = 144 bytes).  At upload the host
-// splits every block into up to four planes, each a row-major array with a row
-// pitch padded to 16 bytes:
+// splits every block into up to four planes:
 //
-//   plane 0  the quant payload (qs / ql), always a multiple of 16 bytes per block,
-//            read by the GEMV as one 16-byte "chunk" per lane, coalesced across
-//            the warp (32 lanes x 16 B = 512 contiguous bytes);
+//   plane 0  the quant payload (qs / ql), a multiple of 16 bytes per block, read
+//            by the GEMV as one 16-byte "chunk" per lane;
 //   plane 1+ the per-block side data (scales, d, dmin, high bits).
 //
-// The split is a lossless byte permutation, except that bytes the reference's
-// dequantiser never reads are dropped (Q3_K_M's 4 bytes at 108..111, Q5_K's
-// qh[16..32), Q8_K's bsums).  High-bit fields (Q5_0/Q5_1/Q5_K qh, Q3_K hmask)
-// are bit-permuted so that the four bits a lane needs for four consecutive
-// bytes sit at bit k of byte k of one 32-bit word (one shift + one mask).
+// Each plane is stored tile by tile: a tile is TILE_ROWS (16) rows x kc columns
+// (kc = 128 chunks of plane 0, the last column tile narrower), and the bytes of
+// one tile of one plane are contiguous in HBM (rows at a 16-byte-aligned tile
+// pitch).  The GEMV therefore moves a tile with one large bulk copy per plane:
+// bulk copies of 1 KB or less reach only ~3-4 TB/s on B200, copies of >= 4 KB
+// with >= 128 KB in flight per SM reach > 7 TB/s.
+//
+// The split keeps every value the reference's dequantiser reads and drops the
+// bytes it never reads (Q3_K_M's 4 bytes at 108..111, Q5_K's qh[16..32), Q8_K's
+// bsums).  High-bit fields (Q5_0/Q5_1/Q5_K qh, Q3_K hmask) are bit-permuted so
+// that the four bits a lane needs for four consecutive bytes sit at bit k of
+// byte k of one 32-bit word (one shift + one mask).  The 12 packed bytes of the
+// Q4_K/Q5_K 6-bit (scale, min) pairs are unpacked with the reference's
+// k_scale_min_6bit (quant.rs:116-124) into sc[8], mn[8] bytes, so the GEMV reads
+// a scale with one byte extract.
 #pragma once
 #include "common.cuh"
 
 namespace ggc {
 
+constexpr int TILE_ROWS = 16;
+
 struct PlaneSpec {
-    int n;          // number of planes
-    int bpb[4];     // bytes per block in each plane
-    int chunk_elems;// elements covered by one 16-byte chunk of plane 0
+    int n;           // number of planes
+    int bpb[4];      // bytes per block in each plane
+    int chunk_elems; // elements covered by one 16-byte chunk of plane 0
 };
 
 __host__ __device__ constexpr PlaneSpec plane_spec(int dt) {
@@ -34,8 +44,8 @@ __host__ __device__ constexpr PlaneSpec plane_spec(int dt) {
          : dt == GGC_Q8_0 ? PlaneSpec{2, {32, 2, 0, 0}, 16}
          : dt == GGC_Q2_K ? PlaneSpec{3, {64, 16, 4, 0}, 64}
          : (dt == GGC_Q3_K_S || dt == GGC_Q3_K_M || dt == GGC_Q3_K_L) ? PlaneSpec{4, {64, 32, 12, 2}, 64}
-         : dt == GGC_Q4_K ? PlaneSpec{2, {128, 16, 0, 0}, 32}
-         : dt == GGC_Q5_K ? PlaneSpec{3, {128, 16, 16, 0}, 32}
+         : dt == GGC_Q4_K ? PlaneSpec{3, {128, 4, 16, 0}, 32}
+         : dt == GGC_Q5_K ? PlaneSpec{4, {128, 16, 4, 16}, 32}
          : dt == GGC_Q6_K ? PlaneSpec{4, {128, 64, 16, 2}, 32}
          : dt == GGC_Q8_K ? PlaneSpec{2, {256, 4, 0, 0}, 16}
          : dt == GGC_F16 ? PlaneSpec{1, {2, 0, 0, 0}, 8}
@@ -44,24 +54,61 @@ __host__ __device__ constexpr PlaneSpec plane_spec(int dt) {
          : PlaneSpec{0, {0, 0, 0, 0}, 0};
 }
 
-// A repacked 2-D weight: `rows` x `cols`, blocks along cols.
-struct QMat {
-    const uint8_t* p[4];
-    uint32_t pitch[4];
-    uint32_t rows, cols;
+// Geometry of a tiled weight (computed identically on host and device).
+struct TileLayout {
+    uint32_t rows, pcols;      // rows, columns padded to the chunk width
+    uint32_t kc, nct, nrb;     // columns of a full column tile, column tiles, row blocks
+    uint32_t tp_full[4];       // tile row pitch of plane p in a full column tile
+    uint32_t tp_last[4];       // ... in the last column tile
+    uint64_t rb_bytes[4];      // bytes of one row block of plane p
 };
 
-// Bytes of one row in plane p, padded to 16.
-inline uint64_t plane_pitch(int dt, int p, uint64_t cols) {
-    PlaneSpec s = plane_spec(dt);
-    uint64_t nb = cols / (uint64_t)block_size_of(dt);
-    uint64_t b = nb * (uint64_t)s.bpb[p];
-    return (b + 15) / 16 * 16;
+__host__ __device__ inline uint32_t round16(uint32_t b) { return (b + 15u) / 16u * 16u; }
+
+__host__ __device__ inline TileLayout make_layout(int dt, uint32_t rows, uint32_t pcols) {
+    const PlaneSpec s = plane_spec(dt);
+    const uint32_t bs = (uint32_t)block_size_of(dt);
+    TileLayout L{};
+    L.rows = rows;
+    L.pcols = pcols;
+    const uint32_t kmax = 128u * (uint32_t)s.chunk_elems;
+    L.kc = pcols < kmax ? pcols : kmax;
+    L.nct = (pcols + L.kc - 1) / L.kc;
+    L.nrb = (rows + TILE_ROWS - 1) / TILE_ROWS;
+    const uint32_t last = pcols - (L.nct - 1) * L.kc;
+    for (int p = 0; p < 4; ++p) {
+        const uint32_t bpb = p < s.n ? (uint32_t)s.bpb[p] : 0u;
+        L.tp_full[p] = round16(L.kc / bs * bpb);
+        L.tp_last[p] = round16(last / bs * bpb);
+        L.rb_bytes[p] = (uint64_t)TILE_ROWS * ((uint64_t)(L.nct - 1) * L.tp_full[p] + L.tp_last[p]);
+    }
+    return L;
 }
 
-// Host: split `rows` raw rows into planes.  `row_src[r]` names the raw row that
-// becomes plane row r (NULL = identity).  Plane buffers must hold rows*pitch.
+// Byte offset of tile (rb, ct) inside plane p.
+__host__ __device__ inline uint64_t tile_offset(const TileLayout& L, int p, uint32_t rb, uint32_t ct) {
+    return (uint64_t)rb * L.rb_bytes[p] + (uint64_t)TILE_ROWS * L.tp_full[p] * ct;
+}
+__host__ __device__ inline uint32_t tile_pitch(const TileLayout& L, int p, uint32_t ct) {
+    return ct + 1 == L.nct ? L.tp_last[p] : L.tp_full[p];
+}
+
+// A tiled weight on the device.
+struct QMat {
+    const uint8_t* p[4];
+    TileLayout L;
+};
+
+// A view of one tile (in shared memory): plane bases and row pitches.
+struct TileView {
+    const uint8_t* p[4];
+    uint32_t pitch[4];
+};
+
+// Host: split `rows` raw GGUF rows into tiled planes.  `row_src[r]` names the raw
+// row that becomes row r (NULL = identity).  planes[p] must hold
+// L.nrb * L.rb_bytes[p] zeroed bytes.
 void repack_rows_host(int dt, const uint8_t* raw, uint64_t rows, uint64_t cols, const uint32_t* row_src,
-                      uint8_t* const planes[4], int nthreads);
+                      const TileLayout& L, uint8_t* const planes[4], int nthreads);
 
 }  // namespace ggc

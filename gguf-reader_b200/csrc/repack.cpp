@@ -1,5 +1,6 @@
 // repack.cpp -- host-side split of raw GGUF rows into the plane layout
 // (see planes.cuh).  Runs once per weight at model load.
+#include <algorithm>
 #include <cstring>
 #include <thread>
 #include <vector>
@@ -27,6 +28,22 @@ uint32_t permute_q5_qh(uint32_t qh) {
             o |= ((qh >> (16 + 4 * w + k)) & 1u) << (8 * k + 4 + w);
         }
     return o;
+}
+
+// quant.rs:116-124 k_scale_min_6bit for j = 0..7 -> sc[j] at out[j], mn[j] at out[8 + j]
+void unpack_scale_min(const uint8_t* q, uint8_t* out) {
+    for (int j = 0; j < 8; ++j) {
+        uint8_t sc, mn;
+        if (j < 4) {
+            sc = q[j] & 0x3F;
+            mn = q[j + 4] & 0x3F;
+        } else {
+            sc = (uint8_t)((q[j + 4] & 0x0F) | ((q[j - 4] >> 6) << 4));
+            mn = (uint8_t)((q[j + 4] >> 4) | ((q[j] >> 6) << 4));
+        }
+        out[j] = sc;
+        out[8 + j] = mn;
+    }
 }
 
 void repack_block(int dt, const uint8_t* b, uint64_t blk, uint8_t* const pl[4]) {
@@ -75,7 +92,8 @@ void repack_block(int dt, const uint8_t* b, uint64_t blk, uint8_t* const pl[4]) 
         }
         case GGC_Q4_K:
             std::memcpy(pl[0] + blk * 128, b + 16, 128);
-            std::memcpy(pl[1] + blk * 16, b, 16);
+            std::memcpy(pl[1] + blk * 4, b, 4);
+            unpack_scale_min(b + 4, pl[2] + blk * 16);
             break;
         case GGC_Q5_K: {
             std::memcpy(pl[0] + blk * 128, b + 48, 128);
@@ -89,7 +107,8 @@ void repack_block(int dt, const uint8_t* b, uint64_t blk, uint8_t* const pl[4]) 
                 words[p / 2] |= bit << (8 * k + w + 4 * (p % 2));
             }
             for (int i = 0; i < 4; ++i) wr32(pl[1] + blk * 16 + 4 * i, words[i]);
-            std::memcpy(pl[2] + blk * 16, b, 16);
+            std::memcpy(pl[2] + blk * 4, b, 4);
+            unpack_scale_min(b + 4, pl[3] + blk * 16);
             break;
         }
         case GGC_Q6_K:
@@ -116,18 +135,26 @@ void repack_block(int dt, const uint8_t* b, uint64_t blk, uint8_t* const pl[4]) 
 }  // namespace
 
 void repack_rows_host(int dt, const uint8_t* raw, uint64_t rows, uint64_t cols, const uint32_t* row_src,
-                      uint8_t* const planes[4], int nthreads) {
-    PlaneSpec s = plane_spec(dt);
+                      const TileLayout& L, uint8_t* const planes[4], int nthreads) {
+    const PlaneSpec s = plane_spec(dt);
     const uint64_t bs = (uint64_t)block_size_of(dt), bb = (uint64_t)block_bytes_of(dt);
     const uint64_t nb = cols / bs, row_bytes = nb * bb;
-    uint64_t pitch[4] = {0, 0, 0, 0};
-    for (int p = 0; p < s.n; ++p) pitch[p] = plane_pitch(dt, p, cols);
+    const uint64_t blocks_per_tile = L.kc / bs;
     auto work = [&](uint64_t r0, uint64_t r1) {
         for (uint64_t r = r0; r < r1; ++r) {
             const uint8_t* src = raw + (uint64_t)(row_src ? row_src[r] : r) * row_bytes;
-            uint8_t* pl[4] = {nullptr, nullptr, nullptr, nullptr};
-            for (int p = 0; p < s.n; ++p) pl[p] = planes[p] + r * pitch[p];
-            for (uint64_t k = 0; k < nb; ++k) repack_block(dt, src + k * bb, k, pl);
+            const uint32_t rb = (uint32_t)(r / TILE_ROWS), rl = (uint32_t)(r % TILE_ROWS);
+            for (uint32_t ct = 0; ct < L.nct; ++ct) {
+                uint8_t* pl[4] = {nullptr, nullptr, nullptr, nullptr};
+                for (int p = 0; p < s.n; ++p)
+                    pl[p] = planes[p] + tile_offset(L, p, rb, ct) + (uint64_t)rl * tile_pitch(L, p, ct);
+                const uint64_t k0 = ct * blocks_per_tile, k1 = std::min<uint64_t>(nb, k0 + blocks_per_tile);
+                if (bs == 1) {   // float formats: one contiguous run per tile row
+                    if (k1 > k0) std::memcpy(pl[0], src + k0 * bb, (k1 - k0) * bb);
+                } else {
+                    for (uint64_t k = k0; k < k1; ++k) repack_block(dt, src + k * bb, k - k0, pl);
+                }
+            }
         }
     };
     if (nthreads <= 1 || rows < 64) {
