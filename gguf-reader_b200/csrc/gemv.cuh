@@ -487,8 +487,13 @@ __device__ __forceinline__ float2 h2f2(uint32_t dd) { return __half22float2(*rei
 
 template <int DT> struct DecI { static constexpr bool ok = false; };
 
+// Each INT decoder also names the contiguous x range of a (chunk, scale group):
+// GL elements from grp_base(c, g); step t's four values sit at off(t, j) in it.
 template <> struct DecI<GGC_Q4_K> {
     static constexpr bool ok = true;
+    static constexpr int GL = 16;
+    __device__ static int grp_base(int c, int g) { const int b = c >> 3, p = c & 7; return b * 256 + 64 * (p >> 1) + 32 * g + 16 * (p & 1); }
+    __device__ static constexpr int off(int t, int j) { return 4 * (t >> 1) + j; }
     __device__ static float dot(const Dec<GGC_Q4_K>::Ch& ch, const uint32_t* L, const float* gs, const float* sx, int) {
         const uint32_t w[4] = {ch.q.x, ch.q.y, ch.q.z, ch.q.w};
         Acc3 A, B;
@@ -506,6 +511,12 @@ template <> struct DecI<GGC_Q4_K> {
 
 template <> struct DecI<GGC_Q6_K> {
     static constexpr bool ok = true;
+    static constexpr int GL = 16;
+    __device__ static int grp_base(int c, int g) {
+        const int b = c >> 3, p = c & 7, n = p >> 2, part = p & 3;
+        return b * 256 + 128 * n + 16 * (part & 1) + (part < 2 ? 0 : 32) + 64 * g;
+    }
+    __device__ static constexpr int off(int t, int j) { return 4 * (t >> 1) + j; }
     __device__ static float dot(const Dec<GGC_Q6_K>::Ch& ch, const uint32_t* L, const float* gs, const float* sx, int c) {
         const uint32_t w[4] = {ch.q.x, ch.q.y, ch.q.z, ch.q.w};
         const uint32_t h[4] = {ch.qh.x, ch.qh.y, ch.qh.z, ch.qh.w};
@@ -532,6 +543,9 @@ template <> struct DecI<GGC_Q6_K> {
 
 template <> struct DecI<GGC_Q4_0> {
     static constexpr bool ok = true;
+    static constexpr int GL = 32;
+    __device__ static int grp_base(int c, int) { return 32 * c; }
+    __device__ static constexpr int off(int t, int j) { return 2 * (4 * (t >> 1) + j) + (t & 1); }
     __device__ static float dot(const Dec<GGC_Q4_0>::Ch& ch, const uint32_t* L, const float* gs, const float* sx, int) {
         const uint32_t w[4] = {ch.q.x, ch.q.y, ch.q.z, ch.q.w};
         Acc3 A;
@@ -547,6 +561,9 @@ template <> struct DecI<GGC_Q4_0> {
 
 template <> struct DecI<GGC_Q8_0> {
     static constexpr bool ok = true;
+    static constexpr int GL = 16;
+    __device__ static int grp_base(int c, int) { return 16 * c; }
+    __device__ static constexpr int off(int t, int j) { return 4 * t + j; }
     __device__ static float dot(const Dec<GGC_Q8_0>::Ch& ch, const uint32_t* L, const float* gs, const float*, int) {
         Acc3 A;
         dp3s(ch.q.x, L + 0, A);
@@ -613,7 +630,7 @@ constexpr int GEMV_NCS = 4;                // column slices of 32 chunks per til
 constexpr int GEMV_NRG = GEMV_WARPS / GEMV_NCS;
 constexpr int GEMV_R = TILE_ROWS / GEMV_NRG;   // rows per warp per tile
 constexpr int GEMV_MAX_STAGES = 4;
-constexpr uint32_t GEMV_WAIT_LIMIT = 1u << 22;
+constexpr uint32_t GEMV_WAIT_LIMIT = 1u << 16;   // x up to 20 us suspend each: ~1.3 s bound
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
@@ -627,7 +644,7 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 20000;\n selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
         : "r"(smem_u32(bar)), "r"(parity)
         : "memory");
@@ -842,7 +859,16 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(const GemvArgs a, cons
     const uint32_t ctid = tid, cthreads = GEMV_WARPS * 32;
     if (a.pro == PRO_RMSNORM) {
         double ss = 0.0;
-        for (uint32_t i = ctid; i < a.xcols; i += cthreads) { const double v = (double)a.x[i]; ss += v * v; }
+        if ((a.xcols & 3) == 0) {
+            const float4* x4 = reinterpret_cast<const float4*>(a.x);
+            for (uint32_t i = ctid; i < a.xcols / 4; i += cthreads) {
+                const float4 v = x4[i];
+                ss += (double)v.x * (double)v.x + (double)v.y * (double)v.y + (double)v.z * (double)v.z +
+                      (double)v.w * (double)v.w;
+            }
+        } else {
+            for (uint32_t i = ctid; i < a.xcols; i += cthreads) { const double v = (double)a.x[i]; ss += v * v; }
+        }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         if (lane == 0) red[warp] = ss;
@@ -856,33 +882,59 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(const GemvArgs a, cons
     }
     const float scale = (a.pro == PRO_RMSNORM) ? s_scale : 0.f;
     if constexpr (INT) {
-        // one thread per (chunk, scale group): values -> power-of-two scale -> limbs
+        // one thread per (chunk, scale group): its GL contiguous x values with float4
+        // loads issued back to back -> power-of-two scale -> limbs
+        using DI = DecI<DT>;
+        constexpr int GL = DI::GL;
         for (uint32_t q = ctid; q < nch * NG; q += cthreads) {
             const uint32_t c = q / NG, g = q % NG;
-            float v[D::T][4];
-            float mx = 0.f, sum = 0.f;
+            const int base = DI::grp_base((int)c, (int)g);
+            float v[GL];
+            {
+                const float4* x4 = reinterpret_cast<const float4*>(a.x + base);
+                float4 xa[GL / 4], xb[GL / 4];
 #pragma unroll
-            for (int t = 0; t < D::T; ++t) {
-                if (NG > 1 && D::group(t) != (int)g) continue;
+                for (int k = 0; k < GL / 4; ++k) xa[k] = x4[k];
+                if (a.pro != PRO_PLAIN) {
+                    const float4* y4 = reinterpret_cast<const float4*>(a.x2 + base);
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    v[t][j] = gemv_xval(a, (uint32_t)D::elem((int)c, t, j), scale);
-                    mx = fmaxf(mx, fabsf(v[t][j]));
-                    sum += v[t][j];
+                    for (int k = 0; k < GL / 4; ++k) xb[k] = y4[k];
+                }
+#pragma unroll
+                for (int k = 0; k < GL / 4; ++k) {
+                    const float xx[4] = {xa[k].x, xa[k].y, xa[k].z, xa[k].w};
+                    const float yy[4] = {xb[k].x, xb[k].y, xb[k].z, xb[k].w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        float r = xx[j];
+                        if (a.pro == PRO_RMSNORM) {
+                            r = __fmul_rn(__fmul_rn(xx[j], scale), yy[j]);   // ops.rs:272
+                        } else if (a.pro == PRO_SWIGLU) {                 // ops.rs:237-247, llama.rs:564-567
+                            const float gg = xx[j];
+                            float sig;
+                            if (gg >= 0.0f) sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gg)));
+                            else { const float ex = expf(gg); sig = __fdiv_rn(ex, __fadd_rn(1.0f, ex)); }
+                            r = __fmul_rn(__fmul_rn(gg, sig), yy[j]);
+                        }
+                        v[4 * k + j] = r;
+                    }
                 }
             }
-            int k = 0;
-            frexpf(mx, &k);
+            float mx = 0.f, sum = 0.f;
+#pragma unroll
+            for (int k = 0; k < GL; ++k) { mx = fmaxf(mx, fabsf(v[k])); sum += v[k]; }
+            int ex = 0;
+            frexpf(mx, &ex);
             const bool finite = isfinite(mx) && isfinite(sum);
-            const float mul = (mx > 0.f && finite) ? ldexpf(1.f, 22 - k) : 0.f;
-            const float gs = !finite ? __int_as_float(0x7FC00000) : (mx > 0.f ? ldexpf(1.f, k - 22) : 0.f);
+            const float mul = (mx > 0.f && finite) ? ldexpf(1.f, 22 - ex) : 0.f;
+            const float gs = !finite ? __int_as_float(0x7FC00000) : (mx > 0.f ? ldexpf(1.f, ex - 22) : 0.f);
 #pragma unroll
             for (int t = 0; t < D::T; ++t) {
                 if (NG > 1 && D::group(t) != (int)g) continue;
                 uint32_t w0 = 0, w1 = 0, w2 = 0;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    const int xi = __float2int_rn(v[t][j] * mul);
+                    const int xi = __float2int_rn(v[DI::off(t, j)] * mul);
                     w0 |= (uint32_t)(xi & 0xFF) << (8 * j);
                     w1 |= (uint32_t)((xi >> 8) & 0xFF) << (8 * j);
                     w2 |= (uint32_t)((xi >> 16) & 0xFF) << (8 * j);
