@@ -21,6 +21,7 @@
 #include "planes.cuh"
 #include "gemv.cuh"
 #include "attention.cuh"
+#include "noalloc.cuh"
 
 using namespace ggc;
 
@@ -356,6 +357,81 @@ extern "C" int ggc_quant_matvec(ggc_ctx* ctx, int dtype, const void* w, uint64_t
         GGC_CUDA_TRY(cudaMemcpyAsync(y, dy, rows * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
         GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
     }
+    return GGC_OK;
+}
+
+// ---------------------------------------------------------------------------
+// ggc_quant_matvec_static: the same product as ggc_quant_matvec over device
+// buffers, split over columns, with its scratch in g_noalloc_scratch.  It calls
+// no allocating routine: the first call on a device looks the scratch up with
+// cudaGetSymbolAddress (device current) and caches the pointer; every call then
+// clears the tickets it uses and launches on the caller's stream.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int NOALLOC_MAX_DEVICES = 64;
+
+int noalloc_scratch(int dev, unsigned char** out) {
+    static std::mutex mu;
+    static unsigned char* ptr[NOALLOC_MAX_DEVICES] = {};
+    if (dev < 0 || dev >= NOALLOC_MAX_DEVICES) return set_error(GGC_ERR_INVALID_ARG, "device %d out of range", dev);
+    std::lock_guard<std::mutex> lk(mu);
+    if (!ptr[dev]) {
+        void* p = nullptr;
+        GGC_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+        ptr[dev] = static_cast<unsigned char*>(p);
+    }
+    *out = ptr[dev];
+    return GGC_OK;
+}
+
+template <int DT>
+struct RunMatvecSplitK {
+    static void run(const uint8_t* w, uint64_t rows, uint64_t cols, const float* x, float* y, dim3 grid,
+                    uint32_t nsplit, uint64_t per, unsigned char* scratch, cudaStream_t st, cudaError_t* err) {
+        k_matvec_raw_splitk<DT><<<grid, 256, 0, st>>>(w, rows, cols, x, y, nsplit, per, scratch);
+        *err = cudaGetLastError();
+    }
+};
+
+}  // namespace
+
+extern "C" int ggc_quant_matvec_static(int dtype, const void* w, uint64_t w_len, uint64_t rows, uint64_t cols,
+                                       const float* x, uint64_t x_len, float* y, uint64_t y_len, void* stream) {
+    const int bs = block_size_of(dtype), bb = block_bytes_of(dtype);
+    if (bs < 0 || bb < 0) return set_dequant_error(dtype, 0, 0, "unsupported dtype");
+    if (cols % (uint64_t)bs != 0) return set_shape_error(cols, (uint64_t)bs, "row_bytes");
+    const uint64_t rb = cols / bs * (uint64_t)bb;
+    if (x_len != cols) return set_dequant_error(dtype, cols, x_len, "x length != cols");
+    if (y_len != rows) return set_dequant_error(dtype, rows, y_len, "y length != rows");
+    if (rows * rb > w_len) return set_dequant_error(dtype, rows * rb, w_len, "w shorter than rows*row_bytes");
+    if (rows > NOALLOC_MAX_ROWS)
+        return set_error(GGC_ERR_INVALID_ARG, "rows %llu exceed the static scratch (at most %llu rows)",
+                         (unsigned long long)rows, (unsigned long long)NOALLOC_MAX_ROWS);
+    if (rows == 0) return GGC_OK;
+    if (!w || !y || (!x && cols)) return set_error(GGC_ERR_INVALID_ARG, "null buffer");
+    if (!is_device_ptr(w) || !is_device_ptr(y) || (cols && !is_device_ptr(x)))
+        return set_error(GGC_ERR_INVALID_ARG, "w, x and y must be device buffers");
+    int dev = 0, sms = 148;
+    GGC_CUDA_TRY(cudaGetDevice(&dev));
+    GGC_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    unsigned char* scratch = nullptr;
+    GGC_TRY(noalloc_scratch(dev, &scratch));
+    // enough CTAs for ~8 per SM, at most NOALLOC_MAX_SPLIT splits, partials in scratch
+    const uint64_t groups = cdiv<uint64_t>(rows, NOALLOC_ROWS_PER_CTA), nblk = cols / bs;
+    uint64_t ns = cdiv<uint64_t>((uint64_t)sms * 8, groups);
+    if (ns > NOALLOC_MAX_SPLIT) ns = NOALLOC_MAX_SPLIT;
+    if (ns > NOALLOC_MAX_PARTIALS / rows) ns = NOALLOC_MAX_PARTIALS / rows;
+    if (ns > nblk) ns = nblk;
+    if (ns < 1) ns = 1;
+    const uint64_t per = cdiv<uint64_t>(nblk ? nblk : 1, ns);
+    ns = cdiv<uint64_t>(nblk ? nblk : 1, per);   // no empty split
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    GGC_CUDA_TRY(cudaMemsetAsync(scratch, 0, groups * sizeof(uint32_t), st));
+    cudaError_t err = cudaSuccess;
+    dispatch_dtype<RunMatvecSplitK>(dtype, (const uint8_t*)w, rows, cols, x, y, dim3((unsigned)groups, (unsigned)ns),
+                                    (uint32_t)ns, per, scratch, st, &err);
+    GGC_CUDA_TRY(err);
     return GGC_OK;
 }
 

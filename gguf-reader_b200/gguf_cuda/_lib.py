@@ -126,6 +126,7 @@ SIGNATURES = {
     "ggc_ctx_kernel_launches": (_u64, [_vp]),
     "ggc_dequantize": (_i32, [_vp, _i32, _vp, _u64, _u64, _vp]),
     "ggc_quant_matvec": (_i32, [_vp, _i32, _vp, _u64, _u64, _u64, _vp, _u64, _vp, _u64]),
+    "ggc_quant_matvec_static": (_i32, [_i32, _vp, _u64, _u64, _u64, _vp, _u64, _vp, _u64, _vp]),
     "ggc_tensor_upload": (_i32, [_vp, _vp, _u64, _i32, C.POINTER(_u64), _i32, _i32, C.POINTER(_vp)]),
     "ggc_tensor_free": (_i32, [_vp]),
     "ggc_tensor_matvec": (_i32, [_vp, _vp, _vp, _vp]),

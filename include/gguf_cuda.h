@@ -94,6 +94,26 @@ int ggc_dequantize(ggc_ctx* ctx, int dtype, const void* raw, uint64_t raw_len, u
 int ggc_quant_matvec(ggc_ctx* ctx, int dtype, const void* w, uint64_t w_len, uint64_t rows,
                      uint64_t cols, const float* x, uint64_t x_len, float* y, uint64_t y_len);
 
+/* No counterpart in the reference (it has no allocation-free entry point).
+ * The ggc_quant_matvec product for callers that must not allocate device
+ * memory: w, x, y are the caller's DEVICE buffers on the current device, the
+ * work is queued on `stream` (cudaStream_t as void*; NULL = legacy default
+ * stream) and the call returns without synchronising.  The columns are split
+ * across CTAs; partial sums and per-row-group tickets live in a 4 MiB + 32 KiB
+ * file-scope device array of the library, so the call runs no cudaMalloc,
+ * cudaFree or other allocating routine and needs no ggc_ctx.
+ *   - rows <= 65536, else GGC_ERR_INVALID_ARG (message names the limit); the
+ *     other errors are those of ggc_quant_matvec, in the same order.
+ *   - The first call on each device does a one-time set-up
+ *     (cudaGetSymbolAddress of the scratch, with that device current); make
+ *     that first call before any stream capture on the device.
+ *   - Each call clears the tickets it uses (cudaMemsetAsync on `stream`).
+ *   - One scratch per device: calls that overlap on a device (several streams
+ *     or host threads at once) race on it; the caller serialises them.
+ * Results agree with ggc_quant_matvec within f32 summation-order differences. */
+int ggc_quant_matvec_static(int dtype, const void* w, uint64_t w_len, uint64_t rows, uint64_t cols,
+                            const float* x, uint64_t x_len, float* y, uint64_t y_len, void* stream);
+
 /* ---- device-resident tensors (the loader side of LlamaModel::materialize,
  *      src/infer/model/llama.rs:183-204; weights stay quantized in HBM) ------- */
 typedef struct ggc_tensor ggc_tensor;
