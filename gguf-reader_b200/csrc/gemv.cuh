@@ -1011,15 +1011,20 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(const GemvArgs a, cons
         TileView v;
 #pragma unroll
         for (int p = 0; p < 4; ++p) { v.p[p] = st + tc.poff[p]; v.pitch[p] = tile_pitch(L, p, ct); }
+        // the R rows are computed branch-free (clamped row / chunk, masked result) so
+        // their dependent integer chains interleave
         float accr[R];
+        {
+            const uint32_t cc = (uint32_t)(valid ? c : 0);
+            typename D::Ch ch[R];
 #pragma unroll
-        for (int k = 0; k < R; ++k) {
-            const uint32_t r = (uint32_t)(rg + GEMV_NRG * k);
-            accr[k] = 0.f;
-            if (valid && r < nrows) {
-                const typename D::Ch ch = D::load(v, r, (uint32_t)c);
-                if constexpr (INT) accr[k] = DecI<DT>::dot(ch, Lr, gsr, sxr, c);
-                else accr[k] = chunk_dot<DT>(ch, xr, 1, sxr, c);
+            for (int k = 0; k < R; ++k) ch[k] = D::load(v, min((uint32_t)(rg + GEMV_NRG * k), nrows - 1), cc);
+#pragma unroll
+            for (int k = 0; k < R; ++k) {
+                float d;
+                if constexpr (INT) d = DecI<DT>::dot(ch[k], Lr, gsr, sxr, (int)cc);
+                else d = chunk_dot<DT>(ch[k], xr, 1, sxr, (int)cc);
+                accr[k] = (valid && (uint32_t)(rg + GEMV_NRG * k) < nrows) ? d : 0.f;
             }
         }
 #pragma unroll
