@@ -20,6 +20,7 @@
 #pragma once
 #include "common.cuh"
 #include "planes.cuh"
+#include "mbarrier.cuh"
 
 namespace ggc {
 
@@ -591,7 +592,7 @@ struct Seg {
     QMat m;
     int epi;
     float* out;             // destination (EPI_STORE/EPI_ROPE_Q/EPI_RESID/EPI_LOGITS)
-    void* cache;            // K or V cache of this layer (EPI_ROPE_KC / EPI_VC), [slot][rows]
+    void* cache;            // K or V cache of this layer (EPI_ROPE_KC / EPI_VC), [kv head][kv_ctx][hd]
     const float* bias;      // indexed by logical row; may be null
 };
 
@@ -609,6 +610,7 @@ struct GemvArgs {
     const int64_t* pos;     // position of this step (RoPE)
     const float2* rope;     // [max_ctx][hd/2] (cos, sin)
     uint32_t hd;
+    uint32_t kv_ctx;        // cache rows per kv head (the cache is [kv head][kv_ctx][hd])
     int kv_f16;
     int* errf;
     int err_slot;           // error-flag slot for EPI_RESID NaN
@@ -630,40 +632,7 @@ constexpr int GEMV_NCS = 4;                // column slices of 32 chunks per til
 constexpr int GEMV_NRG = GEMV_WARPS / GEMV_NCS;
 constexpr int GEMV_R = TILE_ROWS / GEMV_NRG;   // rows per warp per tile
 constexpr int GEMV_MAX_STAGES = 4;
-constexpr uint32_t GEMV_WAIT_LIMIT = 1u << 16;   // x up to 20 us suspend each: ~1.3 s bound
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 20000;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Bounded wait on phase `parity`; false (and ERRF_TIMEOUT) when the limit expires.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* errf) {
-    for (uint32_t i = 0; i < GEMV_WAIT_LIMIT; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
-    if (errf) atomicExch(&errf[ERRF_TIMEOUT], 1);
-    return false;
-}
-// 1-D bulk copy global -> shared, completion counted on `bar` (no multicast)
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_u32(dst)),
-                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
-}
+constexpr uint32_t GEMV_WAIT_LIMIT = BULK_WAIT_LIMIT;
 
 __device__ __forceinline__ unsigned long long argmax_key_of(float v, uint32_t idx) {
     uint32_t b = __float_as_uint(v);
@@ -684,7 +653,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, const Seg& sg, 
                 nan |= isnan(acc[r]);
                 sg.out[r0 + r] = __fadd_rn(sg.out[r0 + r], acc[r]);
             }
-            if (nan) atomicMax(&a.errf[a.err_slot], a.err_val);
+            if (nan) atomicCAS(&a.errf[a.err_slot], 0, a.err_val);   // layers run in order: the first NaN layer stays
             break;
         }
         case EPI_LOGITS: {
@@ -701,11 +670,13 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, const Seg& sg, 
             break;
         }
         case EPI_VC: {   // llama.rs:466-469 then cache.rs:46-54 (rows not permuted)
-            const uint64_t base = (uint64_t)(*a.slot) * sg.m.L.rows;
+            const uint32_t slot = *a.slot;
             for (uint32_t r = 0; r < nvalid; ++r) {
-                const float v = sg.bias ? __fadd_rn(acc[r], sg.bias[r0 + r]) : acc[r];
-                if (a.kv_f16) reinterpret_cast<__half*>(sg.cache)[base + r0 + r] = __float2half_rn(v);
-                else reinterpret_cast<float*>(sg.cache)[base + r0 + r] = v;
+                const uint32_t lr = r0 + r, head = lr / a.hd;
+                const uint64_t idx = ((uint64_t)head * a.kv_ctx + slot) * a.hd + (lr - head * a.hd);
+                const float v = sg.bias ? __fadd_rn(acc[r], sg.bias[lr]) : acc[r];
+                if (a.kv_f16) reinterpret_cast<__half*>(sg.cache)[idx] = __float2half_rn(v);
+                else reinterpret_cast<float*>(sg.cache)[idx] = v;
             }
             break;
         }
@@ -724,13 +695,13 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, const Seg& sg, 
             if (sg.epi == EPI_ROPE_Q) {
                 sg.out[l0] = n0; sg.out[l1] = n1;
             } else {
-                const uint64_t base = (uint64_t)(*a.slot) * sg.m.L.rows;
+                const uint64_t base = ((uint64_t)head * a.kv_ctx + *a.slot) * a.hd;
                 if (a.kv_f16) {
                     __half* c = reinterpret_cast<__half*>(sg.cache);
-                    c[base + l0] = __float2half_rn(n0); c[base + l1] = __float2half_rn(n1);
+                    c[base + j] = __float2half_rn(n0); c[base + j + half] = __float2half_rn(n1);
                 } else {
                     float* c = reinterpret_cast<float*>(sg.cache);
-                    c[base + l0] = n0; c[base + l1] = n1;
+                    c[base + j] = n0; c[base + j + half] = n1;
                 }
             }
             break;

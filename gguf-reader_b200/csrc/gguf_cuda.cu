@@ -4,6 +4,7 @@
 // tensors and the LlamaModel forward / Engine greedy loop.  Kernels live in the
 // included .cuh files.  Built with -fmad=false so that the dequantisers' f32
 // arithmetic is never contracted into FMAs (bit-exact with the reference).
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdlib>
@@ -114,6 +115,8 @@ struct ggc_ctx {
     int rank = 0, world = 1;
     ncclComm_t comm = nullptr;
     uint64_t launches = 0;
+    // owner + one per live model / tensor: the context outlives everything made on it
+    std::atomic<int> refs{1};
     // staging buffers for host arguments
     void* stage[3] = {nullptr, nullptr, nullptr};
     size_t stage_cap[3] = {0, 0, 0};
@@ -280,8 +283,9 @@ extern "C" int ggc_ctx_create_tp(int device, int rank, int world, const void* nc
     return GGC_OK;
 }
 
-extern "C" int ggc_ctx_destroy(ggc_ctx* ctx) {
-    if (!ctx) return GGC_OK;
+namespace {
+void ctx_release(ggc_ctx* ctx) {
+    if (ctx->refs.fetch_sub(1) != 1) return;
     {
         DeviceGuard g(ctx->device);
         cudaStreamSynchronize(ctx->stream);
@@ -291,6 +295,13 @@ extern "C" int ggc_ctx_destroy(ggc_ctx* ctx) {
         cudaStreamDestroy(ctx->stream);
     }
     delete ctx;
+}
+}  // namespace
+
+// Releases the caller's reference; the context is freed once the models and
+// tensors made on it are destroyed too (in any order).
+extern "C" int ggc_ctx_destroy(ggc_ctx* ctx) {
+    if (ctx) ctx_release(ctx);
     return GGC_OK;
 }
 
@@ -533,6 +544,53 @@ struct SetGemvSmem {
     }
 };
 
+// Every k_attn_decode instantiation (head dim 64/128/256, f32/f16 cache, group
+// bound 1/4/8) with its dynamic shared memory.
+template <int HD, bool F16, int MAXG>
+struct AttnDecodeKernel {
+    static constexpr auto kernel = k_attn_decode<HD, F16, MAXG>;
+    static constexpr size_t smem = FaCfg<HD, F16, MAXG>::SMEM;
+};
+// group bound 8 at hd 256 would hold 128 registers of q and accumulators alone:
+// that shape takes the general pair
+template <int HD>
+constexpr bool attn_decode_g8 = HD < 256;
+template <int HD, bool F16, class F>
+void for_each_attn_decode_g(F& f) {
+    f(AttnDecodeKernel<HD, F16, 1>::kernel, AttnDecodeKernel<HD, F16, 1>::smem);
+    f(AttnDecodeKernel<HD, F16, 4>::kernel, AttnDecodeKernel<HD, F16, 4>::smem);
+    if constexpr (attn_decode_g8<HD>) f(AttnDecodeKernel<HD, F16, 8>::kernel, AttnDecodeKernel<HD, F16, 8>::smem);
+}
+template <class F>
+void for_each_attn_decode(F&& f) {
+    for_each_attn_decode_g<64, false>(f); for_each_attn_decode_g<64, true>(f);
+    for_each_attn_decode_g<128, false>(f); for_each_attn_decode_g<128, true>(f);
+    for_each_attn_decode_g<256, false>(f); for_each_attn_decode_g<256, true>(f);
+}
+
+// The k_attn_decode instantiation for (hd, f16 cache, group), or null when the
+// shape needs the general k_attn_scores / k_attn_av pair.
+struct AttnDecodeSel {
+    void (*kernel)(const AttnArgs) = nullptr;
+    size_t smem = 0;
+};
+template <int HD, bool F16>
+AttnDecodeSel attn_decode_sel_g(uint32_t G) {
+    if (G == 1) return {AttnDecodeKernel<HD, F16, 1>::kernel, AttnDecodeKernel<HD, F16, 1>::smem};
+    if (G <= 4) return {AttnDecodeKernel<HD, F16, 4>::kernel, AttnDecodeKernel<HD, F16, 4>::smem};
+    if constexpr (attn_decode_g8<HD>)
+        if (G <= 8) return {AttnDecodeKernel<HD, F16, 8>::kernel, AttnDecodeKernel<HD, F16, 8>::smem};
+    return {};
+}
+AttnDecodeSel attn_decode_sel(uint32_t hd, bool f16, uint32_t G) {
+    switch (hd) {
+        case 64: return f16 ? attn_decode_sel_g<64, true>(G) : attn_decode_sel_g<64, false>(G);
+        case 128: return f16 ? attn_decode_sel_g<128, true>(G) : attn_decode_sel_g<128, false>(G);
+        case 256: return f16 ? attn_decode_sel_g<256, true>(G) : attn_decode_sel_g<256, false>(G);
+        default: return {};
+    }
+}
+
 int init_kernel_attrs() {
     static std::once_flag once;
     static int ok = 1;
@@ -541,6 +599,9 @@ int init_kernel_attrs() {
                            GGC_Q2_K, GGC_Q3_K_S, GGC_Q3_K_M, GGC_Q3_K_L, GGC_Q4_K, GGC_Q5_K, GGC_Q6_K, GGC_Q8_K};
         for (int dt : dts) dispatch_dtype<SetGemvSmem>(dt, &ok);
         if (cudaFuncSetAttribute(k_attn_av, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024) != cudaSuccess) ok = 0;
+        for_each_attn_decode([](auto kernel, size_t smem) {
+            if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) ok = 0;
+        });
     });
     if (!ok) return set_error(GGC_ERR_CUDA, "cudaFuncSetAttribute failed");
     return GGC_OK;
@@ -623,17 +684,22 @@ extern "C" int ggc_tensor_upload(ggc_ctx* ctx, const void* raw, uint64_t bytes, 
         GGC_CUDA_TRY(cudaMemcpy(t->raw, raw, need, cudaMemcpyHostToDevice));
         t->raw_bytes = need;
     }
+    ctx->refs++;
     *out = t.release();
     return GGC_OK;
 }
 
 extern "C" int ggc_tensor_free(ggc_tensor* t) {
     if (!t) return GGC_OK;
-    DeviceGuard g(t->ctx->device);
-    cudaStreamSynchronize(t->ctx->stream);
-    free_mat(t->mat);
-    if (t->raw) cudaFree(t->raw);
+    ggc_ctx* ctx = t->ctx;
+    {
+        DeviceGuard g(ctx->device);
+        cudaStreamSynchronize(ctx->stream);
+        free_mat(t->mat);
+        if (t->raw) cudaFree(t->raw);
+    }
     delete t;
+    ctx_release(ctx);
     return GGC_OK;
 }
 
@@ -807,7 +873,8 @@ struct ggc_model {
     float2* rope = nullptr;
     // activations / scratch
     float *hidden = nullptr, *q = nullptr, *o = nullptr, *ubuf = nullptr, *gbuf = nullptr, *logits = nullptr;
-    float *scores = nullptr, *pmax = nullptr, *opart = nullptr;
+    float *scores = nullptr, *pmax = nullptr, *psum = nullptr, *opart = nullptr;
+    AttnDecodeSel attn;   // fused decode attention, or null for the general pair
     float2* stats = nullptr;
     unsigned* tickets = nullptr;
     unsigned long long* argmax_key = nullptr;
@@ -922,6 +989,7 @@ int enqueue_step(ggc_model* m) {
     base.pos = &m->st->pos;
     base.rope = m->rope;
     base.hd = m->hd;
+    base.kv_ctx = hp.max_ctx;
     base.kv_f16 = hp.kv_f16 ? 1 : 0;
     base.errf = m->errf;
     base.argmax_key = m->argmax_key;
@@ -956,9 +1024,15 @@ int enqueue_step(ggc_model* m) {
         aa.nsplit = m->nsplit;
         aa.inv = 1.0f / sqrtf((float)m->hd);
         aa.kv_f16 = base.kv_f16;
-        GGC_CUDA_TRY(launch(ctx, k_attn_scores, dim3(hp.n_kv_heads, m->nsplit), dim3(ATTN_WARPS * 32), 0, aa));
-        GGC_CUDA_TRY(launch(ctx, k_attn_av, dim3(hp.n_kv_heads, m->nsplit), dim3(ATTN_WARPS * 32),
-                            attn_av_smem(hp.n_heads / hp.n_kv_heads, m->hd), aa));
+        aa.psum = m->psum;
+        aa.errf = m->errf;
+        if (m->attn.kernel) {
+            GGC_CUDA_TRY(launch(ctx, m->attn.kernel, dim3(hp.n_kv_heads, m->nsplit), dim3(FA_THREADS), m->attn.smem, aa));
+        } else {
+            GGC_CUDA_TRY(launch(ctx, k_attn_scores, dim3(hp.n_kv_heads, m->nsplit), dim3(ATTN_WARPS * 32), 0, aa));
+            GGC_CUDA_TRY(launch(ctx, k_attn_av, dim3(hp.n_kv_heads, m->nsplit), dim3(ATTN_WARPS * 32),
+                                attn_av_smem(hp.n_heads / hp.n_kv_heads, m->hd), aa));
+        }
         // output projection + residual (llama.rs:485, :309-311), NaN guard (:300-307)
         GemvArgs ro = base;
         ro.err_slot = ERRF_NAN_ATTN;
@@ -1008,17 +1082,21 @@ int build_graph(ggc_model* m) {
 
 void destroy_model(ggc_model* m) {
     if (!m) return;
-    DeviceGuard g(m->ctx->device);
-    cudaStreamSynchronize(m->ctx->stream);
-    if (m->graph) cudaGraphExecDestroy(m->graph);
-    for (auto& L : m->layers) {
-        free_mat(L.wq); free_mat(L.wk); free_mat(L.wv); free_mat(L.wo);
-        free_mat(L.up); free_mat(L.gate); free_mat(L.down);
+    ggc_ctx* ctx = m->ctx;
+    {
+        DeviceGuard g(ctx->device);
+        cudaStreamSynchronize(ctx->stream);
+        if (m->graph) cudaGraphExecDestroy(m->graph);
+        for (auto& L : m->layers) {
+            free_mat(L.wq); free_mat(L.wk); free_mat(L.wv); free_mat(L.wo);
+            free_mat(L.up); free_mat(L.gate); free_mat(L.down);
+        }
+        free_mat(m->output);
+        for (void* p : m->allocs) cudaFree(p);
+        if (m->rb) cudaFreeHost(m->rb);
     }
-    free_mat(m->output);
-    for (void* p : m->allocs) cudaFree(p);
-    if (m->rb) cudaFreeHost(m->rb);
     delete m;
+    ctx_release(ctx);
 }
 
 }  // namespace
@@ -1041,6 +1119,7 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
     GGC_TRY(init_kernel_attrs());
     std::unique_ptr<ggc_model, void (*)(ggc_model*)> m(new ggc_model(), destroy_model);
     m->ctx = ctx;
+    ctx->refs++;   // released by destroy_model
     m->hp = hp;
     m->hd = hd;
     m->qdim = hp.n_heads * hd;
@@ -1083,7 +1162,7 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
         GGC_TRY(upload_weight(m.get(), L[10], f, d, nullptr, ML.gate, "ffn_gate"));
         GGC_TRY(upload_weight(m.get(), L[11], d, f, nullptr, ML.down, "ffn_down"));
     }
-    // KV cache resident in HBM: [layer][max_ctx][n_kv][hd]
+    // KV cache resident in HBM, head-major: [layer][n_kv][max_ctx][hd]
     const size_t kv_bytes = (size_t)hp.n_layers * hp.max_ctx * m->kvdim * m->kv_elem;
     GGC_TRY(dalloc(m.get(), (uint8_t**)&m->kcache, kv_bytes));
     GGC_TRY(dalloc(m.get(), (uint8_t**)&m->vcache, kv_bytes));
@@ -1101,8 +1180,15 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
         GGC_TRY(dalloc(m.get(), &m->rope, tab.size()));
         GGC_CUDA_TRY(cudaMemcpy(m->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
     }
-    uint32_t ns = cdiv<uint32_t>((uint32_t)ctx->num_sms * 2, hp.n_kv_heads);
-    m->nsplit = ns < 1 ? 1 : (ns > 64 ? 64 : ns);
+    // fused attention: two resident CTAs per SM over (kv head, split); general pair: ~2 per SM, <= 64 splits
+    m->attn = attn_decode_sel(hd, hp.kv_f16 != 0, hp.n_heads / hp.n_kv_heads);
+    if (m->attn.kernel) {
+        const uint32_t ns = (uint32_t)ctx->num_sms * 2 / hp.n_kv_heads;
+        m->nsplit = ns < 1 ? 1 : ns;
+    } else {
+        const uint32_t ns = cdiv<uint32_t>((uint32_t)ctx->num_sms * 2, hp.n_kv_heads);
+        m->nsplit = ns < 1 ? 1 : (ns > 64 ? 64 : ns);
+    }
     GGC_TRY(dalloc(m.get(), &m->hidden, d));
     GGC_TRY(dalloc(m.get(), &m->q, m->qdim));
     GGC_TRY(dalloc(m.get(), &m->o, m->qdim));
@@ -1111,6 +1197,7 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
     GGC_TRY(dalloc(m.get(), &m->logits, hp.vocab_size));
     GGC_TRY(dalloc(m.get(), &m->scores, (size_t)hp.n_heads * hp.max_ctx));
     GGC_TRY(dalloc(m.get(), &m->pmax, (size_t)hp.n_heads * m->nsplit));
+    GGC_TRY(dalloc(m.get(), &m->psum, (size_t)hp.n_heads * m->nsplit));
     GGC_TRY(dalloc(m.get(), &m->stats, hp.n_heads));
     GGC_TRY(dalloc(m.get(), &m->opart, (size_t)m->nsplit * m->qdim));
     GGC_TRY(dalloc(m.get(), &m->tickets, 2 * hp.n_kv_heads));
@@ -1289,6 +1376,25 @@ extern "C" int ggc_model_truncate(ggc_model* m, uint64_t new_len) {
 
 extern "C" int ggc_model_reset_cache(ggc_model* m) { return ggc_model_truncate(m, 0); }
 
+namespace {
+// Copies `seq` rows of [seq][kvh * hd] (element size esz, host or device memory)
+// into / out of the head-major cache rows [h][base .. base + seq) of one layer.
+int kv_rows_to_cache(ggc_model* m, uint8_t* layer, const void* src, uint64_t base, uint64_t seq, size_t esz) {
+    const size_t hd = m->hd, kvdim = m->kvdim;
+    for (uint32_t h = 0; h < m->hp.n_kv_heads; ++h)
+        GGC_CUDA_TRY(cudaMemcpy2D(layer + ((size_t)h * m->hp.max_ctx + base) * hd * esz, hd * esz,
+                                  (const uint8_t*)src + h * hd * esz, kvdim * esz, hd * esz, seq, cudaMemcpyDefault));
+    return GGC_OK;
+}
+int kv_cache_to_rows(ggc_model* m, const uint8_t* layer, void* dst, uint64_t seq, size_t esz) {
+    const size_t hd = m->hd, kvdim = m->kvdim;
+    for (uint32_t h = 0; h < m->hp.n_kv_heads; ++h)
+        GGC_CUDA_TRY(cudaMemcpy2D((uint8_t*)dst + h * hd * esz, kvdim * esz, layer + (size_t)h * m->hp.max_ctx * hd * esz,
+                                  hd * esz, hd * esz, seq, cudaMemcpyDefault));
+    return GGC_OK;
+}
+}  // namespace
+
 extern "C" int ggc_model_cache_append(ggc_model* m, uint32_t layer, const float* k, const float* v, uint64_t seq) {
     if (!m || !k || !v) return set_error(GGC_ERR_INVALID_ARG, "null argument");
     if (layer >= m->hp.n_layers) return set_error(GGC_ERR_INVALID_ARG, "layer %u out of range", layer);
@@ -1298,21 +1404,24 @@ extern "C" int ggc_model_cache_append(ggc_model* m, uint32_t layer, const float*
         return set_error(GGC_ERR_KV_CACHE_OVERFLOW, "KvCacheOverflow { seq_len: %llu, max_seq: %u }",
                          (unsigned long long)(base + seq), m->hp.max_ctx);
     DeviceGuard g(m->ctx->device);
+    GGC_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
     const size_t layer_kv = (size_t)m->hp.max_ctx * m->kvdim * m->kv_elem;
     const size_t n = (size_t)seq * m->kvdim;
-    uint8_t* kd = (uint8_t*)m->kcache + layer * layer_kv + base * m->kvdim * m->kv_elem;
-    uint8_t* vd = (uint8_t*)m->vcache + layer * layer_kv + base * m->kvdim * m->kv_elem;
-    if (m->hp.kv_f16) {
-        std::vector<__half> hk(n), hv(n);
-        std::vector<float> fk(n), fv(n);
-        GGC_CUDA_TRY(cudaMemcpy(fk.data(), k, n * 4, is_device_ptr(k) ? cudaMemcpyDeviceToHost : cudaMemcpyHostToHost));
-        GGC_CUDA_TRY(cudaMemcpy(fv.data(), v, n * 4, is_device_ptr(v) ? cudaMemcpyDeviceToHost : cudaMemcpyHostToHost));
-        for (size_t i = 0; i < n; ++i) { hk[i] = __float2half_rn(fk[i]); hv[i] = __float2half_rn(fv[i]); }
-        GGC_CUDA_TRY(cudaMemcpy(kd, hk.data(), n * 2, cudaMemcpyHostToDevice));
-        GGC_CUDA_TRY(cudaMemcpy(vd, hv.data(), n * 2, cudaMemcpyHostToDevice));
-    } else {
-        GGC_CUDA_TRY(cudaMemcpy(kd, k, n * 4, cudaMemcpyDefault));
-        GGC_CUDA_TRY(cudaMemcpy(vd, v, n * 4, cudaMemcpyDefault));
+    uint8_t* kd = (uint8_t*)m->kcache + layer * layer_kv;
+    uint8_t* vd = (uint8_t*)m->vcache + layer * layer_kv;
+    if (seq) {
+        if (m->hp.kv_f16) {
+            std::vector<__half> hk(n), hv(n);
+            std::vector<float> fk(n), fv(n);
+            GGC_CUDA_TRY(cudaMemcpy(fk.data(), k, n * 4, cudaMemcpyDefault));
+            GGC_CUDA_TRY(cudaMemcpy(fv.data(), v, n * 4, cudaMemcpyDefault));
+            for (size_t i = 0; i < n; ++i) { hk[i] = __float2half_rn(fk[i]); hv[i] = __float2half_rn(fv[i]); }
+            GGC_TRY(kv_rows_to_cache(m, kd, hk.data(), base, seq, 2));
+            GGC_TRY(kv_rows_to_cache(m, vd, hv.data(), base, seq, 2));
+        } else {
+            GGC_TRY(kv_rows_to_cache(m, kd, k, base, seq, 4));
+            GGC_TRY(kv_rows_to_cache(m, vd, v, base, seq, 4));
+        }
     }
     if (layer == m->hp.n_layers - 1) {
         const uint32_t slot = (uint32_t)(base + seq);
@@ -1328,20 +1437,22 @@ extern "C" int ggc_model_cache_read(ggc_model* m, uint32_t layer, float* k, floa
     DeviceGuard g(m->ctx->device);
     GGC_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
     const size_t layer_kv = (size_t)m->hp.max_ctx * m->kvdim * m->kv_elem;
-    const size_t n = (size_t)m->cache_len * m->kvdim;
+    const uint64_t len = m->cache_len;
+    const size_t n = (size_t)len * m->kvdim;
+    if (n == 0) return GGC_OK;
     const uint8_t* kd = (const uint8_t*)m->kcache + layer * layer_kv;
     const uint8_t* vd = (const uint8_t*)m->vcache + layer * layer_kv;
     if (m->hp.kv_f16) {
         std::vector<__half> hk(n), hv(n);
-        GGC_CUDA_TRY(cudaMemcpy(hk.data(), kd, n * 2, cudaMemcpyDeviceToHost));
-        GGC_CUDA_TRY(cudaMemcpy(hv.data(), vd, n * 2, cudaMemcpyDeviceToHost));
+        GGC_TRY(kv_cache_to_rows(m, kd, hk.data(), len, 2));
+        GGC_TRY(kv_cache_to_rows(m, vd, hv.data(), len, 2));
         std::vector<float> fk(n), fv(n);
         for (size_t i = 0; i < n; ++i) { fk[i] = __half2float(hk[i]); fv[i] = __half2float(hv[i]); }
         GGC_CUDA_TRY(cudaMemcpy(k, fk.data(), n * 4, cudaMemcpyDefault));
         GGC_CUDA_TRY(cudaMemcpy(v, fv.data(), n * 4, cudaMemcpyDefault));
     } else {
-        GGC_CUDA_TRY(cudaMemcpy(k, kd, n * 4, cudaMemcpyDefault));
-        GGC_CUDA_TRY(cudaMemcpy(v, vd, n * 4, cudaMemcpyDefault));
+        GGC_TRY(kv_cache_to_rows(m, kd, k, len, 4));
+        GGC_TRY(kv_cache_to_rows(m, vd, v, len, 4));
     }
     return GGC_OK;
 }

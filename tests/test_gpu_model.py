@@ -154,6 +154,48 @@ def test_cache_append_read_truncate(ggc, orc, ctx):   # cache.rs:46-93
     assert m.cache_len() == 0
 
 
+# ---- long cached context: every attention split spans several K/V tiles ------
+# (the fused decode attention streams 16 KB tiles through a 3-stage ring; the
+# general pair covers the shapes the fused kernel does not take)
+HD256 = dict(vocab_size=512, embed_dim=1024, n_heads=4, n_kv_heads=1, ffn_dim=512, n_layers=1, rope_freq_base=1e4,
+             qkv_bias=False, weights="q8_0_normal")
+LONG_CASES = [
+    ("llama2-7b-1layer-ctx1000", "llama2-7b-q4_k_m", 1, 4000, 1000, False),   # hd 128, group 1, 4 tiles / split
+    ("mini-ctx3000", MINI, None, None, 3000, False),                            # hd 64, group 4
+    ("mini-ctx3000-kv-f16", MINI, None, None, 3000, True),                      # hd 64, f16 cache
+    ("llama3-8b-1layer-ctx1500-kv-f16", "llama3-8b-q4_0", 1, 4000, 1500, True),  # hd 128, group 4, f16 cache
+    ("hd256-g4-ctx2500", HD256, None, None, 2500, False),                       # hd 256, group 4
+    ("hd256-g8-ctx600", dict(HD256, embed_dim=2048, n_heads=8), None, None, 600, False),   # general pair
+    ("hd64-g8-ctx2000", dict(MINI, n_kv_heads=1), None, None, 2000, False),     # group 8
+    ("hd32-g2-ctx700", dict(MINI, n_heads=16, n_kv_heads=8), None, None, 700, False),      # hd 32: general pair
+]
+
+
+@pytest.mark.parametrize("name,cfg,n_layers,vocab,ctx_len,kv_f16", LONG_CASES, ids=[c[0] for c in LONG_CASES])
+def test_long_cached_context(ggc, orc, ctx, name, cfg, n_layers, vocab, ctx_len, kv_f16):
+    hp, m, o = model_pair(ggc, orc, ctx, cfg, n_layers=n_layers, vocab=vocab, max_ctx=ctx_len + 8, seed=21,
+                          kv_f16=kv_f16)
+    kvd = m.kv_dim
+    rng = np.random.default_rng(2)
+    for l in range(hp["n_layers"]):
+        k = rng.normal(size=(ctx_len, kvd)).astype(np.float32)
+        v = rng.normal(size=(ctx_len, kvd)).astype(np.float32)
+        m.cache_append(l, k, v)
+        o.cache_append(l, k, v)
+    kk, vv = m.cache_read(hp["n_layers"] - 1)
+    if kv_f16:
+        assert np.array_equal(kk, k.astype(np.float16).astype(np.float32).reshape(-1))
+    else:
+        assert np.array_equal(kk, k.reshape(-1)) and np.array_equal(vv, v.reshape(-1))
+    got = m.forward([7], [ctx_len])
+    want = o.forward([7], [ctx_len])
+    assert np.all(np.isfinite(got))
+    assert rel_l2(got, want) <= (1e-2 if kv_f16 else REL_L2), rel_l2(got, want)
+    if not kv_f16:   # the device loop past the planted context
+        assert m.generate_greedy([11], 4, start_pos=ctx_len + 1) == o.generate_greedy([11], 4, start_pos=ctx_len + 1)
+        assert m.cache_len() == o.cache_len() == ctx_len + 6
+
+
 def test_positions_mask_by_absolute_position(ggc, orc, ctx):   # llama.rs:523-529
     """Re-running positions 0.. on a filled cache masks later cache rows (s > pos)."""
     hp, m, o = model_pair(ggc, orc, ctx, MINI, seed=8)
