@@ -3,8 +3,9 @@
 
 Metric: decode tokens/s of a Llama-2-7B-shaped model in the Q4_K_M mix (Q4_K,
 Q6_K for the output head and attn_v / ffn_down of even layers, f32 norms), batch
-1, at context 2048 (the KV cache is prefilled so the K timed steps end at 2048),
-f32 KV cache as the reference keeps it.  Weights are seeded synthetic blocks.
+1, at context 2048 (the KV cache is prefilled with planted K/V rows so the K
+timed steps end at 2048), f32 KV cache as the reference keeps it.  Weights are
+seeded synthetic blocks.
 
 One step = one token through all 32 layers (greedy sample -> forward), run by the
 device-side decode loop (one CUDA graph per token).  `value` is timed with CUDA
@@ -45,6 +46,7 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ctx", type=int, default=2048)
+    ap.add_argument("--layers", type=int, default=None, help="fewer layers (small profiling cases only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -172,8 +174,9 @@ def run_reference(args, rank, world):
 
 
 def config_block(args):
-    return {"workload": f"{MODEL} decode, batch 1, context {args.ctx} (cache prefilled so the timed steps end at "
-                        f"{args.ctx}), f32 KV cache", "global_batch": 1, "seq_len": args.ctx,
+    layers = "" if args.layers is None else f", first {args.layers} layers only (profiling case)"
+    return {"workload": f"{MODEL} decode, batch 1, context {args.ctx} (cache prefilled with planted K/V rows so the "
+                        f"timed steps end at {args.ctx}), f32 KV cache{layers}", "global_batch": 1, "seq_len": args.ctx,
             "parallelism": f"replicas x{args.gpus}", "l2": "per-step traffic ~6 GB >> 126 MB L2 (no flush needed)"}
 
 
@@ -230,14 +233,18 @@ def run_ours(args, rank, world, local_rank):
     stream = torch.cuda.ExternalStream(ctx.stream)
     peak_gbs, peak_src = peaks()
 
-    hp, ts = synth.make_model(MODEL, seed=0)
+    hp, ts = synth.make_model(MODEL, seed=0, n_layers=args.layers)
     W, K, C = args.warmup, args.steps, args.ctx
     P = C - W - K
     assert P >= 1, "context too small for warmup + steps"
     model = ggc.LlamaModel(hp, ts, max_ctx=C, ctx=ctx)
     w_bytes = synth.weight_bytes_per_token(ts)
-    prompt = np.random.default_rng(1).integers(0, hp["vocab_size"], size=P).astype(np.uint32)
-    model.forward(prompt, np.arange(P, dtype=np.int64), want_logits=False)
+    # prefill: P seeded K/V rows planted in every layer (a decode step's cost does
+    # not depend on the cached values)
+    rng = np.random.default_rng(1)
+    for l in range(hp["n_layers"]):
+        kv = rng.normal(size=(P, model.kv_dim)).astype(np.float32)
+        model.cache_append(l, kv, kv)
 
     def barrier():
         if dist is not None:

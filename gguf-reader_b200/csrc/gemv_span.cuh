@@ -1,0 +1,575 @@
+// gemv_span.cuh -- decode GEMV y = W x for the integer formats (Q4_K, Q6_K,
+// Q4_0, Q8_0) over the span layout (planes.cuh).
+//
+// Work split.  One CTA per SM over a contiguous range of 16-row blocks; a
+// producer warp streams tiles (16 rows x 4096 columns, every plane: one bulk copy
+// per plane) into a ring of shared-memory stages, column tile by column tile.  8
+// consumer warps each own an adjacent row pair of every tile (RoPE pairs stay in
+// one warp); lane l owns the 128-element span l of the column tile, so a row is
+// one pass of 32 lanes over their spans and one warp reduction.
+//
+// x arithmetic.  Before the first tile the CTA turns x (plain, RMS-normalised or
+// silu(gate) * up) into, per span, a 22-bit fixed-point integer with one
+// power-of-two scale gs (|x| / gs < 2^22: exact scaling), split into three 8-bit
+// limbs (two unsigned, the top one signed), stored per (column tile, word, lane)
+// in shared memory.  A lane loads the 96 limb words of its span into registers
+// once per column tile.  One dp4a multiplies four weight codes by four limbs in
+// int32; per-sub-block scales (6-bit / int8) fold into the int32 limb sums; the
+// three limb sums recombine in f32 once per row and lane.  High nibbles are used
+// as 16 * q (mask, no shift), the factor 16 folded into the scale.  The relative
+// error of a row is ~2^-22 * max|x| / rms|x| (f32 reference: ~1e-6).
+//
+// Every wait is bounded (ERRF_TIMEOUT); the first stages are issued before
+// griddepcontrol.wait, so the weights stream while the predecessor finishes.
+#pragma once
+#include "common.cuh"
+#include "planes.cuh"
+#include "mbarrier.cuh"
+#include "gemv.cuh"
+
+namespace ggc {
+
+constexpr int GS_WARPS = 8;
+constexpr int GS_THREADS = GS_WARPS * 32 + 32;
+constexpr int GS_MAX_STAGES = 4;
+constexpr int GS_WORDS = 96;    // limb words per span: 32 steps x 3 limbs
+constexpr int GS_XF = 9;        // floats per span: gs, then the sums of x over its eight 16-element quarters
+
+// ---- per-format span decoders --------------------------------------------
+// step s (0..31) of a span multiplies four weight codes by x elements
+// elem(s, 0..3) of the span; quarter q (0..7) holds the steps of span elements
+// [16q, 16q + 16): step_of(q, t), t = 0..3, whose element j is 16q + qoff(t, j).
+template <int DT> struct SpanFmt;
+
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(smem_addr(p)));
+    return v;
+}
+__device__ __forceinline__ uint2 lds64(const uint8_t* p) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(smem_addr(p)));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds32(const uint8_t* p) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_addr(p)));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds16(const uint8_t* p) {
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(smem_addr(p)));
+    return v;
+}
+__device__ __forceinline__ uint32_t wsel(const uint4& u, int i) { return i == 0 ? u.x : i == 1 ? u.y : i == 2 ? u.z : u.w; }
+__device__ __forceinline__ float comb3(int t0, int t1, int t2) {
+    return fmaf(65536.f, (float)t2, fmaf(256.f, (float)t1, (float)t0));
+}
+
+// Plane rows of one tile row (shared memory) and the lane count of the tile.
+struct SpanRow {
+    const uint8_t* p[4];
+    int nl;
+};
+
+// Q4_K: span = half n of a block; qs unit k = bytes 64n + 16k .. +16; byte i of
+// a 32-byte segment j: low nibble -> element 64j + i (sub-block 2j), high ->
+// 64j + 32 + i (quant.rs:262-283).  Local sub-blocks 0..3 of the span.
+template <> struct SpanFmt<GGC_Q4_K> {
+    __device__ static constexpr int elem(int s, int j) {
+        const int w = s >> 1, hi = s & 1, k = w >> 2, i = w & 3;
+        return 64 * (k >> 1) + 32 * hi + 16 * (k & 1) + 4 * i + j;
+    }
+    __device__ static constexpr int step_of(int q, int t) {   // quarter q: sub-block q/2, half q%2
+        const int g = q >> 1, k = 2 * (g >> 1) + (q & 1), hi = g & 1;
+        return 2 * (4 * k + t) + hi;
+    }
+    __device__ static constexpr int qoff(int t, int j) { return 4 * t + j; }   // elem(step_of(q, t), j) - 16 q
+    __device__ static float dot(const SpanRow& R, int lane, const uint32_t* L, const float* xf) {
+        uint4 u[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) u[k] = lds128(R.p[0] + (k * R.nl + lane) * 16);
+        const uint32_t dd = lds32(R.p[1] + (lane >> 1) * 4);
+        const uint2 scm = lds64(R.p[2] + lane * 8);
+        Acc3 A[4];
+#pragma unroll
+        for (int w = 0; w < 16; ++w) {
+            const uint32_t q = wsel(u[w >> 2], w & 3);
+            const int sb = 2 * ((w >> 2) >> 1);
+            dp3u(q & 0x0F0F0F0Fu, L + 6 * w, A[sb]);
+            dp3u(q & 0xF0F0F0F0u, L + 6 * w + 3, A[sb + 1]);   // 16 q
+        }
+        // 16 * sum_q sc_q (codes . x_int): low sub-blocks take 16 sc, high ones sc
+        int T0 = 0, T1 = 0, T2 = 0;
+#pragma unroll
+        for (int sb = 0; sb < 4; ++sb) {
+            const int c = (int)((scm.x >> (8 * sb)) & 0xFFu) << ((sb & 1) ? 0 : 4);
+            T0 += c * A[sb].a0; T1 += c * A[sb].a1; T2 += c * A[sb].a2;
+        }
+        float mn = 0.f;
+#pragma unroll
+        for (int sb = 0; sb < 4; ++sb) mn = fmaf((float)((scm.y >> (8 * sb)) & 0xFFu), xf[GS_XF + sb], mn);
+        const float2 dm = h2f2(dd);
+        // value = d sc q - dmin mn  (quant.rs:275-279)
+        return fmaf(dm.x * (xf[0] * 0.0625f), comb3(T0, T1, T2), -dm.y * mn);
+    }
+};
+
+// Q6_K: span = half n of a block: ql[64n ..] (4 units), qh[32n ..] (2 units),
+// scales[8n ..], d.  For l < 32: q1 = ql[l] lo | qh[l] bits 0-1 (element l), q2 =
+// ql[32 + l] lo | bits 2-3 (32 + l), q3 = ql[l] hi | bits 4-5 (64 + l), q4 =
+// ql[32 + l] hi | bits 6-7 (96 + l); element e uses scale e / 16 (quant.rs:312-336).
+template <> struct SpanFmt<GGC_Q6_K> {
+    __device__ static constexpr int elem(int s, int j) {
+        const int w = s >> 1, hi = s & 1, l0 = 4 * w;
+        return l0 < 32 ? (hi ? 64 : 0) + l0 + j : (hi ? 96 : 32) + (l0 - 32) + j;
+    }
+    __device__ static constexpr int step_of(int q, int t) {   // 16-element group q
+        const int part = q >> 1, l = 16 * (q & 1) + 4 * t;
+        const int l0 = (part & 1) ? 32 + l : l, hi = part >> 1;
+        return 2 * (l0 >> 2) + hi;
+    }
+    __device__ static constexpr int qoff(int t, int j) { return 4 * t + j; }
+    __device__ static float dot(const SpanRow& R, int lane, const uint32_t* L, const float* xf) {
+        uint4 u[4], h[2];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) u[k] = lds128(R.p[0] + (k * R.nl + lane) * 16);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) h[k] = lds128(R.p[1] + (k * R.nl + lane) * 16);
+        const uint2 sc = lds64(R.p[2] + lane * 8);
+        const uint32_t d16 = lds16(R.p[3] + (lane >> 1) * 2);
+        Acc3 A[8];
+#pragma unroll
+        for (int w = 0; w < 16; ++w) {
+            const uint32_t q = wsel(u[w >> 2], w & 3);
+            const int v = w & 7;
+            const uint32_t hb = wsel(h[v >> 2], v & 3);
+            uint32_t lo, hi;
+            int glo, ghi;
+            if (w < 8) {
+                lo = (q & 0x0F0F0F0Fu) | ((hb << 4) & 0x30303030u);
+                hi = ((q >> 4) & 0x0F0F0F0Fu) | (hb & 0x30303030u);
+                glo = w >> 2; ghi = 4 + (w >> 2);
+            } else {
+                lo = (q & 0x0F0F0F0Fu) | ((hb << 2) & 0x30303030u);
+                hi = ((q >> 4) & 0x0F0F0F0Fu) | ((hb >> 2) & 0x30303030u);
+                glo = 2 + ((w - 8) >> 2); ghi = 6 + ((w - 8) >> 2);
+            }
+            dp3u(lo, L + 6 * w, A[glo]);
+            dp3u(hi, L + 6 * w + 3, A[ghi]);
+        }
+        // value = d sc (u - 32): sum_g sc_g (u . x_int) - 32 sum_g sc_g X_g
+        int T0 = 0, T1 = 0, T2 = 0;
+        float off = 0.f;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+            const int c = (int)(int8_t)(((g < 4 ? sc.x : sc.y) >> (8 * (g & 3))) & 0xFFu);
+            T0 += c * A[g].a0; T1 += c * A[g].a1; T2 += c * A[g].a2;
+            off = fmaf((float)c, xf[1 + g], off);
+        }
+        const float d = h2f(d16);
+        return d * fmaf(xf[0], comb3(T0, T1, T2), -32.f * off);
+    }
+};
+
+// Q4_0 (the reference's interleaved nibbles: byte m of qs holds element 2m in
+// its low and 2m + 1 in its high nibble, quant.rs:139-150): span = 4 blocks.
+template <> struct SpanFmt<GGC_Q4_0> {
+    __device__ static constexpr int elem(int s, int j) {
+        const int k = s >> 3, i = (s >> 1) & 3, hi = s & 1;
+        return 32 * k + 8 * i + 2 * j + hi;
+    }
+    __device__ static constexpr int step_of(int q, int t) {   // elements 16q .. +16: block q/2, words 2(q%2) + t/2
+        return 8 * (q >> 1) + 2 * (2 * (q & 1) + (t >> 1)) + (t & 1);
+    }
+    __device__ static constexpr int qoff(int t, int j) { return 8 * (t >> 1) + 2 * j + (t & 1); }
+    __device__ static float dot(const SpanRow& R, int lane, const uint32_t* L, const float* xf) {
+        uint4 u[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) u[k] = lds128(R.p[0] + (k * R.nl + lane) * 16);
+        const uint2 dd = lds64(R.p[1] + lane * 8);
+        float r = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            Acc3 lo, hi;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t q = wsel(u[k], i);
+                dp3u(q & 0x0F0F0F0Fu, L + 3 * (8 * k + 2 * i), lo);
+                dp3u(q & 0xF0F0F0F0u, L + 3 * (8 * k + 2 * i + 1), hi);   // 16 q
+            }
+            const float s16 = comb3(16 * lo.a0 + hi.a0, 16 * lo.a1 + hi.a1, 16 * lo.a2 + hi.a2);
+            const float d = h2f(((k < 2 ? dd.x : dd.y) >> (16 * (k & 1))) & 0xFFFFu);
+            // value = d (q - 8)  (quant.rs:139-150)
+            r = fmaf(d, fmaf(xf[0] * 0.0625f, s16, -8.f * xf[GS_XF + k]), r);
+        }
+        return r;
+    }
+};
+
+// Q8_0: span = 4 blocks of 32 int8; unit k = bytes 16 (k % 2) .. of block k / 2.
+template <> struct SpanFmt<GGC_Q8_0> {
+    __device__ static constexpr int elem(int s, int j) {
+        const int k = s >> 2, i = s & 3;
+        return 32 * (k >> 1) + 16 * (k & 1) + 4 * i + j;
+    }
+    __device__ static constexpr int step_of(int q, int t) { return 4 * q + t; }
+    __device__ static constexpr int qoff(int t, int j) { return 4 * t + j; }
+    __device__ static float dot(const SpanRow& R, int lane, const uint32_t* L, const float* xf) {
+        uint4 u[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) u[k] = lds128(R.p[0] + (k * R.nl + lane) * 16);
+        const uint2 dd = lds64(R.p[1] + lane * 8);
+        float r = 0.f;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            Acc3 A;
+#pragma unroll
+            for (int k = 2 * b; k < 2 * b + 2; ++k)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) dp3s(wsel(u[k], i), L + 3 * (4 * k + i), A);
+            const float d = h2f(((b < 2 ? dd.x : dd.y) >> (16 * (b & 1))) & 0xFFFFu);
+            r = fmaf(d, comb(A), r);   // value = d q  (quant.rs:173-180)
+        }
+        return r * xf[0];
+    }
+};
+
+// ---- launch geometry (host) ------------------------------------------------
+struct SpanCfg {
+    uint32_t poff[4];       // plane offsets inside a stage
+    uint32_t stage_bytes, stages;
+    uint32_t xl_bytes;      // limb words + per-span floats of every column tile
+    uint32_t part_rows;     // partial row sums kept per CTA (multi-tile rows)
+    uint32_t smem;          // dynamic shared memory
+};
+
+template <int DT>
+SpanCfg make_span_cfg(uint32_t pcols, uint32_t total_rb, uint32_t ctas, size_t smem_limit) {
+    const TileLayout L = make_layout(DT, TILE_ROWS, pcols);
+    const SpanSpec sp = span_spec(DT);
+    SpanCfg c{};
+    uint32_t off = 0;
+    for (int p = 0; p < 4; ++p) {
+        c.poff[p] = off;
+        off += p < sp.n ? (TILE_ROWS * L.tp_full[p] + 127u) / 128u * 128u : 0u;
+    }
+    c.stage_bytes = off;
+    const uint32_t nsp_full = L.nct * SPAN_LANES;
+    c.xl_bytes = (nsp_full * (GS_WORDS + GS_XF) * 4u + 127u) / 128u * 128u;
+    c.part_rows = L.nct > 1 ? ((total_rb + ctas - 1) / ctas) * TILE_ROWS : 0u;
+    const size_t fixed = (size_t)c.xl_bytes + c.part_rows * 4u + 128;
+    const size_t st = smem_limit > fixed ? (smem_limit - fixed) / c.stage_bytes : 0;
+    c.stages = (uint32_t)(st > (size_t)GS_MAX_STAGES ? GS_MAX_STAGES : st);
+    c.smem = (uint32_t)(fixed + (size_t)c.stages * c.stage_bytes);
+    return c;
+}
+
+// ---- the kernel ------------------------------------------------------------
+template <int DT>
+__global__ void __launch_bounds__(GS_THREADS, 1) k_gemv_span(const GemvArgs a, const SpanCfg cfg) {
+    using F = SpanFmt<DT>;
+    constexpr SpanSpec SP = span_spec(DT);
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ Seg sseg[3];
+    __shared__ double red[GS_WARPS];
+    __shared__ float s_scale;
+    __shared__ unsigned long long s_best[GS_WARPS];
+    __shared__ int s_nan;
+
+    uint32_t* xl = reinterpret_cast<uint32_t*>(smem);                                // [ct][24][lane][4]
+    const uint32_t nct = a.seg[0].m.L.nct;
+    float* xfs = reinterpret_cast<float*>(smem + (size_t)nct * SPAN_LANES * GS_WORDS * 4);   // [ct][9][lane]
+    float* part = reinterpret_cast<float*>(smem + cfg.xl_bytes);                      // [part_rows]
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + cfg.xl_bytes + cfg.part_rows * 4u);
+    uint64_t* empty = full + GS_MAX_STAGES;
+    uint8_t* stages = reinterpret_cast<uint8_t*>(full) + 128;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid < a.nseg) sseg[tid] = a.seg[tid];
+    if (tid == 0) {
+        for (uint32_t s = 0; s < cfg.stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], GS_WARPS);
+        }
+        s_nan = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (tid < GS_WARPS) s_best[tid] = 0ull;
+    __syncthreads();
+    pdl_trigger();
+
+    // contiguous range of row blocks (over all segments); tiles column-tile-major
+    uint32_t total_rb = 0;
+    for (int i = 0; i < a.nseg; ++i) total_rb += sseg[i].m.L.nrb;
+    const uint32_t rb0 = (uint32_t)((uint64_t)total_rb * blockIdx.x / gridDim.x);
+    const uint32_t rb1 = (uint32_t)((uint64_t)total_rb * (blockIdx.x + 1) / gridDim.x);
+    const uint32_t nrb = rb1 - rb0, ntiles = nrb * nct;
+    auto locate = [&](uint32_t g, int& si, uint32_t& rb) {
+        si = 0;
+        rb = g;
+        while (si + 1 < a.nseg && rb >= sseg[si].m.L.nrb) { rb -= sseg[si].m.L.nrb; ++si; }
+    };
+    auto skip = [&]() { return (a.st_done && *a.st_done) || (a.st_skip && a.st_skip[0] < a.st_skip[1]); };
+
+    if (warp == GS_WARPS) {
+        // ---------------- producer warp ----------------
+        const uint32_t prefetch = ntiles < cfg.stages ? ntiles : cfg.stages;
+        bool waited = false;
+        uint32_t s = 0, ph = 1, rbl = 0, ct = 0, rb = 0;   // empty[s] phase: the first round needs no wait
+        int si = 0;
+        locate(rb0, si, rb);
+        for (uint32_t i = 0; i < ntiles; ++i) {
+            if (i == prefetch) {
+                pdl_wait();
+                waited = true;
+                if (skip()) break;
+            }
+            if (i >= cfg.stages && !mbar_wait(&empty[s], ph, a.errf)) break;
+            if (lane == 0) {
+                const QMat& m = sseg[si].m;
+                uint32_t bytes = 0;
+#pragma unroll
+                for (int p = 0; p < SP.n; ++p) bytes += TILE_ROWS * tile_pitch(m.L, p, ct);
+                mbar_arrive_expect_tx(&full[s], bytes);
+                uint8_t* st = stages + (size_t)s * cfg.stage_bytes;
+#pragma unroll
+                for (int p = 0; p < SP.n; ++p)
+                    bulk_g2s(st + cfg.poff[p], m.p[p] + tile_offset(m.L, p, rb, ct), TILE_ROWS * tile_pitch(m.L, p, ct),
+                             &full[s]);
+            }
+            __syncwarp();
+            if (++s == cfg.stages) { s = 0; ph ^= 1u; }
+            if (++rbl == nrb) {
+                rbl = 0;
+                ++ct;
+                locate(rb0, si, rb);
+            } else if (++rb == sseg[si].m.L.nrb) {
+                rb = 0;
+                ++si;
+            }
+        }
+        if (!waited) pdl_wait();
+        return;
+    }
+
+    // ---------------- consumer warps ----------------
+    pdl_wait();
+    if (skip()) {   // drain the copies issued before the flag was seen
+        const uint32_t n = ntiles < cfg.stages ? ntiles : cfg.stages;
+        for (uint32_t i = 0; i < n; ++i) mbar_wait(&full[i], 0, a.errf);
+        return;
+    }
+    constexpr uint32_t CT = GS_WARPS * 32;
+    auto cbar = [] { asm volatile("bar.sync 1, %0;" ::"r"(CT) : "memory"); };
+    float scale = 0.f;
+    if (a.pro == PRO_RMSNORM) {
+        double ss = 0.0;
+        if ((a.xcols & 3) == 0) {
+            const float4* x4 = reinterpret_cast<const float4*>(a.x);
+            for (uint32_t i = tid; i < a.xcols / 4; i += CT) {
+                const float4 v = x4[i];
+                ss += (double)v.x * (double)v.x + (double)v.y * (double)v.y + (double)v.z * (double)v.z +
+                      (double)v.w * (double)v.w;
+            }
+        } else {
+            for (uint32_t i = tid; i < a.xcols; i += CT) { const double v = (double)a.x[i]; ss += v * v; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) red[warp] = ss;
+        cbar();
+        if (tid == 0) {
+            double t = 0.0;
+            for (int w = 0; w < GS_WARPS; ++w) t += red[w];
+            s_scale = (float)sqrt(1.0 / (t / (double)a.xcols + (double)1e-6f));   // ops.rs:262-274
+        }
+        cbar();
+        scale = s_scale;
+    }
+    // x -> limbs: 8 threads per span (one quarter of 16 elements each)
+    {
+        const uint32_t nsp = nct * SPAN_LANES, items = nsp * 8;
+        for (uint32_t base = 0; base < items; base += CT) {
+            const uint32_t it = base + tid;
+            const uint32_t sp = it >> 3, q = it & 7;
+            const bool live = it < items;
+            float v[16];
+            const uint32_t e0 = sp * SPAN + 16 * q;
+#pragma unroll
+            for (int k = 0; k < 16; ++k) v[k] = 0.f;
+            if (live && e0 + 16 <= a.xcols) {
+                const float4* x4 = reinterpret_cast<const float4*>(a.x + e0);
+                float4 xa[4], ya[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) xa[k] = x4[k];
+                if (a.pro != PRO_PLAIN) {
+                    const float4* y4 = reinterpret_cast<const float4*>(a.x2 + e0);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) ya[k] = y4[k];
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float xx[4] = {xa[k].x, xa[k].y, xa[k].z, xa[k].w};
+                    const float yy[4] = {ya[k].x, ya[k].y, ya[k].z, ya[k].w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        float r = xx[j];
+                        if (a.pro == PRO_RMSNORM) {
+                            r = __fmul_rn(__fmul_rn(xx[j], scale), yy[j]);   // ops.rs:272
+                        } else if (a.pro == PRO_SWIGLU) {                 // ops.rs:237-247, llama.rs:564-567
+                            const float gg = xx[j];
+                            float sig;
+                            if (gg >= 0.0f) sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gg)));
+                            else { const float ex = expf(gg); sig = __fdiv_rn(ex, __fadd_rn(1.0f, ex)); }
+                            r = __fmul_rn(__fmul_rn(gg, sig), yy[j]);
+                        }
+                        v[4 * k + j] = r;
+                    }
+                }
+            } else if (live) {
+#pragma unroll
+                for (int k = 0; k < 16; ++k)
+                    if (e0 + k < a.xcols) v[k] = gemv_xval(a, e0 + k, scale);
+            }
+            float mx = 0.f, sum = 0.f;
+#pragma unroll
+            for (int k = 0; k < 16; ++k) { mx = fmaxf(mx, fabsf(v[k])); sum += v[k]; }
+            bool finite = isfinite(mx) && isfinite(sum);
+            // the 8 quarters of a span are 8 consecutive threads of one warp
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) {
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                finite = __shfl_xor_sync(0xffffffffu, (int)finite, o) && finite;
+            }
+            int ex = 0;
+            frexpf(mx, &ex);
+            const float mul = (mx > 0.f && finite) ? ldexpf(1.f, 22 - ex) : 0.f;
+            const float gs = !finite ? __int_as_float(0x7FC00000) : (mx > 0.f ? ldexpf(1.f, ex - 22) : 0.f);
+            if (live) {
+                const uint32_t ct = sp / SPAN_LANES, l = sp % SPAN_LANES;
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const int s = F::step_of((int)q, t);
+                    uint32_t w0 = 0, w1 = 0, w2 = 0;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int xi = __float2int_rn(v[F::qoff(t, j)] * mul);
+                        w0 |= (uint32_t)(xi & 0xFF) << (8 * j);
+                        w1 |= (uint32_t)((xi >> 8) & 0xFF) << (8 * j);
+                        w2 |= (uint32_t)((xi >> 16) & 0xFF) << (8 * j);
+                    }
+                    const uint32_t wi[3] = {(uint32_t)(3 * s), (uint32_t)(3 * s + 1), (uint32_t)(3 * s + 2)};
+                    const uint32_t wv[3] = {w0, w1, w2};
+#pragma unroll
+                    for (int k = 0; k < 3; ++k)
+                        xl[(((size_t)ct * 24 + wi[k] / 4) * SPAN_LANES + l) * 4 + wi[k] % 4] = wv[k];
+                }
+                xfs[((size_t)ct * GS_XF + 1 + q) * SPAN_LANES + l] = sum;
+                if (q == 0) xfs[((size_t)ct * GS_XF) * SPAN_LANES + l] = gs;
+            }
+        }
+    }
+    for (uint32_t i = tid; i < cfg.part_rows; i += CT) part[i] = 0.f;
+    cbar();
+
+    const int r0 = 2 * warp;   // this warp's row pair in every tile
+    uint32_t L[GS_WORDS];
+    float xf[GS_XF + 4];        // gs, the eight quarter sums, the four 32-element sums
+    unsigned long long best = 0ull;
+    bool nan_logit = false;
+    // tile i = (column tile ct, row block rb0 + rbl); counters advance instead of dividing
+    uint32_t s = 0, ph = 0, rbl = 0, ct = 0, rb = 0;
+    int si = 0;
+    locate(rb0, si, rb);
+    int nl = 0;
+    uint32_t rowoff[2][4];
+    for (uint32_t i = 0; i < ntiles; ++i) {
+        if (!mbar_wait(&full[s], ph, a.errf)) return;
+        if (rbl == 0) {   // a new column tile: x of this lane's span into registers, tile geometry
+            const TileLayout& L0 = sseg[0].m.L;
+            nl = ct + 1 == L0.nct ? (int)((L0.pcols - ct * SPAN_KC) / SPAN) : SPAN_LANES;
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+                const uint32_t pitch = tile_pitch(L0, p, ct);
+                rowoff[0][p] = cfg.poff[p] + (uint32_t)r0 * pitch;
+                rowoff[1][p] = rowoff[0][p] + pitch;
+            }
+#pragma unroll
+            for (int k = 0; k < GS_WORDS / 4; ++k) {
+                const uint4 w4 = *reinterpret_cast<const uint4*>(xl + (((size_t)ct * 24 + k) * SPAN_LANES + lane) * 4);
+                L[4 * k] = w4.x; L[4 * k + 1] = w4.y; L[4 * k + 2] = w4.z; L[4 * k + 3] = w4.w;
+            }
+#pragma unroll
+            for (int k = 0; k < GS_XF; ++k) xf[k] = xfs[((size_t)ct * GS_XF + k) * SPAN_LANES + lane];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) xf[GS_XF + k] = xf[1 + 2 * k] + xf[2 + 2 * k];
+        }
+        const uint8_t* st = stages + (size_t)s * cfg.stage_bytes;
+        float y[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            SpanRow R;
+#pragma unroll
+            for (int p = 0; p < 4; ++p) R.p[p] = st + rowoff[k][p];
+            R.nl = nl;
+            y[k] = lane < nl ? F::dot(R, lane, L, xf) : 0.f;
+        }
+        // two row sums: halve the exchange (lanes < 16 keep row 0), then reduce
+        {
+            const bool up = lane & 16;
+            const float send = up ? y[0] : y[1];
+            float v = (up ? y[1] : y[0]) + __shfl_xor_sync(0xffffffffu, send, 16);
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            y[0] = __shfl_sync(0xffffffffu, v, 0);
+            y[1] = __shfl_sync(0xffffffffu, v, 16);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        // this tile's (segment, row block, column tile); then advance the counters
+        const int tsi = si;
+        const uint32_t trb = rb, trbl = rbl, tct = ct;
+        if (++s == cfg.stages) { s = 0; ph ^= 1u; }
+        if (++rbl == nrb) {
+            rbl = 0;
+            ++ct;
+            locate(rb0, si, rb);
+        } else if (++rb == sseg[si].m.L.nrb) {
+            rb = 0;
+            ++si;
+        }
+        const uint32_t nrows = min((uint32_t)TILE_ROWS, sseg[tsi].m.L.rows - trb * TILE_ROWS);
+        if ((uint32_t)r0 >= nrows) continue;
+        const uint32_t nv = min(2u, nrows - (uint32_t)r0);
+        if (nct > 1) {
+            float* pp = part + trbl * TILE_ROWS + r0;
+            if (tct + 1 < nct) {
+                if (lane == 0) { pp[0] += y[0]; pp[1] += y[1]; }
+                continue;
+            }
+            y[0] += pp[0];
+            y[1] += pp[1];
+        }
+        if (lane == 0) {
+            const Seg& sg = sseg[tsi];
+            const uint32_t row = trb * TILE_ROWS + (uint32_t)r0;
+            if (sg.epi == EPI_LOGITS) {   // logits + running argmax (one atomic per warp at the end)
+                for (uint32_t k = 0; k < nv; ++k) {
+                    sg.out[row + k] = y[k];
+                    nan_logit |= isnan(y[k]);
+                    const unsigned long long key = argmax_key_of(y[k], row + k);
+                    best = key > best ? key : best;
+                }
+            } else {
+                gemv_epilogue(a, sg, row, nv, y);
+            }
+        }
+    }
+    if (lane == 0 && (best || nan_logit)) {
+        if (nan_logit) atomicMax(&a.errf[ERRF_NAN_LOGITS], 1);
+        atomicMax(a.argmax_key, best);
+    }
+}
+
+}  // namespace ggc

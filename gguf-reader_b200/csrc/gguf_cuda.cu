@@ -21,6 +21,7 @@
 #include "dequant.cuh"
 #include "planes.cuh"
 #include "gemv.cuh"
+#include "gemv_span.cuh"
 #include "attention.cuh"
 #include "noalloc.cuh"
 
@@ -498,7 +499,9 @@ int upload_mat(ggc_ctx* ctx, const void* raw, uint64_t raw_bytes, int dt, uint64
     if (cols % (uint64_t)bs != 0) return set_shape_error(cols, bs, "matrix columns");
     const uint64_t E = (uint64_t)chunk_elems(dt);
     uint64_t pcols = cols;
-    if (cols % E != 0) {
+    if (is_span_dt(dt)) {
+        pcols = (cols + SPAN - 1) / SPAN * SPAN;   // zero-padded spans
+    } else if (cols % E != 0) {
         if (bs != 1) return set_shape_error(cols, E, "matrix columns (chunk)");
         pcols = (cols + E - 1) / E * E;
     }
@@ -507,6 +510,7 @@ int upload_mat(ggc_ctx* ctx, const void* raw, uint64_t raw_bytes, int dt, uint64
     if (rows == 0 || rows > 0xFFFFFFFFull || pcols > 0xFFFFFFFFull) return set_error(GGC_ERR_INVALID_ARG, "matrix shape");
     const TileLayout L = make_layout(dt, (uint32_t)rows, (uint32_t)pcols);
     uint64_t off[4] = {0, 0, 0, 0}, total = 0;
+    if (is_span_dt(dt)) ps.n = span_spec(dt).n;
     for (int p = 0; p < ps.n; ++p) {
         off[p] = total;
         total += ((uint64_t)L.nrb * L.rb_bytes[p] + 255) / 256 * 256;
@@ -539,8 +543,12 @@ constexpr size_t GEMV_SMEM_LIMIT = 227 * 1024 - 4096;   // dynamic shared bytes 
 template <int DT>
 struct SetGemvSmem {
     static void run(int* ok) {
-        if (cudaFuncSetAttribute(k_gemv<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMV_SMEM_LIMIT) != cudaSuccess)
-            *ok = 0;
+        cudaError_t e;
+        if constexpr (is_span_dt(DT))
+            e = cudaFuncSetAttribute(k_gemv_span<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMV_SMEM_LIMIT);
+        else
+            e = cudaFuncSetAttribute(k_gemv<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMV_SMEM_LIMIT);
+        if (e != cudaSuccess) *ok = 0;
     }
 };
 
@@ -619,11 +627,17 @@ struct RunGemv {
     static void run(ggc_ctx* ctx, const GemvArgs* a, cudaError_t* err) {
         uint32_t total_rb = 0;
         for (int i = 0; i < a->nseg; ++i) total_rb += a->seg[i].m.L.nrb;
-        const TileCfg tc = make_tile_cfg<DT>(a->cols, GEMV_SMEM_LIMIT);
-        if (tc.stages < 2) { *err = cudaErrorInvalidConfiguration; return; }
         uint32_t ctas = total_rb < (uint32_t)ctx->num_sms ? total_rb : (uint32_t)ctx->num_sms;
         if (ctas == 0) ctas = 1;
-        *err = launch(ctx, k_gemv<DT>, dim3(ctas), dim3(GEMV_THREADS), gemv_smem_bytes(tc), *a, tc);
+        if constexpr (is_span_dt(DT)) {
+            const SpanCfg c = make_span_cfg<DT>(a->cols, total_rb, ctas, GEMV_SMEM_LIMIT);
+            if (c.stages < 2) { *err = cudaErrorInvalidConfiguration; return; }
+            *err = launch(ctx, k_gemv_span<DT>, dim3(ctas), dim3(GS_THREADS), c.smem, *a, c);
+        } else {
+            const TileCfg tc = make_tile_cfg<DT>(a->cols, GEMV_SMEM_LIMIT);
+            if (tc.stages < 2) { *err = cudaErrorInvalidConfiguration; return; }
+            *err = launch(ctx, k_gemv<DT>, dim3(ctas), dim3(GEMV_THREADS), gemv_smem_bytes(tc), *a, tc);
+        }
     }
 };
 

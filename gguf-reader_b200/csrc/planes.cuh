@@ -54,6 +54,32 @@ __host__ __device__ constexpr PlaneSpec plane_spec(int dt) {
          : PlaneSpec{0, {0, 0, 0, 0}, 0};
 }
 
+// Span layout (Q4_K, Q6_K, Q4_0, Q8_0: the formats of the integer GEMV).  A
+// column tile is 4096 columns = 32 lanes x one 128-element "span" per lane; the
+// bytes a lane reads for its span of a row are, per plane, either 16-byte units
+// interleaved by lane (unit k of lane l at (k * nl + l) * 16, nl = lanes of the
+// column tile) or a small per-lane record (at l * bps), or a per-block record
+// shared by a lane pair (Q4_K d|dmin, Q6_K d).  Rows are padded with zero bytes
+// to a multiple of 128 columns.
+constexpr int SPAN = 128;
+constexpr int SPAN_LANES = 32;
+constexpr uint32_t SPAN_KC = SPAN * SPAN_LANES;
+
+__host__ __device__ constexpr bool is_span_dt(int dt) {
+    return dt == GGC_Q4_K || dt == GGC_Q6_K || dt == GGC_Q4_0 || dt == GGC_Q8_0;
+}
+struct SpanSpec {
+    int n;          // planes
+    int bps[4];     // bytes per span (per lane) in each plane
+};
+__host__ __device__ constexpr SpanSpec span_spec(int dt) {
+    return dt == GGC_Q4_K ? SpanSpec{3, {64, 2, 8, 0}}     // qs units | d,dmin per block | sc[4] mn[4]
+         : dt == GGC_Q6_K ? SpanSpec{4, {64, 32, 8, 1}}    // ql units | qh units | sc[8] | d per block
+         : dt == GGC_Q4_0 ? SpanSpec{2, {64, 8, 0, 0}}     // qs units (4 blocks) | d[4]
+         : dt == GGC_Q8_0 ? SpanSpec{2, {128, 8, 0, 0}}    // qs units (4 blocks) | d[4]
+         : SpanSpec{0, {0, 0, 0, 0}};
+}
+
 // Geometry of a tiled weight (computed identically on host and device).
 struct TileLayout {
     uint32_t rows, pcols;      // rows, columns padded to the chunk width
@@ -66,6 +92,23 @@ struct TileLayout {
 __host__ __device__ inline uint32_t round16(uint32_t b) { return (b + 15u) / 16u * 16u; }
 
 __host__ __device__ inline TileLayout make_layout(int dt, uint32_t rows, uint32_t pcols) {
+    if (is_span_dt(dt)) {   // pcols: a multiple of SPAN
+        const SpanSpec sp = span_spec(dt);
+        TileLayout L{};
+        L.rows = rows;
+        L.pcols = pcols;
+        L.kc = SPAN_KC;
+        L.nct = (pcols + SPAN_KC - 1) / SPAN_KC;
+        L.nrb = (rows + TILE_ROWS - 1) / TILE_ROWS;
+        const uint32_t nl_last = (pcols - (L.nct - 1) * SPAN_KC) / SPAN;
+        for (int p = 0; p < 4; ++p) {
+            const uint32_t bps = p < sp.n ? (uint32_t)sp.bps[p] : 0u;
+            L.tp_full[p] = round16(bps * SPAN_LANES);
+            L.tp_last[p] = round16(bps * nl_last);
+            L.rb_bytes[p] = (uint64_t)TILE_ROWS * ((uint64_t)(L.nct - 1) * L.tp_full[p] + L.tp_last[p]);
+        }
+        return L;
+    }
     const PlaneSpec s = plane_spec(dt);
     const uint32_t bs = (uint32_t)block_size_of(dt);
     TileLayout L{};
@@ -105,9 +148,9 @@ struct TileView {
     uint32_t pitch[4];
 };
 
-// Host: split `rows` raw GGUF rows into tiled planes.  `row_src[r]` names the raw
-// row that becomes row r (NULL = identity).  planes[p] must hold
-// L.nrb * L.rb_bytes[p] zeroed bytes.
+// Host: split `rows` raw GGUF rows into tiled planes (the span layout for the
+// span formats).  `row_src[r]` names the raw row that becomes row r (NULL =
+// identity).  planes[p] must hold L.nrb * L.rb_bytes[p] zeroed bytes.
 void repack_rows_host(int dt, const uint8_t* raw, uint64_t rows, uint64_t cols, const uint32_t* row_src,
                       const TileLayout& L, uint8_t* const planes[4], int nthreads);
 

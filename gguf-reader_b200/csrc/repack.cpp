@@ -132,6 +132,58 @@ void repack_block(int dt, const uint8_t* b, uint64_t blk, uint8_t* const pl[4]) 
     }
 }
 
+// One 128-element span (lane l of a column tile with nl lanes) of one row into
+// the span layout; row[p] is the plane's row base in the tile.  Blocks past the
+// row's end stay zero.
+void repack_span(int dt, const uint8_t* src, uint64_t nb, uint64_t sp, uint32_t l, uint32_t nl, uint8_t* const row[4]) {
+    auto unit = [&](int p, int k) { return row[p] + ((uint64_t)k * nl + l) * 16; };
+    switch (dt) {
+        case GGC_Q4_K: {   // span = half n of block sp / 2
+            const uint64_t b = sp / 2;
+            const int n = (int)(sp % 2);
+            if (b >= nb) return;
+            const uint8_t* blk = src + b * 144;
+            for (int k = 0; k < 4; ++k) std::memcpy(unit(0, k), blk + 16 + 64 * n + 16 * k, 16);
+            if (n == 0) std::memcpy(row[1] + (l / 2) * 4, blk, 4);
+            uint8_t scm[16];
+            unpack_scale_min(blk + 4, scm);
+            std::memcpy(row[2] + l * 8, scm + 4 * n, 4);
+            std::memcpy(row[2] + l * 8 + 4, scm + 8 + 4 * n, 4);
+            break;
+        }
+        case GGC_Q6_K: {
+            const uint64_t b = sp / 2;
+            const int n = (int)(sp % 2);
+            if (b >= nb) return;
+            const uint8_t* blk = src + b * 210;
+            for (int k = 0; k < 4; ++k) std::memcpy(unit(0, k), blk + 64 * n + 16 * k, 16);
+            for (int k = 0; k < 2; ++k) std::memcpy(unit(1, k), blk + 128 + 32 * n + 16 * k, 16);
+            std::memcpy(row[2] + l * 8, blk + 192 + 8 * n, 8);
+            if (n == 0) std::memcpy(row[3] + (l / 2) * 2, blk + 208, 2);
+            break;
+        }
+        case GGC_Q4_0:
+            for (int k = 0; k < 4; ++k) {
+                const uint64_t b = sp * 4 + k;
+                if (b >= nb) break;
+                std::memcpy(unit(0, k), src + b * 18 + 2, 16);
+                std::memcpy(row[1] + l * 8 + 2 * k, src + b * 18, 2);
+            }
+            break;
+        case GGC_Q8_0:
+            for (int k = 0; k < 4; ++k) {
+                const uint64_t b = sp * 4 + k;
+                if (b >= nb) break;
+                std::memcpy(unit(0, 2 * k), src + b * 34 + 2, 16);
+                std::memcpy(unit(0, 2 * k + 1), src + b * 34 + 18, 16);
+                std::memcpy(row[1] + l * 8 + 2 * k, src + b * 34, 2);
+            }
+            break;
+        default:
+            break;
+    }
+}
+
 }  // namespace
 
 void repack_rows_host(int dt, const uint8_t* raw, uint64_t rows, uint64_t cols, const uint32_t* row_src,
@@ -141,6 +193,23 @@ void repack_rows_host(int dt, const uint8_t* raw, uint64_t rows, uint64_t cols, 
     const uint64_t nb = cols / bs, row_bytes = nb * bb;
     const uint64_t blocks_per_tile = L.kc / bs;
     auto work = [&](uint64_t r0, uint64_t r1) {
+        if (is_span_dt(dt)) {
+            const SpanSpec sp = span_spec(dt);
+            const uint64_t nsp = L.pcols / SPAN;
+            for (uint64_t r = r0; r < r1; ++r) {
+                const uint8_t* src = raw + (uint64_t)(row_src ? row_src[r] : r) * row_bytes;
+                const uint32_t rb = (uint32_t)(r / TILE_ROWS), rl = (uint32_t)(r % TILE_ROWS);
+                for (uint64_t q = 0; q < nsp; ++q) {
+                    const uint32_t ct = (uint32_t)(q / SPAN_LANES), l = (uint32_t)(q % SPAN_LANES);
+                    const uint32_t nl = ct + 1 == L.nct ? (uint32_t)(nsp - (uint64_t)ct * SPAN_LANES) : SPAN_LANES;
+                    uint8_t* row[4] = {nullptr, nullptr, nullptr, nullptr};
+                    for (int p = 0; p < sp.n; ++p)
+                        row[p] = planes[p] + tile_offset(L, p, rb, ct) + (uint64_t)rl * tile_pitch(L, p, ct);
+                    repack_span(dt, src, nb, q, l, nl, row);
+                }
+            }
+            return;
+        }
         for (uint64_t r = r0; r < r1; ++r) {
             const uint8_t* src = raw + (uint64_t)(row_src ? row_src[r] : r) * row_bytes;
             const uint32_t rb = (uint32_t)(r / TILE_ROWS), rl = (uint32_t)(r % TILE_ROWS);
