@@ -68,7 +68,7 @@ __device__ __forceinline__ void attn_range(const AttnArgs& a, uint32_t split, ui
     s1 = min(s0 + chunk, visible);
 }
 
-__global__ void __launch_bounds__(ATTN_WARPS * 32) k_attn_scores(const AttnArgs a) {
+static __global__ void __launch_bounds__(ATTN_WARPS * 32) k_attn_scores(const AttnArgs a) {
     pdl_trigger();
     pdl_wait();
     if (*a.done) return;
@@ -148,7 +148,7 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) k_attn_scores(const AttnArgs 
     if (tid == 0) a.tickets[kvhead] = 0;
 }
 
-__global__ void __launch_bounds__(ATTN_WARPS * 32) k_attn_av(const AttnArgs a) {
+static __global__ void __launch_bounds__(ATTN_WARPS * 32) k_attn_av(const AttnArgs a) {
     pdl_trigger();
     pdl_wait();
     if (*a.done) return;

@@ -585,8 +585,18 @@ enum EpiKind : int {
     EPI_ROPE_KC = 2,    // same, written into the K cache row of this step's slot
     EPI_VC = 3,         // out = acc + bias written into the V cache row
     EPI_RESID = 4,      // out[r] += acc, NaN -> error flag
-    EPI_LOGITS = 5      // out[r] = acc and greedy argmax into a 64-bit key
+    EPI_LOGITS = 5,     // out[r] = acc and greedy argmax into a 64-bit key
+    EPI_SWIGLU = 6      // rows (2i, 2i+1) = (ffn_up_i, ffn_gate_i): out[i] = silu(gate_i) * up_i
 };
+
+// silu(g) * u as the reference computes it (ops.rs:237-247, llama.rs:564-567).
+// Not inlined: one copy of its expf and two divisions serves every call site.
+static __device__ __noinline__ float ffn_silu_mul(float g, float u) {
+    float sig;
+    if (g >= 0.0f) sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
+    else { const float ex = expf(g); sig = __fdiv_rn(ex, __fadd_rn(1.0f, ex)); }
+    return __fmul_rn(__fmul_rn(g, sig), u);
+}
 
 struct Seg {
     QMat m;
@@ -646,6 +656,9 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, const Seg& sg, 
     switch (sg.epi) {
         case EPI_STORE:
             for (uint32_t r = 0; r < nvalid; ++r) sg.out[r0 + r] = sg.bias ? __fadd_rn(acc[r], sg.bias[r0 + r]) : acc[r];
+            break;
+        case EPI_SWIGLU:   // r0 even, both rows valid (the fused matrix has 2 f rows)
+            if (nvalid == 2) sg.out[r0 >> 1] = ffn_silu_mul(acc[1], acc[0]);
             break;
         case EPI_RESID: {
             bool nan = false;

@@ -33,7 +33,7 @@ constexpr int GS_WARPS = 8;
 constexpr int GS_THREADS = GS_WARPS * 32 + 32;
 constexpr int GS_MAX_STAGES = 4;
 constexpr int GS_WORDS = 96;    // limb words per span: 32 steps x 3 limbs
-constexpr int GS_XF = 9;        // floats per span: gs, then the sums of x over its eight 16-element quarters
+constexpr int GS_XF = 13;       // floats per span and column tile: gs, then 3 float4 of x sums (see xq_load)
 
 // ---- per-format span decoders --------------------------------------------
 // step s (0..31) of a span multiplies four weight codes by x elements
@@ -61,6 +61,13 @@ __device__ __forceinline__ uint32_t lds16(const uint8_t* p) {
     asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(smem_addr(p)));
     return v;
 }
+// x sums of a lane's span (shared memory, [k][lane] float4): k = 0, 1: the sums over
+// its eight 16-element quarters, k = 2: the sums over its four 32-element halves
+__device__ __forceinline__ float4 xq_load(const float* xq, int k) {
+    const uint4 v = lds128(reinterpret_cast<const uint8_t*>(xq + 128 * k));
+    return make_float4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z), __uint_as_float(v.w));
+}
+__device__ __forceinline__ float f4sel(const float4& v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
 __device__ __forceinline__ uint32_t wsel(const uint4& u, int i) { return i == 0 ? u.x : i == 1 ? u.y : i == 2 ? u.z : u.w; }
 __device__ __forceinline__ float comb3(int t0, int t1, int t2) {
     return fmaf(65536.f, (float)t2, fmaf(256.f, (float)t1, (float)t0));
@@ -85,7 +92,7 @@ template <> struct SpanFmt<GGC_Q4_K> {
         return 2 * (4 * k + t) + hi;
     }
     __device__ static constexpr int qoff(int t, int j) { return 4 * t + j; }   // elem(step_of(q, t), j) - 16 q
-    __device__ static float dot(const SpanRow& R, int lane, const uint32_t* L, const float* xf) {
+    __device__ static float dot(const SpanRow& R, int lane, const uint32_t* L, float gs, const float* xq) {
         uint4 u[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) u[k] = lds128(R.p[0] + (k * R.nl + lane) * 16);
@@ -106,12 +113,13 @@ template <> struct SpanFmt<GGC_Q4_K> {
             const int c = (int)((scm.x >> (8 * sb)) & 0xFFu) << ((sb & 1) ? 0 : 4);
             T0 += c * A[sb].a0; T1 += c * A[sb].a1; T2 += c * A[sb].a2;
         }
+        const float4 xs = xq_load(xq, 2);
         float mn = 0.f;
 #pragma unroll
-        for (int sb = 0; sb < 4; ++sb) mn = fmaf((float)((scm.y >> (8 * sb)) & 0xFFu), xf[GS_XF + sb], mn);
+        for (int sb = 0; sb < 4; ++sb) mn = fmaf((float)((scm.y >> (8 * sb)) & 0xFFu), f4sel(xs, sb), mn);
         const float2 dm = h2f2(dd);
         // value = d sc q - dmin mn  (quant.rs:275-279)
-        return fmaf(dm.x * (xf[0] * 0.0625f), comb3(T0, T1, T2), -dm.y * mn);
+        return fmaf(dm.x * (gs * 0.0625f), comb3(T0, T1, T2), -dm.y * mn);
     }
 };
 
@@ -130,45 +138,49 @@ template <> struct SpanFmt<GGC_Q6_K> {
         return 2 * (l0 >> 2) + hi;
     }
     __device__ static constexpr int qoff(int t, int j) { return 4 * t + j; }
-    __device__ static float dot(const SpanRow& R, int lane, const uint32_t* L, const float* xf) {
-        uint4 u[4], h[2];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) u[k] = lds128(R.p[0] + (k * R.nl + lane) * 16);
+    __device__ static float dot(const SpanRow& R, int lane, const uint32_t* L, float gs, const float* xq) {
+        uint4 h[2];
 #pragma unroll
         for (int k = 0; k < 2; ++k) h[k] = lds128(R.p[1] + (k * R.nl + lane) * 16);
         const uint2 sc = lds64(R.p[2] + lane * 8);
         const uint32_t d16 = lds16(R.p[3] + (lane >> 1) * 2);
-        Acc3 A[8];
-#pragma unroll
-        for (int w = 0; w < 16; ++w) {
-            const uint32_t q = wsel(u[w >> 2], w & 3);
-            const int v = w & 7;
-            const uint32_t hb = wsel(h[v >> 2], v & 3);
-            uint32_t lo, hi;
-            int glo, ghi;
-            if (w < 8) {
-                lo = (q & 0x0F0F0F0Fu) | ((hb << 4) & 0x30303030u);
-                hi = ((q >> 4) & 0x0F0F0F0Fu) | (hb & 0x30303030u);
-                glo = w >> 2; ghi = 4 + (w >> 2);
-            } else {
-                lo = (q & 0x0F0F0F0Fu) | ((hb << 2) & 0x30303030u);
-                hi = ((q >> 4) & 0x0F0F0F0Fu) | ((hb >> 2) & 0x30303030u);
-                glo = 2 + ((w - 8) >> 2); ghi = 6 + ((w - 8) >> 2);
-            }
-            dp3u(lo, L + 6 * w, A[glo]);
-            dp3u(hi, L + 6 * w + 3, A[ghi]);
-        }
-        // value = d sc (u - 32): sum_g sc_g (u . x_int) - 32 sum_g sc_g X_g
+        // value = d sc (u - 32): sum_g sc_g (u . x_int) - 32 sum_g sc_g X_g; two passes
+        // of eight ql words (groups {0,1,4,5}, then {2,3,6,7}) fold as they finish
         int T0 = 0, T1 = 0, T2 = 0;
         float off = 0.f;
+        const float4 xa = xq_load(xq, 0), xb = xq_load(xq, 1);
 #pragma unroll
-        for (int g = 0; g < 8; ++g) {
-            const int c = (int)(int8_t)(((g < 4 ? sc.x : sc.y) >> (8 * (g & 3))) & 0xFFu);
-            T0 += c * A[g].a0; T1 += c * A[g].a1; T2 += c * A[g].a2;
-            off = fmaf((float)c, xf[1 + g], off);
+        for (int half = 0; half < 2; ++half) {
+            uint4 u[2];
+#pragma unroll
+            for (int k = 0; k < 2; ++k) u[k] = lds128(R.p[0] + ((2 * half + k) * R.nl + lane) * 16);
+            Acc3 A[4];   // groups 2 half + {0, 1} (low nibbles), 4 + 2 half + {0, 1} (high)
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+                const int w = 8 * half + v;
+                const uint32_t q = wsel(u[v >> 2], v & 3);
+                const uint32_t hb = wsel(h[v >> 2], v & 3);
+                uint32_t lo, hi;
+                if (half == 0) {
+                    lo = (q & 0x0F0F0F0Fu) | ((hb << 4) & 0x30303030u);
+                    hi = ((q >> 4) & 0x0F0F0F0Fu) | (hb & 0x30303030u);
+                } else {
+                    lo = (q & 0x0F0F0F0Fu) | ((hb << 2) & 0x30303030u);
+                    hi = ((q >> 4) & 0x0F0F0F0Fu) | ((hb >> 2) & 0x30303030u);
+                }
+                dp3u(lo, L + 6 * w, A[v >> 2]);
+                dp3u(hi, L + 6 * w + 3, A[2 + (v >> 2)]);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int g = (j < 2 ? 0 : 4) + 2 * half + (j & 1);
+                const int c = (int)(int8_t)(((g < 4 ? sc.x : sc.y) >> (8 * (g & 3))) & 0xFFu);
+                T0 += c * A[j].a0; T1 += c * A[j].a1; T2 += c * A[j].a2;
+                off = fmaf((float)c, f4sel(g < 4 ? xa : xb, g & 3), off);
+            }
         }
         const float d = h2f(d16);
-        return d * fmaf(xf[0], comb3(T0, T1, T2), -32.f * off);
+        return d * fmaf(gs, comb3(T0, T1, T2), -32.f * off);
     }
 };
 
@@ -183,11 +195,12 @@ template <> struct SpanFmt<GGC_Q4_0> {
         return 8 * (q >> 1) + 2 * (2 * (q & 1) + (t >> 1)) + (t & 1);
     }
     __device__ static constexpr int qoff(int t, int j) { return 8 * (t >> 1) + 2 * j + (t & 1); }
-    __device__ static float dot(const SpanRow& R, int lane, const uint32_t* L, const float* xf) {
+    __device__ static float dot(const SpanRow& R, int lane, const uint32_t* L, float gs, const float* xq) {
         uint4 u[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) u[k] = lds128(R.p[0] + (k * R.nl + lane) * 16);
         const uint2 dd = lds64(R.p[1] + lane * 8);
+        const float4 xs = xq_load(xq, 2);
         float r = 0.f;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -201,7 +214,7 @@ template <> struct SpanFmt<GGC_Q4_0> {
             const float s16 = comb3(16 * lo.a0 + hi.a0, 16 * lo.a1 + hi.a1, 16 * lo.a2 + hi.a2);
             const float d = h2f(((k < 2 ? dd.x : dd.y) >> (16 * (k & 1))) & 0xFFFFu);
             // value = d (q - 8)  (quant.rs:139-150)
-            r = fmaf(d, fmaf(xf[0] * 0.0625f, s16, -8.f * xf[GS_XF + k]), r);
+            r = fmaf(d, fmaf(gs * 0.0625f, s16, -8.f * f4sel(xs, k)), r);
         }
         return r;
     }
@@ -215,7 +228,7 @@ template <> struct SpanFmt<GGC_Q8_0> {
     }
     __device__ static constexpr int step_of(int q, int t) { return 4 * q + t; }
     __device__ static constexpr int qoff(int t, int j) { return 4 * t + j; }
-    __device__ static float dot(const SpanRow& R, int lane, const uint32_t* L, const float* xf) {
+    __device__ static float dot(const SpanRow& R, int lane, const uint32_t* L, float gs, const float* xq) {
         uint4 u[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) u[k] = lds128(R.p[0] + (k * R.nl + lane) * 16);
@@ -231,7 +244,7 @@ template <> struct SpanFmt<GGC_Q8_0> {
             const float d = h2f(((b < 2 ? dd.x : dd.y) >> (16 * (b & 1))) & 0xFFFFu);
             r = fmaf(d, comb(A), r);   // value = d q  (quant.rs:173-180)
         }
-        return r * xf[0];
+        return r * gs;
     }
 };
 
@@ -263,6 +276,140 @@ SpanCfg make_span_cfg(uint32_t pcols, uint32_t total_rb, uint32_t ctas, size_t s
     c.stages = (uint32_t)(st > (size_t)GS_MAX_STAGES ? GS_MAX_STAGES : st);
     c.smem = (uint32_t)(fixed + (size_t)c.stages * c.stage_bytes);
     return c;
+}
+
+// x of one GEMV into the span limb layout for every column tile: xl[ct][24][lane][4]
+// limb words and xfs[ct] (gs per lane, then [3][lane] float4 of x sums).  Run by the 256 consumer
+// threads (named barrier 1); activations are read through L2 (written by other
+// CTAs of a persistent grid).  `red`: GS_WARPS doubles, `s_scale`: one float.
+// The prologue's input by value (kernel parameters cannot alias the stores the
+// prologue makes; fields read through a reference to global memory would be
+// re-loaded after each of them).
+struct SpanX {
+    const float* x;
+    const float* x2;
+    uint32_t xcols;
+    int pro;
+};
+__device__ __forceinline__ SpanX span_x_of(const GemvArgs& a) { return SpanX{a.x, a.x2, a.xcols, a.pro}; }
+
+__device__ __forceinline__ float span_xval(const SpanX a, uint32_t e, float scale) {
+    if (e >= a.xcols) return 0.f;
+    const float x = __ldcg(a.x + e);
+    if (a.pro == PRO_RMSNORM) return __fmul_rn(__fmul_rn(x, scale), __ldcg(a.x2 + e));
+    if (a.pro == PRO_SWIGLU) return ffn_silu_mul(x, __ldcg(a.x2 + e));
+    return x;
+}
+
+template <int DT>
+__device__ void span_x_prologue(const SpanX a, uint32_t nct, uint32_t* xl, float* xfs, double* red, float* s_scale) {
+    using F = SpanFmt<DT>;
+    constexpr uint32_t CT = GS_WARPS * 32;
+    auto cbar = [] { asm volatile("bar.sync 1, %0;" ::"r"(CT) : "memory"); };
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float scale = 0.f;
+    if (a.pro == PRO_RMSNORM) {
+        double ss = 0.0;
+        if ((a.xcols & 3) == 0) {
+            const float4* x4 = reinterpret_cast<const float4*>(a.x);
+            for (uint32_t i = tid; i < a.xcols / 4; i += CT) {
+                const float4 v = __ldcg(x4 + i);
+                ss += (double)v.x * (double)v.x + (double)v.y * (double)v.y + (double)v.z * (double)v.z +
+                      (double)v.w * (double)v.w;
+            }
+        } else {
+            for (uint32_t i = tid; i < a.xcols; i += CT) { const double v = (double)__ldcg(a.x + i); ss += v * v; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) red[warp] = ss;
+        cbar();
+        if (tid == 0) {
+            double t = 0.0;
+            for (int w = 0; w < GS_WARPS; ++w) t += red[w];
+            *s_scale = (float)sqrt(1.0 / (t / (double)a.xcols + (double)1e-6f));   // ops.rs:262-274
+        }
+        cbar();
+        scale = *s_scale;
+    }
+    // x -> limbs: 8 threads per span (one quarter of 16 elements each)
+    {
+        const uint32_t nsp = nct * SPAN_LANES, items = nsp * 8;
+        for (uint32_t base = 0; base < items; base += CT) {
+            const uint32_t it = base + tid;
+            const uint32_t sp = it >> 3, q = it & 7;
+            const bool live = it < items;
+            float v[16];
+            const uint32_t e0 = sp * SPAN + 16 * q;
+#pragma unroll
+            for (int k = 0; k < 16; ++k) v[k] = 0.f;
+            if (live && e0 + 16 <= a.xcols) {
+                const float4* x4 = reinterpret_cast<const float4*>(a.x + e0);
+                float4 xa[4], ya[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) xa[k] = __ldcg(x4 + k);
+                if (a.pro != PRO_PLAIN) {
+                    const float4* y4 = reinterpret_cast<const float4*>(a.x2 + e0);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) ya[k] = __ldcg(y4 + k);
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float xx[4] = {xa[k].x, xa[k].y, xa[k].z, xa[k].w};
+                    const float yy[4] = {ya[k].x, ya[k].y, ya[k].z, ya[k].w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        v[4 * k + j] = a.pro == PRO_RMSNORM ? __fmul_rn(__fmul_rn(xx[j], scale), yy[j])   // ops.rs:272
+                                     : a.pro == PRO_SWIGLU ? ffn_silu_mul(xx[j], yy[j])
+                                     : xx[j];
+                    }
+                }
+            } else if (live) {
+#pragma unroll
+                for (int k = 0; k < 16; ++k) v[k] = span_xval(a, e0 + k, scale);   // checks e < xcols
+            }
+            float mx = 0.f, sum = 0.f;
+#pragma unroll
+            for (int k = 0; k < 16; ++k) { mx = fmaxf(mx, fabsf(v[k])); sum += v[k]; }
+            bool finite = isfinite(mx) && isfinite(sum);
+            // the 8 quarters of a span are 8 consecutive threads of one warp
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) {
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                finite = __shfl_xor_sync(0xffffffffu, (int)finite, o) && finite;
+            }
+            const float pair = __shfl_xor_sync(0xffffffffu, sum, 1);   // the other quarter of the 32-element half
+            int ex = 0;
+            frexpf(mx, &ex);
+            const float mul = (mx > 0.f && finite) ? ldexpf(1.f, 22 - ex) : 0.f;
+            const float gs = !finite ? __int_as_float(0x7FC00000) : (mx > 0.f ? ldexpf(1.f, ex - 22) : 0.f);
+            if (live) {
+                const uint32_t ct = sp / SPAN_LANES, l = sp % SPAN_LANES;
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const int s = F::step_of((int)q, t);
+                    uint32_t w0 = 0, w1 = 0, w2 = 0;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int xi = __float2int_rn(v[F::qoff(t, j)] * mul);
+                        w0 |= (uint32_t)(xi & 0xFF) << (8 * j);
+                        w1 |= (uint32_t)((xi >> 8) & 0xFF) << (8 * j);
+                        w2 |= (uint32_t)((xi >> 16) & 0xFF) << (8 * j);
+                    }
+                    const uint32_t wi[3] = {(uint32_t)(3 * s), (uint32_t)(3 * s + 1), (uint32_t)(3 * s + 2)};
+                    const uint32_t wv[3] = {w0, w1, w2};
+#pragma unroll
+                    for (int k = 0; k < 3; ++k)
+                        xl[(((size_t)ct * 24 + wi[k] / 4) * SPAN_LANES + l) * 4 + wi[k] % 4] = wv[k];
+                }
+                float* xc = xfs + (size_t)ct * GS_XF * SPAN_LANES;   // [gs x 32][3][32] float4
+                xc[SPAN_LANES + ((q >> 2) * SPAN_LANES + l) * 4 + (q & 3)] = sum;
+                if ((q & 1) == 0) xc[SPAN_LANES + (2 * SPAN_LANES + l) * 4 + (q >> 1)] = sum + pair;
+                if (q == 0) xc[l] = gs;
+            }
+        }
+    }
+    cbar();
 }
 
 // ---- the kernel ------------------------------------------------------------
@@ -362,120 +509,14 @@ __global__ void __launch_bounds__(GS_THREADS, 1) k_gemv_span(const GemvArgs a, c
     }
     constexpr uint32_t CT = GS_WARPS * 32;
     auto cbar = [] { asm volatile("bar.sync 1, %0;" ::"r"(CT) : "memory"); };
-    float scale = 0.f;
-    if (a.pro == PRO_RMSNORM) {
-        double ss = 0.0;
-        if ((a.xcols & 3) == 0) {
-            const float4* x4 = reinterpret_cast<const float4*>(a.x);
-            for (uint32_t i = tid; i < a.xcols / 4; i += CT) {
-                const float4 v = x4[i];
-                ss += (double)v.x * (double)v.x + (double)v.y * (double)v.y + (double)v.z * (double)v.z +
-                      (double)v.w * (double)v.w;
-            }
-        } else {
-            for (uint32_t i = tid; i < a.xcols; i += CT) { const double v = (double)a.x[i]; ss += v * v; }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        if (lane == 0) red[warp] = ss;
-        cbar();
-        if (tid == 0) {
-            double t = 0.0;
-            for (int w = 0; w < GS_WARPS; ++w) t += red[w];
-            s_scale = (float)sqrt(1.0 / (t / (double)a.xcols + (double)1e-6f));   // ops.rs:262-274
-        }
-        cbar();
-        scale = s_scale;
-    }
-    // x -> limbs: 8 threads per span (one quarter of 16 elements each)
-    {
-        const uint32_t nsp = nct * SPAN_LANES, items = nsp * 8;
-        for (uint32_t base = 0; base < items; base += CT) {
-            const uint32_t it = base + tid;
-            const uint32_t sp = it >> 3, q = it & 7;
-            const bool live = it < items;
-            float v[16];
-            const uint32_t e0 = sp * SPAN + 16 * q;
-#pragma unroll
-            for (int k = 0; k < 16; ++k) v[k] = 0.f;
-            if (live && e0 + 16 <= a.xcols) {
-                const float4* x4 = reinterpret_cast<const float4*>(a.x + e0);
-                float4 xa[4], ya[4];
-#pragma unroll
-                for (int k = 0; k < 4; ++k) xa[k] = x4[k];
-                if (a.pro != PRO_PLAIN) {
-                    const float4* y4 = reinterpret_cast<const float4*>(a.x2 + e0);
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) ya[k] = y4[k];
-                }
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const float xx[4] = {xa[k].x, xa[k].y, xa[k].z, xa[k].w};
-                    const float yy[4] = {ya[k].x, ya[k].y, ya[k].z, ya[k].w};
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        float r = xx[j];
-                        if (a.pro == PRO_RMSNORM) {
-                            r = __fmul_rn(__fmul_rn(xx[j], scale), yy[j]);   // ops.rs:272
-                        } else if (a.pro == PRO_SWIGLU) {                 // ops.rs:237-247, llama.rs:564-567
-                            const float gg = xx[j];
-                            float sig;
-                            if (gg >= 0.0f) sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gg)));
-                            else { const float ex = expf(gg); sig = __fdiv_rn(ex, __fadd_rn(1.0f, ex)); }
-                            r = __fmul_rn(__fmul_rn(gg, sig), yy[j]);
-                        }
-                        v[4 * k + j] = r;
-                    }
-                }
-            } else if (live) {
-#pragma unroll
-                for (int k = 0; k < 16; ++k)
-                    if (e0 + k < a.xcols) v[k] = gemv_xval(a, e0 + k, scale);
-            }
-            float mx = 0.f, sum = 0.f;
-#pragma unroll
-            for (int k = 0; k < 16; ++k) { mx = fmaxf(mx, fabsf(v[k])); sum += v[k]; }
-            bool finite = isfinite(mx) && isfinite(sum);
-            // the 8 quarters of a span are 8 consecutive threads of one warp
-#pragma unroll
-            for (int o = 1; o < 8; o <<= 1) {
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-                finite = __shfl_xor_sync(0xffffffffu, (int)finite, o) && finite;
-            }
-            int ex = 0;
-            frexpf(mx, &ex);
-            const float mul = (mx > 0.f && finite) ? ldexpf(1.f, 22 - ex) : 0.f;
-            const float gs = !finite ? __int_as_float(0x7FC00000) : (mx > 0.f ? ldexpf(1.f, ex - 22) : 0.f);
-            if (live) {
-                const uint32_t ct = sp / SPAN_LANES, l = sp % SPAN_LANES;
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const int s = F::step_of((int)q, t);
-                    uint32_t w0 = 0, w1 = 0, w2 = 0;
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const int xi = __float2int_rn(v[F::qoff(t, j)] * mul);
-                        w0 |= (uint32_t)(xi & 0xFF) << (8 * j);
-                        w1 |= (uint32_t)((xi >> 8) & 0xFF) << (8 * j);
-                        w2 |= (uint32_t)((xi >> 16) & 0xFF) << (8 * j);
-                    }
-                    const uint32_t wi[3] = {(uint32_t)(3 * s), (uint32_t)(3 * s + 1), (uint32_t)(3 * s + 2)};
-                    const uint32_t wv[3] = {w0, w1, w2};
-#pragma unroll
-                    for (int k = 0; k < 3; ++k)
-                        xl[(((size_t)ct * 24 + wi[k] / 4) * SPAN_LANES + l) * 4 + wi[k] % 4] = wv[k];
-                }
-                xfs[((size_t)ct * GS_XF + 1 + q) * SPAN_LANES + l] = sum;
-                if (q == 0) xfs[((size_t)ct * GS_XF) * SPAN_LANES + l] = gs;
-            }
-        }
-    }
+    span_x_prologue<DT>(span_x_of(a), nct, xl, xfs, red, &s_scale);
     for (uint32_t i = tid; i < cfg.part_rows; i += CT) part[i] = 0.f;
     cbar();
 
     const int r0 = 2 * warp;   // this warp's row pair in every tile
     uint32_t L[GS_WORDS];
-    float xf[GS_XF + 4];        // gs, the eight quarter sums, the four 32-element sums
+    float gs = 0.f;             // x scale of this lane's span in the current column tile
+    const float* xq = nullptr;  // its x sums (shared memory)
     unsigned long long best = 0ull;
     bool nan_logit = false;
     // tile i = (column tile ct, row block rb0 + rbl); counters advance instead of dividing
@@ -500,10 +541,8 @@ __global__ void __launch_bounds__(GS_THREADS, 1) k_gemv_span(const GemvArgs a, c
                 const uint4 w4 = *reinterpret_cast<const uint4*>(xl + (((size_t)ct * 24 + k) * SPAN_LANES + lane) * 4);
                 L[4 * k] = w4.x; L[4 * k + 1] = w4.y; L[4 * k + 2] = w4.z; L[4 * k + 3] = w4.w;
             }
-#pragma unroll
-            for (int k = 0; k < GS_XF; ++k) xf[k] = xfs[((size_t)ct * GS_XF + k) * SPAN_LANES + lane];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) xf[GS_XF + k] = xf[1 + 2 * k] + xf[2 + 2 * k];
+            gs = xfs[(size_t)ct * GS_XF * SPAN_LANES + lane];
+            xq = xfs + (size_t)ct * GS_XF * SPAN_LANES + SPAN_LANES + lane * 4;
         }
         const uint8_t* st = stages + (size_t)s * cfg.stage_bytes;
         float y[2];
@@ -513,7 +552,7 @@ __global__ void __launch_bounds__(GS_THREADS, 1) k_gemv_span(const GemvArgs a, c
 #pragma unroll
             for (int p = 0; p < 4; ++p) R.p[p] = st + rowoff[k][p];
             R.nl = nl;
-            y[k] = lane < nl ? F::dot(R, lane, L, xf) : 0.f;
+            y[k] = lane < nl ? F::dot(R, lane, L, gs, xq) : 0.f;
         }
         // two row sums: halve the exchange (lanes < 16 keep row 0), then reduce
         {

@@ -8,6 +8,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdlib>
+#include <cstring>
 #include <memory>
 #include <mutex>
 #include <string>
@@ -24,6 +25,7 @@
 #include "gemv_span.cuh"
 #include "attention.cuh"
 #include "noalloc.cuh"
+#include "stream.cuh"
 
 using namespace ggc;
 
@@ -747,6 +749,26 @@ extern "C" int ggc_tensor_matvec(ggc_ctx* ctx, const ggc_tensor* t, const float*
     return GGC_OK;
 }
 
+extern "C" int ggc_tensor_matvec_batch(ggc_ctx* ctx, const ggc_tensor* const* ts, uint64_t n, const float* x, float* y) {
+    if (!ctx || (!ts && n) || !x || !y) return set_error(GGC_ERR_INVALID_ARG, "null argument");
+    if (!is_device_ptr(x) || !is_device_ptr(y)) return set_error(GGC_ERR_INVALID_ARG, "x and y must be device buffers");
+    DeviceGuard g(ctx->device);
+    for (uint64_t i = 0; i < n; ++i) {
+        const ggc_tensor* t = ts[i];
+        if (!t || !t->repacked) return set_error(GGC_ERR_INVALID_ARG, "tensor %llu missing or not in plane layout",
+                                                 (unsigned long long)i);
+        GemvArgs a{};
+        a.seg[0] = make_seg(t->mat, EPI_STORE, y, nullptr, nullptr);
+        a.nseg = 1;
+        a.pro = PRO_PLAIN;
+        a.x = x;
+        a.cols = t->mat.cols;
+        a.xcols = t->mat.xcols;
+        GGC_TRY(run_gemv(ctx, t->dtype, a));
+    }
+    return GGC_OK;
+}
+
 extern "C" int ggc_tensor_dequantize(ggc_ctx* ctx, const ggc_tensor* t, float* out) {
     if (!ctx || !t || !out) return set_error(GGC_ERR_INVALID_ARG, "null argument");
     if (t->repacked) return set_error(GGC_ERR_INVALID_ARG, "tensor was uploaded in plane layout; upload with repack=0");
@@ -869,6 +891,7 @@ struct ModelLayer {
     float* bk = nullptr;
     float* bv = nullptr;
     DevMat wq, wk, wv, wo, up, gate, down;
+    DevMat ug;   // ffn_up / ffn_gate rows interleaved (same dtype): one GEMV with the SwiGLU epilogue
 };
 
 struct ggc_model {
@@ -889,6 +912,11 @@ struct ggc_model {
     float *hidden = nullptr, *q = nullptr, *o = nullptr, *ubuf = nullptr, *gbuf = nullptr, *logits = nullptr;
     float *scores = nullptr, *pmax = nullptr, *psum = nullptr, *opart = nullptr;
     AttnDecodeSel attn;   // fused decode attention, or null for the general pair
+    // the persistent decode step (k_stream), when every weight is a span format
+    bool stream = false;
+    StreamArgs sargs{};
+    size_t stream_smem = 0;
+    unsigned stream_grid = 0;
     float2* stats = nullptr;
     unsigned* tickets = nullptr;
     unsigned long long* argmax_key = nullptr;
@@ -951,6 +979,31 @@ int upload_weight(ggc_model* m, const ggc_tensor_desc& t, uint64_t rows, uint64_
     return upload_mat(m->ctx, t.data, t.nbytes, t.dtype, rows, cols, row_src, out);
 }
 
+// ffn_up and ffn_gate (llama.rs:547-580).  With one dtype they become one matrix
+// whose rows 2i, 2i+1 are up row i, gate row i, so a row pair of the GEMV yields
+// silu(gate_i) * up_i in its epilogue; otherwise two matrices.
+int upload_ffn_up_gate(ggc_model* m, const ggc_tensor_desc& up, const ggc_tensor_desc& gate, uint64_t f, uint64_t d,
+                       ModelLayer& ML) {
+    if (!up.data) return set_error(GGC_ERR_MISSING_TENSOR, "MissingTensor { name: ffn_up, kind: tensor }");
+    if (!gate.data) return set_error(GGC_ERR_MISSING_TENSOR, "MissingTensor { name: ffn_gate, kind: tensor }");
+    if (up.n_elements != f * d) return set_dequant_error(GGC_F32, f * d, up.n_elements, "ffn_up");
+    if (gate.n_elements != f * d) return set_dequant_error(GGC_F32, f * d, gate.n_elements, "ffn_gate");
+    const int bs = block_size_of(up.dtype), bb = block_bytes_of(up.dtype);
+    if (up.dtype != gate.dtype || bs < 0 || d % (uint64_t)bs != 0) {
+        GGC_TRY(upload_weight(m, up, f, d, nullptr, ML.up, "ffn_up"));
+        return upload_weight(m, gate, f, d, nullptr, ML.gate, "ffn_gate");
+    }
+    const uint64_t rb = d / bs * (uint64_t)bb;
+    if (up.nbytes < f * rb) return set_dequant_error(up.dtype, f * rb, up.nbytes, "ffn_up");
+    if (gate.nbytes < f * rb) return set_dequant_error(gate.dtype, f * rb, gate.nbytes, "ffn_gate");
+    std::vector<uint8_t> both(2 * f * rb);
+    for (uint64_t i = 0; i < f; ++i) {
+        memcpy(both.data() + (2 * i) * rb, (const uint8_t*)up.data + i * rb, rb);
+        memcpy(both.data() + (2 * i + 1) * rb, (const uint8_t*)gate.data + i * rb, rb);
+    }
+    return upload_mat(m->ctx, both.data(), both.size(), up.dtype, 2 * f, d, nullptr, ML.ug);
+}
+
 // RoPE pair order: plane row 2m / 2m+1 = logical rows h hd + j / h hd + j + hd/2
 std::vector<uint32_t> rope_row_order(uint32_t heads, uint32_t hd) {
     std::vector<uint32_t> v((size_t)heads * hd);
@@ -997,6 +1050,14 @@ int enqueue_step(ggc_model* m) {
     cudaError_t err = cudaSuccess;
     dispatch_dtype<RunEmbed>(m->embd_dtype, ctx, (const uint8_t*)m->embd, m->embd_rows, d, m->st, m->hidden, m->errf, &err);
     GGC_CUDA_TRY(err);
+    if (m->stream) {
+        GGC_CUDA_TRY(stream_launch(m->hd, hp.kv_f16 != 0, hp.n_heads / hp.n_kv_heads, m->sargs, m->stream_grid,
+                                   m->stream_smem, ctx->stream));
+        ctx->launches++;
+        GGC_CUDA_TRY(launch(ctx, k_step_end, dim3(1), dim3(32), 0, m->st, (const unsigned long long*)m->argmax_key,
+                            m->out_ids, m->errf));
+        return GGC_OK;
+    }
     GemvArgs base{};
     base.st_done = &m->st->done;
     base.slot = &m->st->slot;
@@ -1054,15 +1115,22 @@ int enqueue_step(ggc_model* m) {
         GGC_TRY(run_segments(m, {{L.wo.dtype, make_seg(L.wo, EPI_RESID, m->hidden, nullptr, nullptr)}}, PRO_PLAIN, m->o,
                              nullptr, L.wo.cols, L.wo.xcols, ro));
         // ffn_block (llama.rs:547-580): rmsnorm -> up, gate -> silu(gate)*up -> down + residual
-        GGC_TRY(run_segments(m,
-                             {{L.up.dtype, make_seg(L.up, EPI_STORE, m->ubuf, nullptr, nullptr)},
-                              {L.gate.dtype, make_seg(L.gate, EPI_STORE, m->gbuf, nullptr, nullptr)}},
-                             PRO_RMSNORM, m->hidden, L.ffn_norm, L.up.cols, d, base));
         GemvArgs rd = base;
         rd.err_slot = ERRF_NAN_FFN;
         rd.err_val = (int)l + 1;
-        GGC_TRY(run_segments(m, {{L.down.dtype, make_seg(L.down, EPI_RESID, m->hidden, nullptr, nullptr)}}, PRO_SWIGLU,
-                             m->gbuf, m->ubuf, L.down.cols, f, rd));
+        if (L.ug.base) {   // fused up/gate: h = silu(gate) * up in the epilogue (into ubuf), then down
+            GGC_TRY(run_segments(m, {{L.ug.dtype, make_seg(L.ug, EPI_SWIGLU, m->ubuf, nullptr, nullptr)}}, PRO_RMSNORM,
+                                 m->hidden, L.ffn_norm, L.ug.cols, d, base));
+            GGC_TRY(run_segments(m, {{L.down.dtype, make_seg(L.down, EPI_RESID, m->hidden, nullptr, nullptr)}},
+                                 PRO_PLAIN, m->ubuf, nullptr, L.down.cols, f, rd));
+        } else {
+            GGC_TRY(run_segments(m,
+                                 {{L.up.dtype, make_seg(L.up, EPI_STORE, m->ubuf, nullptr, nullptr)},
+                                  {L.gate.dtype, make_seg(L.gate, EPI_STORE, m->gbuf, nullptr, nullptr)}},
+                                 PRO_RMSNORM, m->hidden, L.ffn_norm, L.up.cols, d, base));
+            GGC_TRY(run_segments(m, {{L.down.dtype, make_seg(L.down, EPI_RESID, m->hidden, nullptr, nullptr)}},
+                                 PRO_SWIGLU, m->gbuf, m->ubuf, L.down.cols, f, rd));
+        }
     }
     // final norm + lm_head for the last token only (llama.rs:333, :582-616) + greedy argmax
     GemvArgs lh = base;
@@ -1071,6 +1139,159 @@ int enqueue_step(ggc_model* m) {
                          PRO_RMSNORM, m->hidden, m->output_norm, m->output.cols, d, lh));
     GGC_CUDA_TRY(launch(ctx, k_step_end, dim3(1), dim3(32), 0, m->st, (const unsigned long long*)m->argmax_key,
                         m->out_ids, m->errf));
+    return GGC_OK;
+}
+
+// The op list of one decode step for k_stream (llama.rs:266-350): per layer the
+// Q/K/V GEMVs (RMSNorm prologue, bias + RoPE + cache-append epilogues), attention,
+// the output projection (+ residual), up/gate (RMSNorm), down (silu(gate) * up
+// prologue, + residual); then the final norm + lm_head with the greedy argmax.
+// Used only with GGC_DECODE_PATH=stream (the per-op kernels are the default);
+// leaves m->stream false when a weight is not a span format or the attention
+// shape has no fused kernel.
+int build_stream(ggc_model* m) {
+    const char* env = getenv("GGC_DECODE_PATH");
+    if (!env || strcmp(env, "stream") != 0) return GGC_OK;
+    const ggc_hparams& hp = m->hp;
+    const uint32_t G = hp.n_heads / hp.n_kv_heads;
+    const bool f16 = hp.kv_f16 != 0;
+    if (!m->attn.kernel || !stream_supported(m->hd, f16, G)) return GGC_OK;
+    for (auto& L : m->layers) {
+        if (!L.ug.base) return GGC_OK;   // the stream runs the fused up/gate GEMV
+        for (const DevMat* d : {&L.wq, &L.wk, &L.wv, &L.wo, &L.ug, &L.down})
+            if (!is_span_dt(d->dtype)) return GGC_OK;
+    }
+    if (!is_span_dt(m->output.dtype)) return GGC_OK;
+    ggc_ctx* ctx = m->ctx;
+    const unsigned grid = (unsigned)ctx->num_sms;
+    std::vector<StreamOp> ops;
+    uint32_t stage_bytes = 0, xl_bytes = 0, part_rows = 0;
+    GemvArgs base{};
+    base.slot = &m->st->slot;
+    base.pos = &m->st->pos;
+    base.rope = m->rope;
+    base.hd = m->hd;
+    base.kv_ctx = hp.max_ctx;
+    base.kv_f16 = f16 ? 1 : 0;
+    base.errf = m->errf;
+    base.argmax_key = m->argmax_key;
+    // GEMV ops over segments grouped by dtype (<= 3 per op), all depending on `dep`
+    auto add_gemv = [&](std::vector<std::pair<int, Seg>> segs, int pro, const float* x, const float* x2, uint32_t cols,
+                        uint32_t xcols, int err_slot, int err_val, int logits, int dep) {
+        while (!segs.empty()) {
+            const int dt = segs.front().first;
+            StreamOp op{};
+            op.kind = SOP_GEMV;
+            op.dtype = dt;
+            op.dep = dep;
+            op.logits = logits;
+            op.g = base;
+            op.g.nseg = 0;
+            std::vector<std::pair<int, Seg>> rest;
+            for (auto& sg : segs) {
+                if (sg.first == dt && op.g.nseg < 3) op.g.seg[op.g.nseg++] = sg.second;
+                else rest.push_back(sg);
+            }
+            op.g.pro = pro;
+            op.g.x = x;
+            op.g.x2 = x2;
+            op.g.cols = cols;
+            op.g.xcols = xcols;
+            op.g.err_slot = err_slot;
+            op.g.err_val = err_val;
+            const TileLayout L = make_layout(dt, TILE_ROWS, cols);
+            const SpanSpec sp = span_spec(dt);
+            uint32_t off = 0;
+            for (int p = 0; p < 4; ++p) {
+                op.poff[p] = off;
+                off += p < sp.n ? (TILE_ROWS * L.tp_full[p] + 127u) / 128u * 128u : 0u;
+            }
+            stage_bytes = std::max(stage_bytes, off);
+            xl_bytes = std::max(xl_bytes, L.nct * SPAN_LANES * (uint32_t)(GS_WORDS + GS_XF) * 4u);
+            uint32_t total_rb = 0;
+            for (int i = 0; i < op.g.nseg; ++i) total_rb += op.g.seg[i].m.L.nrb;
+            op.part_rows = L.nct > 1 ? (total_rb + grid - 1) / grid * TILE_ROWS : 0u;
+            part_rows = std::max(part_rows, op.part_rows);
+            ops.push_back(op);
+            segs.swap(rest);
+        }
+        return (int)ops.size() - 1;
+    };
+    const uint32_t d = hp.embed_dim, f = hp.ffn_dim;
+    const size_t layer_kv = (size_t)hp.max_ctx * m->kvdim * m->kv_elem;
+    int last = -1;
+    for (uint32_t l = 0; l < hp.n_layers; ++l) {
+        ModelLayer& L = m->layers[l];
+        void* kc = (uint8_t*)m->kcache + l * layer_kv;
+        void* vc = (uint8_t*)m->vcache + l * layer_kv;
+        const int qkv = add_gemv({{L.wq.dtype, make_seg(L.wq, EPI_ROPE_Q, m->q, nullptr, L.bq)},
+                                  {L.wk.dtype, make_seg(L.wk, EPI_ROPE_KC, nullptr, kc, L.bk)},
+                                  {L.wv.dtype, make_seg(L.wv, EPI_VC, nullptr, vc, L.bv)}},
+                                 PRO_RMSNORM, m->hidden, L.attn_norm, L.wq.cols, d, 0, 0, 0, last);
+        StreamOp at{};
+        at.kind = SOP_ATTN;
+        at.dep = qkv;
+        at.at.q = m->q;
+        at.at.kc = kc;
+        at.at.vc = vc;
+        at.at.pmax = m->pmax;
+        at.at.psum = m->psum;
+        at.at.opart = m->opart;
+        at.at.o = m->o;
+        at.at.tickets = m->tickets;
+        at.at.slot = &m->st->slot;
+        at.at.pos = &m->st->pos;
+        at.at.done = &m->st->done;
+        at.at.errf = m->errf;
+        at.at.n_heads = hp.n_heads;
+        at.at.kvh = hp.n_kv_heads;
+        at.at.hd = m->hd;
+        at.at.max_ctx = hp.max_ctx;
+        at.at.nsplit = m->nsplit;
+        at.at.inv = 1.0f / sqrtf((float)m->hd);
+        at.at.kv_f16 = f16 ? 1 : 0;
+        ops.push_back(at);
+        const int attn = (int)ops.size() - 1;
+        const int o = add_gemv({{L.wo.dtype, make_seg(L.wo, EPI_RESID, m->hidden, nullptr, nullptr)}}, PRO_PLAIN, m->o,
+                               nullptr, L.wo.cols, L.wo.xcols, ERRF_NAN_ATTN, (int)l + 1, 0, attn);
+        const int ug = add_gemv({{L.ug.dtype, make_seg(L.ug, EPI_SWIGLU, m->ubuf, nullptr, nullptr)}}, PRO_RMSNORM,
+                                m->hidden, L.ffn_norm, L.ug.cols, d, 0, 0, 0, o);
+        last = add_gemv({{L.down.dtype, make_seg(L.down, EPI_RESID, m->hidden, nullptr, nullptr)}}, PRO_PLAIN, m->ubuf,
+                        nullptr, L.down.cols, f, ERRF_NAN_FFN, (int)l + 1, 0, ug);
+    }
+    add_gemv({{m->output.dtype, make_seg(m->output, EPI_LOGITS, m->logits, nullptr, nullptr)}}, PRO_RMSNORM, m->hidden,
+             m->output_norm, m->output.cols, d, 0, 0, 1, last);
+    uint32_t attn_tile = 0, attn_scratch = 0;
+    stream_attn_geometry(m->hd, f16, G, &attn_tile, &attn_scratch);
+    auto r128 = [](uint32_t b) { return (b + 127u) / 128u * 128u; };
+    StreamArgs& P = m->sargs;
+    P.stage_bytes = r128(std::max(stage_bytes, attn_tile));
+    P.xl_bytes = r128(std::max(xl_bytes, attn_scratch));
+    P.part_bytes = r128(part_rows * 4u);
+    const size_t fixed = (size_t)P.xl_bytes + P.part_bytes + 128;
+    const size_t st = GEMV_SMEM_LIMIT > fixed ? (GEMV_SMEM_LIMIT - fixed) / P.stage_bytes : 0;
+    P.stages = (uint32_t)std::min<size_t>(st, GS_MAX_STAGES);
+    if (P.stages < 2) return GGC_OK;   // does not fit: per-op kernels
+    m->stream_smem = fixed + (size_t)P.stages * P.stage_bytes;
+    int per_sm = 0;
+    if (stream_prepare(m->hd, f16, G, m->stream_smem, &per_sm) != cudaSuccess || per_sm < 1) {
+        cudaGetLastError();
+        return GGC_OK;
+    }
+    StreamOp* dops = nullptr;
+    GGC_TRY(dalloc(m, &dops, ops.size()));
+    GGC_CUDA_TRY(cudaMemcpy(dops, ops.data(), ops.size() * sizeof(StreamOp), cudaMemcpyHostToDevice));
+    unsigned* done = nullptr;
+    GGC_TRY(dalloc(m, &done, ops.size() + 1));
+    P.ops = dops;
+    P.n_ops = (int)ops.size();
+    P.done = done;
+    P.st_done = &m->st->done;
+    P.st_skip = &m->st->in_idx;
+    P.errf = m->errf;
+    P.argmax_key = m->argmax_key;
+    m->stream_grid = grid;
+    m->stream = true;
     return GGC_OK;
 }
 
@@ -1103,7 +1324,7 @@ void destroy_model(ggc_model* m) {
         if (m->graph) cudaGraphExecDestroy(m->graph);
         for (auto& L : m->layers) {
             free_mat(L.wq); free_mat(L.wk); free_mat(L.wv); free_mat(L.wo);
-            free_mat(L.up); free_mat(L.gate); free_mat(L.down);
+            free_mat(L.up); free_mat(L.gate); free_mat(L.down); free_mat(L.ug);
         }
         free_mat(m->output);
         for (void* p : m->allocs) cudaFree(p);
@@ -1172,8 +1393,7 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
         GGC_TRY(upload_weight(m.get(), L[7], d, m->qdim, nullptr, ML.wo, "attn_output"));
         GGC_TRY(upload_vec(m.get(), L[8], d, &ML.ffn_norm, "ffn_norm"));
         if (!ML.ffn_norm) return set_error(GGC_ERR_MISSING_TENSOR, "MissingTensor { name: blk.%u.ffn_norm, kind: tensor }", l);
-        GGC_TRY(upload_weight(m.get(), L[9], f, d, nullptr, ML.up, "ffn_up"));
-        GGC_TRY(upload_weight(m.get(), L[10], f, d, nullptr, ML.gate, "ffn_gate"));
+        GGC_TRY(upload_ffn_up_gate(m.get(), L[9], L[10], f, d, ML));
         GGC_TRY(upload_weight(m.get(), L[11], d, f, nullptr, ML.down, "ffn_down"));
     }
     // KV cache resident in HBM, head-major: [layer][n_kv][max_ctx][hd]
@@ -1226,6 +1446,7 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
     s0.done = 1;
     s0.max_ctx = hp.max_ctx;
     GGC_CUDA_TRY(cudaMemcpy(m->st, &s0, sizeof(s0), cudaMemcpyHostToDevice));
+    GGC_TRY(build_stream(m.get()));
     GGC_TRY(build_graph(m.get()));
     GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
     *out = m.release();
@@ -1268,8 +1489,11 @@ int check_run(ggc_model* m) {
         status = set_error(GGC_ERR_KV_CACHE_OVERFLOW, "KvCacheOverflow { seq_len: %d, max_seq: %u }", e[ERRF_KV_OVERFLOW] - 1,
                            m->hp.max_ctx);
     } else if (e[ERRF_BAD_POS]) status = set_error(GGC_ERR_INFERENCE, "position outside [0, %u)", m->hp.max_ctx);
+    else if (e[ERRF_TIMEOUT]) status = set_error(GGC_ERR_TIMEOUT, "a bounded device wait expired");
     if (status != GGC_OK) {
         cudaMemsetAsync(m->errf, 0, sizeof(int) * ERRF_COUNT, m->ctx->stream);
+        if (m->stream)   // an abandoned launch may leave completion counters behind
+            cudaMemsetAsync(m->sargs.done, 0, sizeof(unsigned) * (m->sargs.n_ops + 1), m->ctx->stream);
         cudaStreamSynchronize(m->ctx->stream);
     }
     return status;

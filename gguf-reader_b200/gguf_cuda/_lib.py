@@ -130,6 +130,7 @@ SIGNATURES = {
     "ggc_tensor_upload": (_i32, [_vp, _vp, _u64, _i32, C.POINTER(_u64), _i32, _i32, C.POINTER(_vp)]),
     "ggc_tensor_free": (_i32, [_vp]),
     "ggc_tensor_matvec": (_i32, [_vp, _vp, _vp, _vp]),
+    "ggc_tensor_matvec_batch": (_i32, [_vp, C.POINTER(_vp), _u64, _vp, _vp]),
     "ggc_tensor_dequantize": (_i32, [_vp, _vp, _vp]),
     "ggc_infer_k_quant_dtype": (_i32, [_u64, _u64, _i32]),
     "ggc_model_create": (_i32, [_vp, C.POINTER(HParams), C.POINTER(TensorDesc), _u64, C.POINTER(_vp)]),

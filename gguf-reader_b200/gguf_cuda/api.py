@@ -152,6 +152,16 @@ class Tensor:
         check(lib().ggc_tensor_matvec(self.ctx.h, self.h, _ptr(x)[0], _ptr(y)[0]))
         return y
 
+    @staticmethod
+    def matvec_batch(tensors, x, y):
+        """y = W_i x for each tensor in turn, queued on the context stream (device x, y)."""
+        if not tensors:
+            return y
+        ctx = tensors[0].ctx
+        arr = (C.c_void_p * len(tensors))(*[t.h.value for t in tensors])
+        check(lib().ggc_tensor_matvec_batch(ctx.h, arr, len(tensors), _ptr(x)[0], _ptr(y)[0]))
+        return y
+
     def dequantize(self, out=None):
         if out is None:
             out = np.empty(self.rows * self.cols, dtype=np.float32)

@@ -125,6 +125,10 @@ int ggc_tensor_upload(ggc_ctx* ctx, const void* raw, uint64_t bytes, int dtype, 
 int ggc_tensor_free(ggc_tensor* t);
 /* y = W x for an uploaded 2-D tensor (rows = ne[1], cols = ne[0]); x, y device or host. */
 int ggc_tensor_matvec(ggc_ctx* ctx, const ggc_tensor* t, const float* x, float* y);
+/* y_i = W_i x for n uploaded tensors of one shape, queued back to back on the
+ * context stream without synchronising (x, y device buffers; y shared).  The
+ * matvec stream a decode step issues, without the host call per matrix. */
+int ggc_tensor_matvec_batch(ggc_ctx* ctx, const ggc_tensor* const* ts, uint64_t n, const float* x, float* y);
 /* Dequantises an uploaded tensor to f32 (n = all elements). */
 int ggc_tensor_dequantize(ggc_ctx* ctx, const ggc_tensor* t, float* out);
 
