@@ -15,7 +15,11 @@ token.  Per-step HBM traffic (~6 GB) is far above L2, so no explicit L2 flush.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Under torchrun each rank decodes its own replica (replicas only; weak scaling).
+Under torchrun (N > 1) the ranks run ONE model tensor-parallel (default,
+`--parallel tp`: q/k/v/up/gate rows and attn_output/ffn_down columns sharded,
+NCCL all-reduce of the hidden state after attn_output and ffn_down; strong
+scaling: `value` is that model's tokens/s) or, with `--parallel replicas`, one
+independent replica per rank (weak scaling: `value` sums the replicas).
 `--impl reference` times the CPU restatement of the reference's rayon path.
 """
 from __future__ import annotations
@@ -48,6 +52,7 @@ def parse_args():
     ap.add_argument("--ctx", type=int, default=2048)
     ap.add_argument("--layers", type=int, default=None, help="fewer layers (small profiling cases only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--parallel", choices=["tp", "replicas"], default="tp", help="multi-GPU mode (N > 1)")
     return ap.parse_args()
 
 
@@ -177,7 +182,19 @@ def config_block(args):
     layers = "" if args.layers is None else f", first {args.layers} layers only (profiling case)"
     return {"workload": f"{MODEL} decode, batch 1, context {args.ctx} (cache prefilled with planted K/V rows so the "
                         f"timed steps end at {args.ctx}), f32 KV cache{layers}", "global_batch": 1, "seq_len": args.ctx,
-            "parallelism": f"replicas x{args.gpus}", "l2": "per-step traffic ~6 GB >> 126 MB L2 (no flush needed)"}
+            "parallelism": parallelism(args), "l2": "per-step traffic ~6 GB >> 126 MB L2 (no flush needed)"}
+
+
+def parallelism(args):
+    if args.gpus <= 1:
+        return "single GPU"
+    if args.parallel == "tp":
+        return f"tp{args.gpus} (NCCL all-reduce after attn_output and ffn_down)"
+    return f"replicas x{args.gpus}"
+
+
+def tp_mode(args, world):
+    return world > 1 and args.parallel == "tp"
 
 
 # ---------------------------------------------------------------------------
@@ -231,7 +248,13 @@ def run_ours(args, rank, world, local_rank):
         import torch.distributed as dist
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local_rank))
-    ctx = ggc.Context(local_rank)
+    tp = tp_mode(args, world)
+    if tp:   # one communicator of the library's own, from rank 0's unique id
+        nid = [ggc.Context.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(nid, src=0)
+        ctx = ggc.Context(local_rank, rank=rank, world=world, nccl_id=nid[0])
+    else:
+        ctx = ggc.Context(local_rank)
     stream = torch.cuda.ExternalStream(ctx.stream)
     peak_gbs, peak_src = peaks()
 
@@ -277,7 +300,8 @@ def run_ours(args, rank, world, local_rank):
         barrier()
     elapsed = max_over_ranks(e0.elapsed_time(e1) / 1e3)
     assert len(ids) == K and model.cache_len() == C
-    value = world * K / elapsed
+    streams = 1 if tp else world   # token streams the job decodes
+    value = streams * K / elapsed
 
     # e2e: reference-facing forward(host token) -> host logits, per token
     model.truncate(P + W)
@@ -302,7 +326,11 @@ def run_ours(args, rank, world, local_rank):
     if rank == 0:
         kv_bytes = synth.kv_bytes_per_token(hp, C - K // 2)
         step_bytes = w_bytes + kv_bytes
-        model_gbs = step_bytes * (K / elapsed) / 1e9
+        # HBM bytes one GPU moves per token: its shard of the layers and the KV
+        # cache, plus the replicated output head (tensor parallel)
+        lm_bytes = int(ts[2]["raw"].nbytes)
+        gpu_bytes = (w_bytes - lm_bytes + kv_bytes) / world + lm_bytes if tp else step_bytes
+        model_gbs = gpu_bytes * (K / elapsed) / 1e9   # per GPU
         rl = gemv_roofline(ggc, ctx, torch, stream, peak_gbs)
         dom = rl["Q4_K_11008x4096"]
         tr = traffic_record().get("k_gemv_span<Q4_K> 11008x4096")
@@ -312,10 +340,11 @@ def run_ours(args, rank, world, local_rank):
             cpu = cpu_decode_sample(hp4, ts4, C, steps=4)
         result = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
-            "ms_per_step": elapsed / K * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": elapsed / K * 1e3, "higher_is_better": True, "scaling": "strong" if tp else "weak",
+            "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (seeded Q4_K_M blocks)",
             "config": config_block(args),
-            "e2e": {"value": world * K / e2e_elapsed, "unit": "tokens/s", "h2d_bytes_per_step": 4 + 8,
+            "e2e": {"value": streams * K / e2e_elapsed, "unit": "tokens/s", "h2d_bytes_per_step": 4 + 8,
                     "d2h_bytes_per_step": 4 * hp["vocab_size"] + 4,
                     "api": "ggc_model_forward(1 host token) -> host logits + argmax, per token"},
             "gpu_launches": launches,
@@ -324,8 +353,8 @@ def run_ours(args, rank, world, local_rank):
                          "kernel": "k_gemv_span<Q4_K> 11008x4096 (ffn_up/gate shape), back-to-back launches",
                          "peak_source": peak_src},
             "model_roofline": {"bytes_per_step": step_bytes, "weight_bytes": w_bytes, "kv_bytes": kv_bytes,
-                               "achieved_gbs": model_gbs, "frac": model_gbs / peak_gbs,
-                               "bound_tokens_s": peak_gbs * 1e9 / step_bytes},
+                               "bytes_per_step_per_gpu": gpu_bytes, "achieved_gbs_per_gpu": model_gbs,
+                               "frac": model_gbs / peak_gbs, "bound_tokens_s": peak_gbs * 1e9 / gpu_bytes * streams},
             "matvec": rl,
             "clocks": sampler.record(),
             "cpu_baseline": cpu,

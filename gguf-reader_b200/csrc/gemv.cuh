@@ -624,7 +624,9 @@ struct GemvArgs {
     int kv_f16;
     int* errf;
     int err_slot;           // error-flag slot for EPI_RESID NaN
-    int err_val;            // value written (layer + 1)
+    int err_val;            // value written (layer + 1); 0: no NaN guard in the epilogue
+    int pro_err_slot;       // PRO_RMSNORM: flag slot for a NaN in x (tensor parallel: the
+    int pro_err_val;        //   reduced hidden state), value written; 0: no check
     unsigned long long* argmax_key;
 };
 
@@ -666,7 +668,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, const Seg& sg, 
                 nan |= isnan(acc[r]);
                 sg.out[r0 + r] = __fadd_rn(sg.out[r0 + r], acc[r]);
             }
-            if (nan) atomicCAS(&a.errf[a.err_slot], 0, a.err_val);   // layers run in order: the first NaN layer stays
+            if (nan && a.err_val) atomicCAS(&a.errf[a.err_slot], 0, a.err_val);   // layers run in order: the first NaN layer stays
             break;
         }
         case EPI_LOGITS: {
@@ -861,6 +863,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(const GemvArgs a, cons
             double t = 0.0;
             for (int w = 0; w < GEMV_WARPS; ++w) t += red[w];
             s_scale = (float)sqrt(1.0 / (t / (double)a.xcols + (double)1e-6f));
+            if (a.pro_err_val && isnan(t)) atomicCAS(&a.errf[a.pro_err_slot], 0, a.pro_err_val);   // NaN in x <=> NaN sum
         }
         asm volatile("bar.sync 1, %0;" ::"r"(cthreads) : "memory");
     }

@@ -290,8 +290,12 @@ struct SpanX {
     const float* x2;
     uint32_t xcols;
     int pro;
+    int* errf;
+    int pro_err_slot, pro_err_val;
 };
-__device__ __forceinline__ SpanX span_x_of(const GemvArgs& a) { return SpanX{a.x, a.x2, a.xcols, a.pro}; }
+__device__ __forceinline__ SpanX span_x_of(const GemvArgs& a) {
+    return SpanX{a.x, a.x2, a.xcols, a.pro, a.errf, a.pro_err_slot, a.pro_err_val};
+}
 
 __device__ __forceinline__ float span_xval(const SpanX a, uint32_t e, float scale) {
     if (e >= a.xcols) return 0.f;
@@ -328,6 +332,7 @@ __device__ void span_x_prologue(const SpanX a, uint32_t nct, uint32_t* xl, float
             double t = 0.0;
             for (int w = 0; w < GS_WARPS; ++w) t += red[w];
             *s_scale = (float)sqrt(1.0 / (t / (double)a.xcols + (double)1e-6f));   // ops.rs:262-274
+            if (a.pro_err_val && isnan(t)) atomicCAS(&a.errf[a.pro_err_slot], 0, a.pro_err_val);   // NaN in x <=> NaN sum
         }
         cbar();
         scale = *s_scale;

@@ -821,9 +821,18 @@ __global__ void k_step_begin(StepState* st, const uint32_t* in_tok, const int64_
     }
 }
 
-__global__ void k_step_end(StepState* st, const unsigned long long* argmax_key, uint32_t* out_ids, int* errf) {
+// `nan_vec` (tensor parallel only): the reduced hidden state after the last layer,
+// checked here because the NaN guards of a sharded model run on reduced vectors
+// (the next RMSNorm prologue) and the lm_head GEMV skips prompt tokens.
+__global__ void k_step_end(StepState* st, const unsigned long long* argmax_key, uint32_t* out_ids, int* errf,
+                           const float* nan_vec, uint32_t nan_n, int nan_val) {
     pdl_trigger();
     pdl_wait();
+    if (nan_vec && !st->done) {   // llama.rs:300-307 for the last layer's ffn
+        bool nan = false;
+        for (uint32_t i = threadIdx.x; i < nan_n; i += blockDim.x) nan |= isnan(nan_vec[i]);
+        if (__syncthreads_or(nan) && threadIdx.x == 0) atomicCAS(&errf[ERRF_NAN_FFN], 0, nan_val);
+    }
     if (threadIdx.x != 0 || st->done) return;
     st->slot += 1;   // this step's K/V were appended
     for (int i = 0; i < ERRF_COUNT; ++i)
@@ -892,12 +901,14 @@ struct ModelLayer {
     float* bv = nullptr;
     DevMat wq, wk, wv, wo, up, gate, down;
     DevMat ug;   // ffn_up / ffn_gate rows interleaved (same dtype): one GEMV with the SwiGLU epilogue
+    uint32_t f_l = 0;   // ffn rows held (all of them, or this rank's shard)
 };
 
 struct ggc_model {
     ggc_ctx* ctx = nullptr;
-    ggc_hparams hp{};
-    uint32_t hd = 0, qdim = 0, kvdim = 0, nsplit = 1;
+    ggc_hparams hp{};   // the whole model's
+    uint32_t hd = 0, qdim = 0, kvdim = 0, nsplit = 1;   // qdim / kvdim: this rank's heads x hd
+    uint32_t heads_l = 0, kv_heads_l = 0;                // heads held (all, or this rank's shard)
     int embd_dtype = -1;
     uint8_t* embd = nullptr;
     uint64_t embd_rows = 0;
@@ -982,26 +993,37 @@ int upload_weight(ggc_model* m, const ggc_tensor_desc& t, uint64_t rows, uint64_
 // ffn_up and ffn_gate (llama.rs:547-580).  With one dtype they become one matrix
 // whose rows 2i, 2i+1 are up row i, gate row i, so a row pair of the GEMV yields
 // silu(gate_i) * up_i in its epilogue; otherwise two matrices.
+int upload_rows(ggc_model* m, const ggc_tensor_desc& t, uint64_t total_rows, uint64_t cols,
+                const std::vector<uint32_t>& rows, DevMat& out, const char* what);
+
+// Rows [f0, f0 + fl) of both (all of them, or a tensor-parallel shard).
 int upload_ffn_up_gate(ggc_model* m, const ggc_tensor_desc& up, const ggc_tensor_desc& gate, uint64_t f, uint64_t d,
-                       ModelLayer& ML) {
+                       uint64_t f0, uint64_t fl, ModelLayer& ML) {
     if (!up.data) return set_error(GGC_ERR_MISSING_TENSOR, "MissingTensor { name: ffn_up, kind: tensor }");
     if (!gate.data) return set_error(GGC_ERR_MISSING_TENSOR, "MissingTensor { name: ffn_gate, kind: tensor }");
     if (up.n_elements != f * d) return set_dequant_error(GGC_F32, f * d, up.n_elements, "ffn_up");
     if (gate.n_elements != f * d) return set_dequant_error(GGC_F32, f * d, gate.n_elements, "ffn_gate");
     const int bs = block_size_of(up.dtype), bb = block_bytes_of(up.dtype);
+    ML.f_l = (uint32_t)fl;
     if (up.dtype != gate.dtype || bs < 0 || d % (uint64_t)bs != 0) {
-        GGC_TRY(upload_weight(m, up, f, d, nullptr, ML.up, "ffn_up"));
-        return upload_weight(m, gate, f, d, nullptr, ML.gate, "ffn_gate");
+        if (f0 == 0 && fl == f) {
+            GGC_TRY(upload_weight(m, up, f, d, nullptr, ML.up, "ffn_up"));
+            return upload_weight(m, gate, f, d, nullptr, ML.gate, "ffn_gate");
+        }
+        std::vector<uint32_t> rows(fl);
+        for (uint64_t i = 0; i < fl; ++i) rows[i] = (uint32_t)(f0 + i);
+        GGC_TRY(upload_rows(m, up, f, d, rows, ML.up, "ffn_up"));
+        return upload_rows(m, gate, f, d, rows, ML.gate, "ffn_gate");
     }
     const uint64_t rb = d / bs * (uint64_t)bb;
     if (up.nbytes < f * rb) return set_dequant_error(up.dtype, f * rb, up.nbytes, "ffn_up");
     if (gate.nbytes < f * rb) return set_dequant_error(gate.dtype, f * rb, gate.nbytes, "ffn_gate");
-    std::vector<uint8_t> both(2 * f * rb);
-    for (uint64_t i = 0; i < f; ++i) {
-        memcpy(both.data() + (2 * i) * rb, (const uint8_t*)up.data + i * rb, rb);
-        memcpy(both.data() + (2 * i + 1) * rb, (const uint8_t*)gate.data + i * rb, rb);
+    std::vector<uint8_t> both(2 * fl * rb);
+    for (uint64_t i = 0; i < fl; ++i) {
+        memcpy(both.data() + (2 * i) * rb, (const uint8_t*)up.data + (f0 + i) * rb, rb);
+        memcpy(both.data() + (2 * i + 1) * rb, (const uint8_t*)gate.data + (f0 + i) * rb, rb);
     }
-    return upload_mat(m->ctx, both.data(), both.size(), up.dtype, 2 * f, d, nullptr, ML.ug);
+    return upload_mat(m->ctx, both.data(), both.size(), up.dtype, 2 * fl, d, nullptr, ML.ug);
 }
 
 // RoPE pair order: plane row 2m / 2m+1 = logical rows h hd + j / h hd + j + hd/2
@@ -1044,7 +1066,7 @@ int run_segments(ggc_model* m, std::vector<std::pair<int, Seg>> segs, int pro, c
 int enqueue_step(ggc_model* m) {
     ggc_ctx* ctx = m->ctx;
     const ggc_hparams& hp = m->hp;
-    const uint32_t d = hp.embed_dim, f = hp.ffn_dim;
+    const uint32_t d = hp.embed_dim;
     GGC_CUDA_TRY(launch(ctx, k_step_begin, dim3(1), dim3(32), 0, m->st, (const uint32_t*)m->in_tok,
                         (const int64_t*)m->in_pos, m->argmax_key, m->errf));
     cudaError_t err = cudaSuccess;
@@ -1055,7 +1077,7 @@ int enqueue_step(ggc_model* m) {
                                    m->stream_smem, ctx->stream));
         ctx->launches++;
         GGC_CUDA_TRY(launch(ctx, k_step_end, dim3(1), dim3(32), 0, m->st, (const unsigned long long*)m->argmax_key,
-                            m->out_ids, m->errf));
+                            m->out_ids, m->errf, (const float*)nullptr, 0u, 0));
         return GGC_OK;
     }
     GemvArgs base{};
@@ -1069,16 +1091,33 @@ int enqueue_step(ggc_model* m) {
     base.errf = m->errf;
     base.argmax_key = m->argmax_key;
     const size_t layer_kv = (size_t)hp.max_ctx * m->kvdim * m->kv_elem;
+    // Tensor parallelism: attn_output / ffn_down give partial sums, the residual
+    // added by rank 0 alone, and an all-reduce of the hidden state completes each
+    // block.  The NaN guards (llama.rs:300-307) then run on the reduced vector in
+    // the next RMSNorm prologue (and k_step_end for the last layer), so every rank
+    // takes the same device-side decisions.
+    const bool tp = ctx->world > 1;
+    const int resid_epi = (!tp || ctx->rank == 0) ? EPI_RESID : EPI_STORE;
+    auto allreduce_hidden = [&]() -> int {
+        if (!tp) return GGC_OK;
+        const ncclResult_t r = nccl().AllReduce(m->hidden, m->hidden, d, ncclFloat, ncclSum, ctx->comm, ctx->stream);
+        return r == ncclSuccess ? GGC_OK : nccl_error("ncclAllReduce", r);
+    };
     for (uint32_t l = 0; l < hp.n_layers; ++l) {
         ModelLayer& L = m->layers[l];
         void* kc = (uint8_t*)m->kcache + l * layer_kv;
         void* vc = (uint8_t*)m->vcache + l * layer_kv;
         // attention_block (llama.rs:417-495): rmsnorm -> q/k/v (+bias, RoPE, cache append)
+        GemvArgs rq = base;
+        if (tp && l > 0) {
+            rq.pro_err_slot = ERRF_NAN_FFN;
+            rq.pro_err_val = (int)l;   // layer l - 1
+        }
         GGC_TRY(run_segments(m,
                              {{L.wq.dtype, make_seg(L.wq, EPI_ROPE_Q, m->q, nullptr, L.bq)},
                               {L.wk.dtype, make_seg(L.wk, EPI_ROPE_KC, nullptr, kc, L.bk)},
                               {L.wv.dtype, make_seg(L.wv, EPI_VC, nullptr, vc, L.bv)}},
-                             PRO_RMSNORM, m->hidden, L.attn_norm, L.wq.cols, d, base));
+                             PRO_RMSNORM, m->hidden, L.attn_norm, L.wq.cols, d, rq));
         AttnArgs aa{};
         aa.q = m->q;
         aa.kc = kc;
@@ -1092,8 +1131,8 @@ int enqueue_step(ggc_model* m) {
         aa.slot = &m->st->slot;
         aa.pos = &m->st->pos;
         aa.done = &m->st->done;
-        aa.n_heads = hp.n_heads;
-        aa.kvh = hp.n_kv_heads;
+        aa.n_heads = m->heads_l;
+        aa.kvh = m->kv_heads_l;
         aa.hd = m->hd;
         aa.max_ctx = hp.max_ctx;
         aa.nsplit = m->nsplit;
@@ -1102,43 +1141,50 @@ int enqueue_step(ggc_model* m) {
         aa.psum = m->psum;
         aa.errf = m->errf;
         if (m->attn.kernel) {
-            GGC_CUDA_TRY(launch(ctx, m->attn.kernel, dim3(hp.n_kv_heads, m->nsplit), dim3(FA_THREADS), m->attn.smem, aa));
+            GGC_CUDA_TRY(launch(ctx, m->attn.kernel, dim3(m->kv_heads_l, m->nsplit), dim3(FA_THREADS), m->attn.smem, aa));
         } else {
-            GGC_CUDA_TRY(launch(ctx, k_attn_scores, dim3(hp.n_kv_heads, m->nsplit), dim3(ATTN_WARPS * 32), 0, aa));
-            GGC_CUDA_TRY(launch(ctx, k_attn_av, dim3(hp.n_kv_heads, m->nsplit), dim3(ATTN_WARPS * 32),
+            GGC_CUDA_TRY(launch(ctx, k_attn_scores, dim3(m->kv_heads_l, m->nsplit), dim3(ATTN_WARPS * 32), 0, aa));
+            GGC_CUDA_TRY(launch(ctx, k_attn_av, dim3(m->kv_heads_l, m->nsplit), dim3(ATTN_WARPS * 32),
                                 attn_av_smem(hp.n_heads / hp.n_kv_heads, m->hd), aa));
         }
         // output projection + residual (llama.rs:485, :309-311), NaN guard (:300-307)
         GemvArgs ro = base;
         ro.err_slot = ERRF_NAN_ATTN;
-        ro.err_val = (int)l + 1;
-        GGC_TRY(run_segments(m, {{L.wo.dtype, make_seg(L.wo, EPI_RESID, m->hidden, nullptr, nullptr)}}, PRO_PLAIN, m->o,
+        ro.err_val = tp ? 0 : (int)l + 1;
+        GGC_TRY(run_segments(m, {{L.wo.dtype, make_seg(L.wo, resid_epi, m->hidden, nullptr, nullptr)}}, PRO_PLAIN, m->o,
                              nullptr, L.wo.cols, L.wo.xcols, ro));
+        GGC_TRY(allreduce_hidden());
         // ffn_block (llama.rs:547-580): rmsnorm -> up, gate -> silu(gate)*up -> down + residual
+        GemvArgs ru = base;
+        if (tp) {
+            ru.pro_err_slot = ERRF_NAN_ATTN;
+            ru.pro_err_val = (int)l + 1;
+        }
         GemvArgs rd = base;
         rd.err_slot = ERRF_NAN_FFN;
-        rd.err_val = (int)l + 1;
+        rd.err_val = tp ? 0 : (int)l + 1;
         if (L.ug.base) {   // fused up/gate: h = silu(gate) * up in the epilogue (into ubuf), then down
             GGC_TRY(run_segments(m, {{L.ug.dtype, make_seg(L.ug, EPI_SWIGLU, m->ubuf, nullptr, nullptr)}}, PRO_RMSNORM,
-                                 m->hidden, L.ffn_norm, L.ug.cols, d, base));
-            GGC_TRY(run_segments(m, {{L.down.dtype, make_seg(L.down, EPI_RESID, m->hidden, nullptr, nullptr)}},
-                                 PRO_PLAIN, m->ubuf, nullptr, L.down.cols, f, rd));
+                                 m->hidden, L.ffn_norm, L.ug.cols, d, ru));
+            GGC_TRY(run_segments(m, {{L.down.dtype, make_seg(L.down, resid_epi, m->hidden, nullptr, nullptr)}},
+                                 PRO_PLAIN, m->ubuf, nullptr, L.down.cols, L.f_l, rd));
         } else {
             GGC_TRY(run_segments(m,
                                  {{L.up.dtype, make_seg(L.up, EPI_STORE, m->ubuf, nullptr, nullptr)},
                                   {L.gate.dtype, make_seg(L.gate, EPI_STORE, m->gbuf, nullptr, nullptr)}},
-                                 PRO_RMSNORM, m->hidden, L.ffn_norm, L.up.cols, d, base));
-            GGC_TRY(run_segments(m, {{L.down.dtype, make_seg(L.down, EPI_RESID, m->hidden, nullptr, nullptr)}},
-                                 PRO_SWIGLU, m->gbuf, m->ubuf, L.down.cols, f, rd));
+                                 PRO_RMSNORM, m->hidden, L.ffn_norm, L.up.cols, d, ru));
+            GGC_TRY(run_segments(m, {{L.down.dtype, make_seg(L.down, resid_epi, m->hidden, nullptr, nullptr)}},
+                                 PRO_SWIGLU, m->gbuf, m->ubuf, L.down.cols, L.f_l, rd));
         }
+        GGC_TRY(allreduce_hidden());
     }
     // final norm + lm_head for the last token only (llama.rs:333, :582-616) + greedy argmax
     GemvArgs lh = base;
     lh.st_skip = &m->st->in_idx;   // skip while in_idx < n_in (a prompt token that is not the last)
     GGC_TRY(run_segments(m, {{m->output.dtype, make_seg(m->output, EPI_LOGITS, m->logits, nullptr, nullptr)}},
                          PRO_RMSNORM, m->hidden, m->output_norm, m->output.cols, d, lh));
-    GGC_CUDA_TRY(launch(ctx, k_step_end, dim3(1), dim3(32), 0, m->st, (const unsigned long long*)m->argmax_key,
-                        m->out_ids, m->errf));
+    GGC_CUDA_TRY(launch(ctx, k_step_end, dim3(1), dim3(tp ? 256 : 32), 0, m->st, (const unsigned long long*)m->argmax_key,
+                        m->out_ids, m->errf, tp ? (const float*)m->hidden : nullptr, d, (int)hp.n_layers));
     return GGC_OK;
 }
 
@@ -1151,7 +1197,7 @@ int enqueue_step(ggc_model* m) {
 // shape has no fused kernel.
 int build_stream(ggc_model* m) {
     const char* env = getenv("GGC_DECODE_PATH");
-    if (!env || strcmp(env, "stream") != 0) return GGC_OK;
+    if (!env || strcmp(env, "stream") != 0 || m->ctx->world > 1) return GGC_OK;
     const ggc_hparams& hp = m->hp;
     const uint32_t G = hp.n_heads / hp.n_kv_heads;
     const bool f16 = hp.kv_f16 != 0;
@@ -1336,6 +1382,85 @@ void destroy_model(ggc_model* m) {
 
 }  // namespace
 
+// Megatron shard of one layer for `rank` of `world`: heads and kv heads in equal
+// contiguous ranges, ffn rows in ffn_down blocks with the remainder on the lowest ranks.
+extern "C" int ggc_tp_plan(const ggc_hparams* hp, int wo_dtype, int down_dtype, int rank, int world, ggc_tp_shard* out) {
+    if (!hp || !out) return set_error(GGC_ERR_INVALID_ARG, "null argument");
+    if (world < 1 || rank < 0 || rank >= world) return set_error(GGC_ERR_INVALID_ARG, "rank %d of world %d", rank, world);
+    if (hp->n_heads == 0 || hp->n_kv_heads == 0 || hp->embed_dim % hp->n_heads != 0)
+        return set_error(GGC_ERR_INFERENCE, "unsupported head configuration");
+    if (hp->n_heads % (uint32_t)world != 0 || hp->n_kv_heads % (uint32_t)world != 0)
+        return set_error(GGC_ERR_INVALID_ARG, "tensor parallel: world %d does not divide n_heads %u and n_kv_heads %u",
+                         world, hp->n_heads, hp->n_kv_heads);
+    const int bo = block_size_of(wo_dtype), bd = block_size_of(down_dtype);
+    if (bo < 0) return set_dequant_error(wo_dtype, 0, 0, "attn_output");
+    if (bd < 0) return set_dequant_error(down_dtype, 0, 0, "ffn_down");
+    const uint32_t hd = hp->embed_dim / hp->n_heads, heads = hp->n_heads / (uint32_t)world;
+    if (((uint64_t)heads * hd) % (uint64_t)bo != 0)
+        return set_error(GGC_ERR_INVALID_ARG, "tensor parallel: %u attn_output columns per rank are not whole %d-element blocks",
+                         heads * hd, bo);
+    if (hp->ffn_dim % (uint32_t)bd != 0) return set_shape_error(hp->ffn_dim, bd, "ffn_down columns");
+    const uint64_t units = hp->ffn_dim / (uint64_t)bd, base = units / (uint64_t)world, extra = units % (uint64_t)world;
+    if (base == 0)
+        return set_error(GGC_ERR_INVALID_ARG, "tensor parallel: %llu ffn_down blocks for %d ranks",
+                         (unsigned long long)units, world);
+    const uint64_t r = (uint64_t)rank;
+    out->head0 = (uint32_t)rank * heads;
+    out->heads = heads;
+    out->kv_heads = hp->n_kv_heads / (uint32_t)world;
+    out->kv_head0 = (uint32_t)rank * out->kv_heads;
+    out->ffn0 = (r * base + (r < extra ? r : extra)) * (uint64_t)bd;
+    out->ffn_len = (base + (r < extra ? 1 : 0)) * (uint64_t)bd;
+    return GGC_OK;
+}
+
+namespace {
+
+// Elements [e0, e0 + n) of a vector tensor as a tensor of its own (whole blocks).
+int slice_vec(const ggc_tensor_desc& t, uint64_t e0, uint64_t n, ggc_tensor_desc* out, const char* what) {
+    *out = t;
+    if (!t.data) return GGC_OK;
+    const int bs = block_size_of(t.dtype), bb = block_bytes_of(t.dtype);
+    if (bs < 0) return set_dequant_error(t.dtype, 0, 0, what);
+    if (e0 % (uint64_t)bs || n % (uint64_t)bs) return set_shape_error(n, bs, what);
+    if (t.n_elements < e0 + n || t.nbytes < (e0 + n) / bs * (uint64_t)bb)
+        return set_dequant_error(t.dtype, e0 + n, t.n_elements, what);
+    out->data = (const uint8_t*)t.data + e0 / bs * (uint64_t)bb;
+    out->nbytes = n / bs * (uint64_t)bb;
+    out->n_elements = n;
+    return GGC_OK;
+}
+
+// Columns [c0, c0 + n) of every row of a rows x cols block matrix (whole blocks).
+int slice_cols(const ggc_tensor_desc& t, uint64_t rows, uint64_t cols, uint64_t c0, uint64_t n,
+               std::vector<uint8_t>& out, const char* what) {
+    if (!t.data) return set_error(GGC_ERR_MISSING_TENSOR, "MissingTensor { name: %s, kind: tensor }", what);
+    const int bs = block_size_of(t.dtype), bb = block_bytes_of(t.dtype);
+    if (bs < 0) return set_dequant_error(t.dtype, 0, 0, what);
+    if (t.n_elements != rows * cols) return set_dequant_error(GGC_F32, rows * cols, t.n_elements, what);
+    if (cols % (uint64_t)bs || c0 % (uint64_t)bs || n % (uint64_t)bs) return set_shape_error(cols, bs, what);
+    const uint64_t rb = cols / bs * (uint64_t)bb, ob = n / bs * (uint64_t)bb, off = c0 / bs * (uint64_t)bb;
+    if (t.nbytes < rows * rb) return set_dequant_error(t.dtype, rows * rb, t.nbytes, what);
+    out.resize(rows * ob);
+    for (uint64_t r = 0; r < rows; ++r) memcpy(out.data() + r * ob, (const uint8_t*)t.data + r * rb + off, ob);
+    return GGC_OK;
+}
+
+// Rows `rows` (source indices, in plane order) of a total_rows x cols matrix.
+int upload_rows(ggc_model* m, const ggc_tensor_desc& t, uint64_t total_rows, uint64_t cols,
+                const std::vector<uint32_t>& rows, DevMat& out, const char* what) {
+    if (!t.data) return set_error(GGC_ERR_MISSING_TENSOR, "MissingTensor { name: %s, kind: tensor }", what);
+    if (t.n_elements != total_rows * cols) return set_dequant_error(GGC_F32, total_rows * cols, t.n_elements, what);
+    const int bs = block_size_of(t.dtype), bb = block_bytes_of(t.dtype);
+    if (bs < 0) return set_dequant_error(t.dtype, 0, 0, what);
+    if (cols % (uint64_t)bs) return set_shape_error(cols, bs, what);
+    if (t.nbytes < total_rows * (cols / bs * (uint64_t)bb))
+        return set_dequant_error(t.dtype, total_rows * (cols / bs * (uint64_t)bb), t.nbytes, what);
+    return upload_mat(m->ctx, t.data, t.nbytes, t.dtype, rows.size(), cols, rows.data(), out);
+}
+
+}  // namespace
+
 extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const ggc_tensor_desc* t, uint64_t n_tensors,
                                 ggc_model** out) {
     if (!ctx || !hp_in || !t || !out) return set_error(GGC_ERR_INVALID_ARG, "null argument");
@@ -1345,7 +1470,6 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
                          (unsigned long long)(3 + 12ull * hp.n_layers), (unsigned long long)n_tensors);
     if (hp.n_heads == 0 || hp.n_kv_heads == 0 || hp.embed_dim % hp.n_heads != 0 || hp.n_heads % hp.n_kv_heads != 0)
         return set_error(GGC_ERR_INFERENCE, "unsupported head configuration");
-    if (ctx->world > 1) return set_error(GGC_ERR_INVALID_ARG, "tensor-parallel model: use ggc_model_create on a TP context (not yet built)");
     const uint32_t hd = hp.embed_dim / hp.n_heads;
     if (hd % 2 != 0 || hd > 256 || hp.n_heads / hp.n_kv_heads > ATTN_MAX_G)
         return set_error(GGC_ERR_INFERENCE, "head_dim %u / GQA group %u not supported", hd, hp.n_heads / hp.n_kv_heads);
@@ -1357,8 +1481,14 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
     ctx->refs++;   // released by destroy_model
     m->hp = hp;
     m->hd = hd;
-    m->qdim = hp.n_heads * hd;
-    m->kvdim = hp.n_kv_heads * hd;
+    const int world = ctx->world;
+    m->heads_l = hp.n_heads / (uint32_t)world;
+    m->kv_heads_l = hp.n_kv_heads / (uint32_t)world;
+    if (world > 1 && (hp.n_heads % (uint32_t)world || hp.n_kv_heads % (uint32_t)world))
+        return set_error(GGC_ERR_INVALID_ARG, "tensor parallel: world %d does not divide n_heads %u and n_kv_heads %u",
+                         world, hp.n_heads, hp.n_kv_heads);
+    m->qdim = m->heads_l * hd;
+    m->kvdim = m->kv_heads_l * hd;
     m->kv_elem = hp.kv_f16 ? 2 : 4;
     const uint32_t d = hp.embed_dim, f = hp.ffn_dim;
     // token_embd: kept raw, one row dequantised per token
@@ -1384,17 +1514,51 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
         ModelLayer& ML = m->layers[l];
         GGC_TRY(upload_vec(m.get(), L[0], d, &ML.attn_norm, "attn_norm"));
         if (!ML.attn_norm) return set_error(GGC_ERR_MISSING_TENSOR, "MissingTensor { name: blk.%u.attn_norm, kind: tensor }", l);
-        GGC_TRY(upload_weight(m.get(), L[1], m->qdim, d, qorder.data(), ML.wq, "attn_q"));
-        GGC_TRY(upload_vec(m.get(), L[2], m->qdim, &ML.bq, "attn_q.bias"));
-        GGC_TRY(upload_weight(m.get(), L[3], m->kvdim, d, korder.data(), ML.wk, "attn_k"));
-        GGC_TRY(upload_vec(m.get(), L[4], m->kvdim, &ML.bk, "attn_k.bias"));
-        GGC_TRY(upload_weight(m.get(), L[5], m->kvdim, d, nullptr, ML.wv, "attn_v"));
-        GGC_TRY(upload_vec(m.get(), L[6], m->kvdim, &ML.bv, "attn_v.bias"));
-        GGC_TRY(upload_weight(m.get(), L[7], d, m->qdim, nullptr, ML.wo, "attn_output"));
+        if (world == 1) {
+            GGC_TRY(upload_weight(m.get(), L[1], m->qdim, d, qorder.data(), ML.wq, "attn_q"));
+            GGC_TRY(upload_vec(m.get(), L[2], m->qdim, &ML.bq, "attn_q.bias"));
+            GGC_TRY(upload_weight(m.get(), L[3], m->kvdim, d, korder.data(), ML.wk, "attn_k"));
+            GGC_TRY(upload_vec(m.get(), L[4], m->kvdim, &ML.bk, "attn_k.bias"));
+            GGC_TRY(upload_weight(m.get(), L[5], m->kvdim, d, nullptr, ML.wv, "attn_v"));
+            GGC_TRY(upload_vec(m.get(), L[6], m->kvdim, &ML.bv, "attn_v.bias"));
+            GGC_TRY(upload_weight(m.get(), L[7], d, m->qdim, nullptr, ML.wo, "attn_output"));
+            GGC_TRY(upload_vec(m.get(), L[8], d, &ML.ffn_norm, "ffn_norm"));
+            if (!ML.ffn_norm)
+                return set_error(GGC_ERR_MISSING_TENSOR, "MissingTensor { name: blk.%u.ffn_norm, kind: tensor }", l);
+            GGC_TRY(upload_ffn_up_gate(m.get(), L[9], L[10], f, d, 0, f, ML));
+            GGC_TRY(upload_weight(m.get(), L[11], d, f, nullptr, ML.down, "ffn_down"));
+            continue;
+        }
+        // tensor-parallel shard (ggc_tp_plan): q/k/v rows and up/gate rows of this
+        // rank, attn_output / ffn_down columns to match (partial sums, all-reduced)
+        if (!L[7].data) return set_error(GGC_ERR_MISSING_TENSOR, "MissingTensor { name: attn_output, kind: tensor }");
+        if (!L[11].data) return set_error(GGC_ERR_MISSING_TENSOR, "MissingTensor { name: ffn_down, kind: tensor }");
+        ggc_tp_shard sh{};
+        GGC_TRY(ggc_tp_plan(&hp, L[7].dtype, L[11].dtype, ctx->rank, world, &sh));
+        const uint32_t qfull = hp.n_heads * hd, kvfull = hp.n_kv_heads * hd;
+        std::vector<uint32_t> qrows = rope_row_order(sh.heads, hd), krows = rope_row_order(sh.kv_heads, hd);
+        std::vector<uint32_t> vrows(m->kvdim);
+        for (auto& r : qrows) r += sh.head0 * hd;
+        for (auto& r : krows) r += sh.kv_head0 * hd;
+        for (uint32_t i = 0; i < m->kvdim; ++i) vrows[i] = sh.kv_head0 * hd + i;
+        ggc_tensor_desc b{};
+        GGC_TRY(upload_rows(m.get(), L[1], qfull, d, qrows, ML.wq, "attn_q"));
+        GGC_TRY(slice_vec(L[2], (uint64_t)sh.head0 * hd, m->qdim, &b, "attn_q.bias"));
+        GGC_TRY(upload_vec(m.get(), b, m->qdim, &ML.bq, "attn_q.bias"));
+        GGC_TRY(upload_rows(m.get(), L[3], kvfull, d, krows, ML.wk, "attn_k"));
+        GGC_TRY(slice_vec(L[4], (uint64_t)sh.kv_head0 * hd, m->kvdim, &b, "attn_k.bias"));
+        GGC_TRY(upload_vec(m.get(), b, m->kvdim, &ML.bk, "attn_k.bias"));
+        GGC_TRY(upload_rows(m.get(), L[5], kvfull, d, vrows, ML.wv, "attn_v"));
+        GGC_TRY(slice_vec(L[6], (uint64_t)sh.kv_head0 * hd, m->kvdim, &b, "attn_v.bias"));
+        GGC_TRY(upload_vec(m.get(), b, m->kvdim, &ML.bv, "attn_v.bias"));
+        std::vector<uint8_t> cols;
+        GGC_TRY(slice_cols(L[7], d, qfull, (uint64_t)sh.head0 * hd, m->qdim, cols, "attn_output"));
+        GGC_TRY(upload_mat(ctx, cols.data(), cols.size(), L[7].dtype, d, m->qdim, nullptr, ML.wo));
         GGC_TRY(upload_vec(m.get(), L[8], d, &ML.ffn_norm, "ffn_norm"));
         if (!ML.ffn_norm) return set_error(GGC_ERR_MISSING_TENSOR, "MissingTensor { name: blk.%u.ffn_norm, kind: tensor }", l);
-        GGC_TRY(upload_ffn_up_gate(m.get(), L[9], L[10], f, d, ML));
-        GGC_TRY(upload_weight(m.get(), L[11], d, f, nullptr, ML.down, "ffn_down"));
+        GGC_TRY(upload_ffn_up_gate(m.get(), L[9], L[10], f, d, sh.ffn0, sh.ffn_len, ML));
+        GGC_TRY(slice_cols(L[11], d, f, sh.ffn0, sh.ffn_len, cols, "ffn_down"));
+        GGC_TRY(upload_mat(ctx, cols.data(), cols.size(), L[11].dtype, d, sh.ffn_len, nullptr, ML.down));
     }
     // KV cache resident in HBM, head-major: [layer][n_kv][max_ctx][hd]
     const size_t kv_bytes = (size_t)hp.n_layers * hp.max_ctx * m->kvdim * m->kv_elem;
@@ -1417,10 +1581,10 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
     // fused attention: two resident CTAs per SM over (kv head, split); general pair: ~2 per SM, <= 64 splits
     m->attn = attn_decode_sel(hd, hp.kv_f16 != 0, hp.n_heads / hp.n_kv_heads);
     if (m->attn.kernel) {
-        const uint32_t ns = (uint32_t)ctx->num_sms * 2 / hp.n_kv_heads;
+        const uint32_t ns = (uint32_t)ctx->num_sms * 2 / m->kv_heads_l;
         m->nsplit = ns < 1 ? 1 : ns;
     } else {
-        const uint32_t ns = cdiv<uint32_t>((uint32_t)ctx->num_sms * 2, hp.n_kv_heads);
+        const uint32_t ns = cdiv<uint32_t>((uint32_t)ctx->num_sms * 2, m->kv_heads_l);
         m->nsplit = ns < 1 ? 1 : (ns > 64 ? 64 : ns);
     }
     GGC_TRY(dalloc(m.get(), &m->hidden, d));
@@ -1429,12 +1593,12 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
     GGC_TRY(dalloc(m.get(), &m->ubuf, f));
     GGC_TRY(dalloc(m.get(), &m->gbuf, f));
     GGC_TRY(dalloc(m.get(), &m->logits, hp.vocab_size));
-    GGC_TRY(dalloc(m.get(), &m->scores, (size_t)hp.n_heads * hp.max_ctx));
-    GGC_TRY(dalloc(m.get(), &m->pmax, (size_t)hp.n_heads * m->nsplit));
-    GGC_TRY(dalloc(m.get(), &m->psum, (size_t)hp.n_heads * m->nsplit));
-    GGC_TRY(dalloc(m.get(), &m->stats, hp.n_heads));
+    GGC_TRY(dalloc(m.get(), &m->scores, (size_t)m->heads_l * hp.max_ctx));
+    GGC_TRY(dalloc(m.get(), &m->pmax, (size_t)m->heads_l * m->nsplit));
+    GGC_TRY(dalloc(m.get(), &m->psum, (size_t)m->heads_l * m->nsplit));
+    GGC_TRY(dalloc(m.get(), &m->stats, m->heads_l));
     GGC_TRY(dalloc(m.get(), &m->opart, (size_t)m->nsplit * m->qdim));
-    GGC_TRY(dalloc(m.get(), &m->tickets, 2 * hp.n_kv_heads));
+    GGC_TRY(dalloc(m.get(), &m->tickets, 2 * m->kv_heads_l));
     GGC_TRY(dalloc(m.get(), &m->argmax_key, 1));
     GGC_TRY(dalloc(m.get(), &m->errf, ERRF_COUNT));
     GGC_TRY(dalloc(m.get(), &m->st, 1));
@@ -1482,7 +1646,9 @@ int check_run(ggc_model* m) {
     m->cache_len = m->rb->st.slot;
     int status = GGC_OK;
     if (e[ERRF_EMBED_OOB]) status = set_error(GGC_ERR_INFERENCE, "embed out of bounds: tok=%d", e[ERRF_EMBED_OOB] - 1);
-    else if (e[ERRF_NAN_ATTN]) status = set_error(GGC_ERR_INFERENCE, "NaN after layer %d attention", e[ERRF_NAN_ATTN] - 1);
+    // the earliest NaN site: attention of layer l runs before the ffn of layer l
+    else if (e[ERRF_NAN_ATTN] && (!e[ERRF_NAN_FFN] || e[ERRF_NAN_ATTN] <= e[ERRF_NAN_FFN]))
+        status = set_error(GGC_ERR_INFERENCE, "NaN after layer %d attention", e[ERRF_NAN_ATTN] - 1);
     else if (e[ERRF_NAN_FFN]) status = set_error(GGC_ERR_INFERENCE, "NaN after layer %d ffn", e[ERRF_NAN_FFN] - 1);
     else if (e[ERRF_NAN_LOGITS]) status = set_error(GGC_ERR_INFERENCE, "NaN in logits");
     else if (e[ERRF_KV_OVERFLOW]) {
@@ -1619,14 +1785,14 @@ namespace {
 // into / out of the head-major cache rows [h][base .. base + seq) of one layer.
 int kv_rows_to_cache(ggc_model* m, uint8_t* layer, const void* src, uint64_t base, uint64_t seq, size_t esz) {
     const size_t hd = m->hd, kvdim = m->kvdim;
-    for (uint32_t h = 0; h < m->hp.n_kv_heads; ++h)
+    for (uint32_t h = 0; h < m->kv_heads_l; ++h)
         GGC_CUDA_TRY(cudaMemcpy2D(layer + ((size_t)h * m->hp.max_ctx + base) * hd * esz, hd * esz,
                                   (const uint8_t*)src + h * hd * esz, kvdim * esz, hd * esz, seq, cudaMemcpyDefault));
     return GGC_OK;
 }
 int kv_cache_to_rows(ggc_model* m, const uint8_t* layer, void* dst, uint64_t seq, size_t esz) {
     const size_t hd = m->hd, kvdim = m->kvdim;
-    for (uint32_t h = 0; h < m->hp.n_kv_heads; ++h)
+    for (uint32_t h = 0; h < m->kv_heads_l; ++h)
         GGC_CUDA_TRY(cudaMemcpy2D((uint8_t*)dst + h * hd * esz, kvdim * esz, layer + (size_t)h * m->hp.max_ctx * hd * esz,
                                   hd * esz, hd * esz, seq, cudaMemcpyDefault));
     return GGC_OK;

@@ -39,6 +39,11 @@ class HParams(C.Structure):
                 ("rope_freq_base", C.c_double), ("max_ctx", C.c_uint32), ("kv_f16", C.c_uint32)]
 
 
+class TpShard(C.Structure):
+    _fields_ = [("head0", C.c_uint32), ("heads", C.c_uint32), ("kv_head0", C.c_uint32), ("kv_heads", C.c_uint32),
+                ("ffn0", C.c_uint64), ("ffn_len", C.c_uint64)]
+
+
 class TensorDesc(C.Structure):
     _fields_ = [("data", C.c_void_p), ("nbytes", C.c_uint64), ("dtype", C.c_int), ("n_elements", C.c_uint64)]
 
@@ -133,6 +138,7 @@ SIGNATURES = {
     "ggc_tensor_matvec_batch": (_i32, [_vp, C.POINTER(_vp), _u64, _vp, _vp]),
     "ggc_tensor_dequantize": (_i32, [_vp, _vp, _vp]),
     "ggc_infer_k_quant_dtype": (_i32, [_u64, _u64, _i32]),
+    "ggc_tp_plan": (_i32, [C.POINTER(HParams), _i32, _i32, _i32, _i32, C.POINTER(TpShard)]),
     "ggc_model_create": (_i32, [_vp, C.POINTER(HParams), C.POINTER(TensorDesc), _u64, C.POINTER(_vp)]),
     "ggc_model_destroy": (_i32, [_vp]),
     "ggc_model_forward": (_i32, [_vp, _vp, _vp, _u64, _vp, _vp]),

@@ -48,6 +48,8 @@ class Context:
             check(lib().ggc_ctx_create(device, C.byref(h)))
         self.h = h
         self.device = device
+        self.rank = rank
+        self.world = world
 
     @staticmethod
     def nccl_unique_id() -> bytes:
@@ -180,6 +182,20 @@ class Tensor:
             pass
 
 
+def _hparams(hp: dict, max_ctx: int = 0, kv_f16: bool = False):
+    return L.HParams(hp["vocab_size"], hp["embed_dim"], hp["n_heads"], hp["n_kv_heads"], hp["ffn_dim"],
+                     hp["n_layers"], float(hp["rope_freq_base"]), max_ctx, 1 if kv_f16 else 0)
+
+
+def tp_plan(hp: dict, attn_output_dtype: int, ffn_down_dtype: int, rank: int, world: int) -> dict:
+    """The tensor-parallel shard of one layer kept by `rank` of `world` (ggc_tp_plan):
+    q heads, kv heads and ffn rows as (first, count) pairs."""
+    out = L.TpShard()
+    check(lib().ggc_tp_plan(C.byref(_hparams(hp)), attn_output_dtype, ffn_down_dtype, rank, world, C.byref(out)))
+    return {"heads": (out.head0, out.heads), "kv_heads": (out.kv_head0, out.kv_heads),
+            "ffn": (out.ffn0, out.ffn_len)}
+
+
 # ---- model/llama.rs ------------------------------------------------------------
 class LlamaModel:
     """LlamaModel over tensors given in role order (see synth.TENSOR_ROLES)."""
@@ -196,13 +212,13 @@ class LlamaModel:
             raw = _as_bytes(t["raw"])
             keep.append(raw)
             descs[i] = L.TensorDesc(raw.ctypes.data, raw.nbytes, t["dtype"], t["n_elements"])
-        self.hp = L.HParams(hp["vocab_size"], hp["embed_dim"], hp["n_heads"], hp["n_kv_heads"], hp["ffn_dim"],
-                            hp["n_layers"], float(hp["rope_freq_base"]), max_ctx, 1 if kv_f16 else 0)
+        self.hp = _hparams(hp, max_ctx, kv_f16)
         h = C.c_void_p()
         check(lib().ggc_model_create(self.ctx.h, C.byref(self.hp), descs, len(tensors), C.byref(h)))
         self.h = h
         self.vocab = hp["vocab_size"]
-        self.kv_dim = hp["n_kv_heads"] * (hp["embed_dim"] // hp["n_heads"])
+        # cache rows hold this rank's kv heads under tensor parallelism
+        self.kv_dim = hp["n_kv_heads"] // self.ctx.world * (hp["embed_dim"] // hp["n_heads"])
 
     def forward(self, tokens, positions, logits=None, want_logits=True):
         """LlamaModel::forward: logits (vocab f32) of the last token; appends K/V."""

@@ -156,6 +156,26 @@ typedef struct ggc_tensor_desc {
     uint64_t n_elements;
 } ggc_tensor_desc;
 
+/* Tensor parallelism: the shard a rank keeps of one layer (Megatron split).
+ *   q heads [head0, head0 + heads): rows of attn_q (+ bias), columns of attn_output;
+ *   kv heads [kv_head0, kv_head0 + kv_heads): rows of attn_k / attn_v (+ biases) and
+ *     the rank's KV cache;
+ *   ffn rows [ffn0, ffn0 + ffn_len) of ffn_up / ffn_gate = columns of ffn_down, split
+ *     on ffn_down's block boundaries, the remainder going to the lowest ranks
+ *     (Llama-2's 43 super-blocks over 2 ranks: 22 + 21).
+ * token_embd, the norms and output are replicated; each rank's attn_output and
+ * ffn_down products are partial sums that an NCCL all-reduce adds up.  Errors:
+ * InvalidArg when world does not divide n_heads and n_kv_heads, when a rank's
+ * attn_output columns are not whole blocks, or when there are fewer ffn blocks
+ * than ranks. */
+typedef struct ggc_tp_shard {
+    uint32_t head0, heads;
+    uint32_t kv_head0, kv_heads;
+    uint64_t ffn0, ffn_len;
+} ggc_tp_shard;
+int ggc_tp_plan(const ggc_hparams* hp, int attn_output_dtype, int ffn_down_dtype, int rank, int world,
+                ggc_tp_shard* out);
+
 /* Tensors in role order: token_embd, output_norm, output, then per layer
  * attn_norm, attn_q, attn_q.bias, attn_k, attn_k.bias, attn_v, attn_v.bias,
  * attn_output, ffn_norm, ffn_up, ffn_gate, ffn_down  (3 + 12 * n_layers entries;

@@ -1,0 +1,141 @@
+"""Tensor-parallel decode on 2 GPUs (one process per GPU, NCCL) against the oracle.
+
+Every rank makes the same calls; the model shards q/k/v/up/gate rows and
+attn_output/ffn_down columns (ggc_tp_plan) and all-reduces the hidden state
+after each of the two.  Logits within 1e-4 relative L2 of the oracle, identical
+on every rank, and greedy ids identical for 32 tokens.  Skipped with fewer
+than two GPUs.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+from gguf_cuda import synth
+
+REL_L2 = 1e-4
+WORLD = 2
+
+MINI = dict(vocab_size=1000, embed_dim=512, n_heads=8, n_kv_heads=2, ffn_dim=1024, n_layers=2, rope_freq_base=1e4,
+            qkv_bias=True, weights="q4_k_m")
+CASES = [
+    ("mini-q4_k_m", MINI, None, None),
+    ("mini-f32-bias", dict(MINI, weights=0), None, None),
+    ("llama2-7b-q4_k_m-2layers", "llama2-7b-q4_k_m", 2, None),     # ffn 43 super-blocks: 22 + 21
+    ("llama3-8b-q4_0-1layer", "llama3-8b-q4_0", 1, 32000),
+]
+
+
+def rel_l2(got, want):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    return float(np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-30))
+
+
+def _need_gpus():
+    import torch
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip(f"needs {WORLD} GPUs")
+
+
+def _worker(rank, world, nid, job, q):
+    """One rank: build the sharded model and run `job` (same calls on every rank)."""
+    try:
+        import torch  # noqa: F401  -- loads the NCCL the parent's unique id came from
+        import gguf_cuda as ggc
+        ctx = ggc.Context(device=rank, rank=rank, world=world, nccl_id=nid)
+        q.put((rank, job(ggc, ctx)))
+    except Exception as e:   # reported to the parent (as text: the library's errors do not pickle)
+        q.put((rank, RuntimeError(f"rank {rank}: {type(e).__name__}: {e}")))
+
+
+def run_ranks(job, timeout=600):
+    import multiprocessing as mp
+    import torch  # noqa: F401  -- the library binds the NCCL already loaded (PyTorch's)
+    import gguf_cuda as ggc
+    nid = ggc.Context.nccl_unique_id()
+    mctx = mp.get_context("spawn")
+    q = mctx.Queue()
+    procs = [mctx.Process(target=_worker, args=(r, WORLD, nid, job, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    try:
+        res = dict(q.get(timeout=timeout) for _ in procs)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    return [res[r] for r in range(WORLD)]
+
+
+class PromptJob:
+    def __init__(self, cfg, n_layers, vocab, seed=0):
+        self.cfg, self.n_layers, self.vocab, self.seed = cfg, n_layers, vocab, seed
+
+    def __call__(self, ggc, ctx):
+        hp, ts = synth.make_model(self.cfg, n_layers=self.n_layers, seed=self.seed, vocab_size=self.vocab)
+        m = ggc.LlamaModel(hp, ts, max_ctx=256, ctx=ctx)
+        prompt = np.random.default_rng(5).integers(0, hp["vocab_size"], size=8).astype(np.uint32)
+        logits = m.forward(prompt, np.arange(8, dtype=np.int64))
+        k, v = m.cache_read(0)
+        step = m.forward([int(prompt[0])], [8])
+        m.reset_cache()
+        ids = m.generate_greedy(np.random.default_rng(9).integers(0, hp["vocab_size"], size=6), 32)
+        return dict(logits=logits, k=k, v=v, step=step, ids=ids, cache_len=m.cache_len())
+
+
+@pytest.mark.parametrize("name,cfg,n_layers,vocab", CASES, ids=[c[0] for c in CASES])
+def test_tp2_matches_oracle(ggc, orc, name, cfg, n_layers, vocab):
+    _need_gpus()
+    res = run_ranks(PromptJob(cfg, n_layers, vocab))
+    for r in res:
+        if isinstance(r, Exception):
+            raise r
+    hp, ts = synth.make_model(cfg, n_layers=n_layers, seed=0, vocab_size=vocab)
+    o = orc.Model(hp, ts)
+    prompt = np.random.default_rng(5).integers(0, hp["vocab_size"], size=8).astype(np.uint32)
+    want = o.forward(prompt, np.arange(8, dtype=np.int64))
+    ko, vo = o.cache_read(0)
+    want_step = o.forward([int(prompt[0])], [8])
+    o.reset_cache()
+    want_ids = o.generate_greedy(np.random.default_rng(9).integers(0, hp["vocab_size"], size=6).astype(np.uint32), 32)
+    hd = hp["embed_dim"] // hp["n_heads"]
+    kvw = hp["n_kv_heads"] * hd
+    for rank, r in enumerate(res):
+        assert rel_l2(r["logits"], want) <= REL_L2, (rank, rel_l2(r["logits"], want))
+        assert rel_l2(r["step"], want_step) <= REL_L2
+        assert r["ids"] == want_ids
+        assert r["cache_len"] == 6 + 32
+        # the rank's cache holds its own kv heads
+        p = ggc.tp_plan(hp, ts[3 + 7]["dtype"], ts[3 + 11]["dtype"], rank, WORLD)
+        h0, nh = p["kv_heads"]
+        sl = slice(h0 * hd, (h0 + nh) * hd)
+        assert rel_l2(r["k"], ko.reshape(-1, kvw)[:, sl].ravel()) <= REL_L2
+        assert rel_l2(r["v"], vo.reshape(-1, kvw)[:, sl].ravel()) <= REL_L2
+    # replicated lm_head over the same reduced hidden state: identical on every rank
+    assert np.array_equal(res[0]["logits"], res[1]["logits"])
+
+
+class NanJob:
+    """NaN planted in the attn_output columns that only rank 1 holds."""
+
+    def __call__(self, ggc, ctx):
+        hp, ts = synth.make_model(dict(MINI, weights=0, qkv_bias=False), seed=2)
+        wo = ts[3 + 7]
+        w = wo["raw"].view(np.float32).copy().reshape(hp["embed_dim"], hp["embed_dim"])
+        w[:, hp["embed_dim"] // 2:] = np.nan
+        ts[3 + 7] = dict(wo, raw=w.ravel().view(np.uint8))
+        m = ggc.LlamaModel(hp, ts, max_ctx=8, ctx=ctx)
+        try:
+            m.forward([1], [0])
+        except ggc.InferenceError as e:
+            return str(e)
+        return None
+
+
+def test_tp2_nan_guard_same_on_every_rank(ggc):
+    _need_gpus()
+    res = run_ranks(NanJob())
+    for r in res:
+        assert isinstance(r, str) and "NaN after layer 0 attention" in r, r
