@@ -21,6 +21,7 @@
 #include "common.cuh"
 #include "planes.cuh"
 #include "mbarrier.cuh"
+#include "allreduce.cuh"
 
 namespace ggc {
 
@@ -586,7 +587,8 @@ enum EpiKind : int {
     EPI_VC = 3,         // out = acc + bias written into the V cache row
     EPI_RESID = 4,      // out[r] += acc, NaN -> error flag
     EPI_LOGITS = 5,     // out[r] = acc and greedy argmax into a 64-bit key
-    EPI_SWIGLU = 6      // rows (2i, 2i+1) = (ffn_up_i, ffn_gate_i): out[i] = silu(gate_i) * up_i
+    EPI_SWIGLU = 6,     // rows (2i, 2i+1) = (ffn_up_i, ffn_gate_i): out[i] = silu(gate_i) * up_i
+    EPI_AR = 7          // tensor parallel: partial rows to every rank, summed into out (allreduce.cuh)
 };
 
 // silu(g) * u as the reference computes it (ops.rs:237-247, llama.rs:564-567).
@@ -627,6 +629,8 @@ struct GemvArgs {
     int err_val;            // value written (layer + 1); 0: no NaN guard in the epilogue
     int pro_err_slot;       // PRO_RMSNORM: flag slot for a NaN in x (tensor parallel: the
     int pro_err_val;        //   reduced hidden state), value written; 0: no check
+    const ArGroup* ar;      // EPI_AR: the rank group (one segment only)
+    uint32_t ar_k;          // EPI_AR: 1-based index of this all-reduce inside a step
     unsigned long long* argmax_key;
 };
 
@@ -658,6 +662,9 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, const Seg& sg, 
     switch (sg.epi) {
         case EPI_STORE:
             for (uint32_t r = 0; r < nvalid; ++r) sg.out[r0 + r] = sg.bias ? __fadd_rn(acc[r], sg.bias[r0 + r]) : acc[r];
+            break;
+        case EPI_AR:
+            ar_store_rows(*a.ar, a.ar_k, sg.out, r0, nvalid, acc);
             break;
         case EPI_SWIGLU:   // r0 even, both rows valid (the fused matrix has 2 f rows)
             if (nvalid == 2) sg.out[r0 >> 1] = ffn_silu_mul(acc[1], acc[0]);
@@ -1059,6 +1066,10 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(const GemvArgs a, cons
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
+    if (a.ar_k)   // tensor parallel: row `warp` of each of the CTA's row blocks, summed over the ranks
+        ar_reduce_rows(
+            a.ar, a.ar_k, rb1 - rb0, [&](uint32_t j) { return (rb0 + j) * TILE_ROWS + (uint32_t)warp; },
+            sseg[0].m.L.rows, sseg[0].out, a.errf, a.err_slot, a.err_val);
 }
 
 // Host: stage layout of a launch over weights of `pcols` columns.

@@ -614,6 +614,10 @@ __global__ void __launch_bounds__(GS_THREADS, 1) k_gemv_span(const GemvArgs a, c
         if (nan_logit) atomicMax(&a.errf[ERRF_NAN_LOGITS], 1);
         atomicMax(a.argmax_key, best);
     }
+    if (a.ar_k)   // tensor parallel: this warp's row pair of each row block, summed over the ranks
+        ar_reduce_rows(
+            a.ar, a.ar_k, 2 * nrb, [&](uint32_t j) { return (rb0 + j / 2) * TILE_ROWS + (uint32_t)r0 + (j & 1); },
+            sseg[0].m.L.rows, sseg[0].out, a.errf, a.err_slot, a.err_val);
 }
 
 }  // namespace ggc

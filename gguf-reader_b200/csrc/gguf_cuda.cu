@@ -16,6 +16,7 @@
 #include <vector>
 
 #include <dlfcn.h>
+#include <unistd.h>
 #include <nccl.h>
 
 #include "common.cuh"
@@ -793,6 +794,7 @@ struct StepState {
     int64_t next_pos;
     uint32_t next_tok;
     uint32_t max_ctx;
+    uint32_t ar_step;   // replays of the step graph (the epoch base of the fused all-reduce)
 };
 }  // namespace ggc
 
@@ -802,7 +804,9 @@ __global__ void k_step_begin(StepState* st, const uint32_t* in_tok, const int64_
                              unsigned long long* argmax_key, int* errf) {
     pdl_trigger();
     pdl_wait();
-    if (threadIdx.x != 0 || st->done) return;
+    if (threadIdx.x != 0) return;
+    st->ar_step += 1;   // every replay, on every rank alike
+    if (st->done) return;
     if (st->in_idx < st->n_in) {
         st->tok = in_tok[st->in_idx];
         st->pos = in_pos[st->in_idx];
@@ -943,6 +947,10 @@ struct ggc_model {
         int errf[ERRF_COUNT];
         unsigned long long key;
     }* rb = nullptr;
+    // tensor parallel: the fused all-reduce over peer memory (allreduce.cuh), else NCCL
+    bool ar_p2p = false;
+    ArGroup* ar = nullptr;                 // device copy
+    std::vector<void*> ar_peer_maps;       // IPC mappings of the other ranks' buffers
     cudaGraphExec_t graph = nullptr;
     uint64_t launches_per_step = 0;
     uint64_t cache_len = 0;
@@ -1096,10 +1104,13 @@ int enqueue_step(ggc_model* m) {
     // block.  The NaN guards (llama.rs:300-307) then run on the reduced vector in
     // the next RMSNorm prologue (and k_step_end for the last layer), so every rank
     // takes the same device-side decisions.
-    const bool tp = ctx->world > 1;
-    const int resid_epi = (!tp || ctx->rank == 0) ? EPI_RESID : EPI_STORE;
+    // With the fused all-reduce (m->ar_p2p) the two row-parallel GEMVs push their
+    // partials to every rank and sum them into the hidden state themselves
+    // (EPI_AR), their NaN guard included; the prologue guards serve the NCCL path.
+    const bool tp = ctx->world > 1, p2p = tp && m->ar_p2p, nccl_tp = tp && !p2p;
+    const int resid_epi = p2p ? EPI_AR : ((!tp || ctx->rank == 0) ? EPI_RESID : EPI_STORE);
     auto allreduce_hidden = [&]() -> int {
-        if (!tp) return GGC_OK;
+        if (!nccl_tp) return GGC_OK;
         const ncclResult_t r = nccl().AllReduce(m->hidden, m->hidden, d, ncclFloat, ncclSum, ctx->comm, ctx->stream);
         return r == ncclSuccess ? GGC_OK : nccl_error("ncclAllReduce", r);
     };
@@ -1109,7 +1120,7 @@ int enqueue_step(ggc_model* m) {
         void* vc = (uint8_t*)m->vcache + l * layer_kv;
         // attention_block (llama.rs:417-495): rmsnorm -> q/k/v (+bias, RoPE, cache append)
         GemvArgs rq = base;
-        if (tp && l > 0) {
+        if (nccl_tp && l > 0) {
             rq.pro_err_slot = ERRF_NAN_FFN;
             rq.pro_err_val = (int)l;   // layer l - 1
         }
@@ -1150,19 +1161,27 @@ int enqueue_step(ggc_model* m) {
         // output projection + residual (llama.rs:485, :309-311), NaN guard (:300-307)
         GemvArgs ro = base;
         ro.err_slot = ERRF_NAN_ATTN;
-        ro.err_val = tp ? 0 : (int)l + 1;
+        ro.err_val = nccl_tp ? 0 : (int)l + 1;
+        if (p2p) {
+            ro.ar = m->ar;
+            ro.ar_k = 2 * l + 1;
+        }
         GGC_TRY(run_segments(m, {{L.wo.dtype, make_seg(L.wo, resid_epi, m->hidden, nullptr, nullptr)}}, PRO_PLAIN, m->o,
                              nullptr, L.wo.cols, L.wo.xcols, ro));
         GGC_TRY(allreduce_hidden());
         // ffn_block (llama.rs:547-580): rmsnorm -> up, gate -> silu(gate)*up -> down + residual
         GemvArgs ru = base;
-        if (tp) {
+        if (nccl_tp) {
             ru.pro_err_slot = ERRF_NAN_ATTN;
             ru.pro_err_val = (int)l + 1;
         }
         GemvArgs rd = base;
         rd.err_slot = ERRF_NAN_FFN;
-        rd.err_val = tp ? 0 : (int)l + 1;
+        rd.err_val = nccl_tp ? 0 : (int)l + 1;
+        if (p2p) {
+            rd.ar = m->ar;
+            rd.ar_k = 2 * l + 2;
+        }
         if (L.ug.base) {   // fused up/gate: h = silu(gate) * up in the epilogue (into ubuf), then down
             GGC_TRY(run_segments(m, {{L.ug.dtype, make_seg(L.ug, EPI_SWIGLU, m->ubuf, nullptr, nullptr)}}, PRO_RMSNORM,
                                  m->hidden, L.ffn_norm, L.ug.cols, d, ru));
@@ -1183,8 +1202,9 @@ int enqueue_step(ggc_model* m) {
     lh.st_skip = &m->st->in_idx;   // skip while in_idx < n_in (a prompt token that is not the last)
     GGC_TRY(run_segments(m, {{m->output.dtype, make_seg(m->output, EPI_LOGITS, m->logits, nullptr, nullptr)}},
                          PRO_RMSNORM, m->hidden, m->output_norm, m->output.cols, d, lh));
-    GGC_CUDA_TRY(launch(ctx, k_step_end, dim3(1), dim3(tp ? 256 : 32), 0, m->st, (const unsigned long long*)m->argmax_key,
-                        m->out_ids, m->errf, tp ? (const float*)m->hidden : nullptr, d, (int)hp.n_layers));
+    GGC_CUDA_TRY(launch(ctx, k_step_end, dim3(1), dim3(nccl_tp ? 256 : 32), 0, m->st,
+                        (const unsigned long long*)m->argmax_key, m->out_ids, m->errf,
+                        nccl_tp ? (const float*)m->hidden : nullptr, d, (int)hp.n_layers));
     return GGC_OK;
 }
 
@@ -1341,6 +1361,93 @@ int build_stream(ggc_model* m) {
     return GGC_OK;
 }
 
+// Tensor parallel: the receive words of the fused all-reduce (allreduce.cuh),
+// mapped on every rank through CUDA IPC (handles exchanged with an NCCL
+// all-gather).  Used when every rank is a separate process on its own GPU and
+// every mapping opens; otherwise (or with GGC_TP_ALLREDUCE=nccl) the step
+// all-reduces with NCCL.  The ranks agree through an all-reduce of their verdicts.
+int setup_allreduce(ggc_model* m) {
+    ggc_ctx* ctx = m->ctx;
+    const int world = ctx->world, rank = ctx->rank;
+    m->ar_p2p = false;
+    if (world < 2) return GGC_OK;
+    const char* env = getenv("GGC_TP_ALLREDUCE");
+    const bool want = !(env && strcmp(env, "nccl") == 0) && world <= AR_MAX_WORLD;
+    const uint32_t d = m->hp.embed_dim;
+    const uint32_t stride = (d + 31u) / 32u * 32u;
+    const size_t buf_bytes = 2ull * world * stride * sizeof(unsigned long long);
+    struct Rec {
+        cudaIpcMemHandle_t h;
+        uint64_t pid;
+        unsigned char uuid[16];
+        int32_t ok, pad;
+    };
+    Rec mine{};
+    mine.pid = (uint64_t)getpid();
+    cudaDeviceProp prop{};
+    GGC_CUDA_TRY(cudaGetDeviceProperties(&prop, ctx->device));
+    memcpy(mine.uuid, &prop.uuid, 16);
+    uint8_t* base = nullptr;
+    if (want) {
+        GGC_TRY(dalloc(m, &base, buf_bytes));   // zeroed: tag 0 matches no epoch
+        mine.ok = cudaIpcGetMemHandle(&mine.h, base) == cudaSuccess;
+        cudaGetLastError();
+    }
+    Rec* drec = nullptr;
+    int32_t* dok = nullptr;
+    GGC_TRY(dalloc(m, (uint8_t**)&drec, sizeof(Rec) * (world + 1)));
+    GGC_TRY(dalloc(m, &dok, 1));
+    GGC_CUDA_TRY(cudaMemcpy(drec + world, &mine, sizeof(Rec), cudaMemcpyHostToDevice));
+    ncclResult_t r = nccl().AllGather(drec + world, drec, sizeof(Rec), ncclChar, ctx->comm, ctx->stream);
+    if (r != ncclSuccess) return nccl_error("ncclAllGather", r);
+    std::vector<Rec> recs(world);
+    GGC_CUDA_TRY(cudaMemcpyAsync(recs.data(), drec, sizeof(Rec) * world, cudaMemcpyDeviceToHost, ctx->stream));
+    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    bool ok = want;
+    for (int p = 0; p < world && ok; ++p) {
+        ok = recs[p].ok != 0;
+        for (int q = 0; q < p && ok; ++q)   // one GPU per rank, one process per rank
+            ok = memcmp(recs[p].uuid, recs[q].uuid, 16) != 0 && recs[p].pid != recs[q].pid;
+    }
+    std::vector<uint8_t*> peer(world, nullptr);
+    peer[rank] = base;
+    for (int p = 0; p < world && ok; ++p) {
+        if (p == rank) continue;
+        void* q = nullptr;
+        if (cudaIpcOpenMemHandle(&q, recs[p].h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            ok = false;
+            break;
+        }
+        m->ar_peer_maps.push_back(q);
+        peer[p] = (uint8_t*)q;
+    }
+    // every rank takes the same path
+    const int32_t vote = ok ? 1 : 0;
+    GGC_CUDA_TRY(cudaMemcpy(dok, &vote, sizeof(vote), cudaMemcpyHostToDevice));
+    r = nccl().AllReduce(dok, dok, 1, ncclInt32, ncclMin, ctx->comm, ctx->stream);
+    if (r != ncclSuccess) return nccl_error("ncclAllReduce", r);
+    int32_t all = 0;
+    GGC_CUDA_TRY(cudaMemcpyAsync(&all, dok, sizeof(all), cudaMemcpyDeviceToHost, ctx->stream));
+    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    if (!all) {
+        for (void* q : m->ar_peer_maps) cudaIpcCloseMemHandle(q);
+        m->ar_peer_maps.clear();
+        return GGC_OK;
+    }
+    ArGroup g{};
+    for (int p = 0; p < world; ++p) g.buf[p] = (unsigned long long*)peer[p];
+    g.world = world;
+    g.rank = rank;
+    g.stride = stride;
+    g.step = &m->st->ar_step;
+    g.per_step = 2u * m->hp.n_layers;
+    GGC_TRY(dalloc(m, &m->ar, 1));
+    GGC_CUDA_TRY(cudaMemcpy(m->ar, &g, sizeof(g), cudaMemcpyHostToDevice));
+    m->ar_p2p = true;
+    return GGC_OK;
+}
+
 int build_graph(ggc_model* m) {
     ggc_ctx* ctx = m->ctx;
     uint64_t before = ctx->launches;
@@ -1373,6 +1480,7 @@ void destroy_model(ggc_model* m) {
             free_mat(L.up); free_mat(L.gate); free_mat(L.down); free_mat(L.ug);
         }
         free_mat(m->output);
+        for (void* p : m->ar_peer_maps) cudaIpcCloseMemHandle(p);
         for (void* p : m->allocs) cudaFree(p);
         if (m->rb) cudaFreeHost(m->rb);
     }
@@ -1611,6 +1719,7 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
     s0.max_ctx = hp.max_ctx;
     GGC_CUDA_TRY(cudaMemcpy(m->st, &s0, sizeof(s0), cudaMemcpyHostToDevice));
     GGC_TRY(build_stream(m.get()));
+    GGC_TRY(setup_allreduce(m.get()));
     GGC_TRY(build_graph(m.get()));
     GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
     *out = m.release();
