@@ -1876,6 +1876,11 @@ extern "C" int ggc_model_wait(ggc_model* m, uint32_t* out_ids, uint64_t* n_out) 
 
 extern "C" uint64_t ggc_model_cache_len(const ggc_model* m) { return m ? m->cache_len : 0; }
 
+extern "C" int ggc_model_allreduce_kind(const ggc_model* m) {
+    if (!m || m->ctx->world < 2) return 0;
+    return m->ar_p2p ? 2 : 1;
+}
+
 extern "C" int ggc_model_truncate(ggc_model* m, uint64_t new_len) {
     if (!m) return set_error(GGC_ERR_INVALID_ARG, "null model");
     if (new_len >= m->cache_len) return GGC_OK;   // cache.rs:86-93 only shrinks

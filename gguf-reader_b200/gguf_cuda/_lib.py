@@ -143,6 +143,7 @@ SIGNATURES = {
     "ggc_model_destroy": (_i32, [_vp]),
     "ggc_model_forward": (_i32, [_vp, _vp, _vp, _u64, _vp, _vp]),
     "ggc_model_cache_len": (_u64, [_vp]),
+    "ggc_model_allreduce_kind": (_i32, [_vp]),
     "ggc_model_reset_cache": (_i32, [_vp]),
     "ggc_model_truncate": (_i32, [_vp, _u64]),
     "ggc_model_cache_append": (_i32, [_vp, _u32, _vp, _vp, _u64]),

@@ -241,6 +241,11 @@ class LlamaModel:
     def reset_cache(self):
         check(lib().ggc_model_reset_cache(self.h))
 
+    @property
+    def allreduce(self) -> str:
+        """How the tensor-parallel partials are summed: "none", "nccl" or "peer"."""
+        return ("none", "nccl", "peer")[lib().ggc_model_allreduce_kind(self.h)]
+
     def truncate(self, new_len: int):
         check(lib().ggc_model_truncate(self.h, new_len))
 

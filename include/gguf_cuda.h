@@ -220,6 +220,10 @@ int ggc_model_generate_greedy(ggc_model* m, const uint32_t* prompt, uint64_t n_p
 int ggc_model_decode(ggc_model* m, uint64_t steps, int64_t eos, int sync, uint32_t* out_ids, uint64_t* n_out);
 int ggc_model_wait(ggc_model* m, uint32_t* out_ids, uint64_t* n_out);
 
+/* How a tensor-parallel model sums its row-parallel partials: 0 = single GPU
+ * (none), 1 = NCCL all-reduce, 2 = fused into the GEMVs over peer memory. */
+int ggc_model_allreduce_kind(const ggc_model* m);
+
 /* Number of kernels this context launched so far (for launch accounting). */
 uint64_t ggc_ctx_kernel_launches(ggc_ctx* ctx);
 

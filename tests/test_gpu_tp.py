@@ -4,8 +4,12 @@ Every rank makes the same calls; the model shards q/k/v/up/gate rows and
 attn_output/ffn_down columns (ggc_tp_plan) and all-reduces the hidden state
 after each of the two.  Logits within 1e-4 relative L2 of the oracle, identical
 on every rank, and greedy ids identical for 32 tokens.  Skipped with fewer
-than two GPUs.
+than two GPUs.  Both all-reduce paths run: the fused one over peer memory
+(default) and NCCL (GGC_TP_ALLREDUCE=nccl).  GGC_TEST_TP_WORLD sets the rank
+count (default 2); cases whose heads it does not divide are skipped.
 """
+import os
+
 import numpy as np
 import pytest
 
@@ -14,7 +18,7 @@ pytestmark = pytest.mark.gpu
 from gguf_cuda import synth
 
 REL_L2 = 1e-4
-WORLD = 2
+WORLD = int(os.environ.get("GGC_TEST_TP_WORLD", "2"))
 
 MINI = dict(vocab_size=1000, embed_dim=512, n_heads=8, n_kv_heads=2, ffn_dim=1024, n_layers=2, rope_freq_base=1e4,
             qkv_bias=True, weights="q4_k_m")
@@ -38,8 +42,12 @@ def _need_gpus():
         pytest.skip(f"needs {WORLD} GPUs")
 
 
-def _worker(rank, world, nid, job, q):
+def _worker(rank, world, nid, job, q, allreduce):
     """One rank: build the sharded model and run `job` (same calls on every rank)."""
+    if allreduce == "nccl":
+        os.environ["GGC_TP_ALLREDUCE"] = "nccl"
+    else:
+        os.environ.pop("GGC_TP_ALLREDUCE", None)
     try:
         import torch  # noqa: F401  -- loads the NCCL the parent's unique id came from
         import gguf_cuda as ggc
@@ -49,14 +57,14 @@ def _worker(rank, world, nid, job, q):
         q.put((rank, RuntimeError(f"rank {rank}: {type(e).__name__}: {e}")))
 
 
-def run_ranks(job, timeout=600):
+def run_ranks(job, timeout=600, allreduce="peer"):
     import multiprocessing as mp
     import torch  # noqa: F401  -- the library binds the NCCL already loaded (PyTorch's)
     import gguf_cuda as ggc
     nid = ggc.Context.nccl_unique_id()
     mctx = mp.get_context("spawn")
     q = mctx.Queue()
-    procs = [mctx.Process(target=_worker, args=(r, WORLD, nid, job, q)) for r in range(WORLD)]
+    procs = [mctx.Process(target=_worker, args=(r, WORLD, nid, job, q, allreduce)) for r in range(WORLD)]
     for p in procs:
         p.start()
     try:
@@ -82,17 +90,20 @@ class PromptJob:
         step = m.forward([int(prompt[0])], [8])
         m.reset_cache()
         ids = m.generate_greedy(np.random.default_rng(9).integers(0, hp["vocab_size"], size=6), 32)
-        return dict(logits=logits, k=k, v=v, step=step, ids=ids, cache_len=m.cache_len())
+        return dict(logits=logits, k=k, v=v, step=step, ids=ids, cache_len=m.cache_len(), allreduce=m.allreduce)
 
 
+@pytest.mark.parametrize("allreduce", ["peer", "nccl"])
 @pytest.mark.parametrize("name,cfg,n_layers,vocab", CASES, ids=[c[0] for c in CASES])
-def test_tp2_matches_oracle(ggc, orc, name, cfg, n_layers, vocab):
+def test_tp_matches_oracle(ggc, orc, name, cfg, n_layers, vocab, allreduce):
     _need_gpus()
-    res = run_ranks(PromptJob(cfg, n_layers, vocab))
+    hp, ts = synth.make_model(cfg, n_layers=n_layers, seed=0, vocab_size=vocab)
+    if hp["n_kv_heads"] % WORLD:
+        pytest.skip(f"{WORLD} ranks do not divide {hp['n_kv_heads']} kv heads")
+    res = run_ranks(PromptJob(cfg, n_layers, vocab), allreduce=allreduce)
     for r in res:
         if isinstance(r, Exception):
             raise r
-    hp, ts = synth.make_model(cfg, n_layers=n_layers, seed=0, vocab_size=vocab)
     o = orc.Model(hp, ts)
     prompt = np.random.default_rng(5).integers(0, hp["vocab_size"], size=8).astype(np.uint32)
     want = o.forward(prompt, np.arange(8, dtype=np.int64))
@@ -103,6 +114,7 @@ def test_tp2_matches_oracle(ggc, orc, name, cfg, n_layers, vocab):
     hd = hp["embed_dim"] // hp["n_heads"]
     kvw = hp["n_kv_heads"] * hd
     for rank, r in enumerate(res):
+        assert r["allreduce"] == allreduce
         assert rel_l2(r["logits"], want) <= REL_L2, (rank, rel_l2(r["logits"], want))
         assert rel_l2(r["step"], want_step) <= REL_L2
         assert r["ids"] == want_ids
@@ -114,17 +126,18 @@ def test_tp2_matches_oracle(ggc, orc, name, cfg, n_layers, vocab):
         assert rel_l2(r["k"], ko.reshape(-1, kvw)[:, sl].ravel()) <= REL_L2
         assert rel_l2(r["v"], vo.reshape(-1, kvw)[:, sl].ravel()) <= REL_L2
     # replicated lm_head over the same reduced hidden state: identical on every rank
-    assert np.array_equal(res[0]["logits"], res[1]["logits"])
+    for r in res[1:]:
+        assert np.array_equal(res[0]["logits"], r["logits"])
 
 
 class NanJob:
-    """NaN planted in the attn_output columns that only rank 1 holds."""
+    """NaN planted in the attn_output columns that only the last rank holds."""
 
     def __call__(self, ggc, ctx):
         hp, ts = synth.make_model(dict(MINI, weights=0, qkv_bias=False), seed=2)
         wo = ts[3 + 7]
         w = wo["raw"].view(np.float32).copy().reshape(hp["embed_dim"], hp["embed_dim"])
-        w[:, hp["embed_dim"] // 2:] = np.nan
+        w[:, hp["embed_dim"] - hp["embed_dim"] // WORLD:] = np.nan
         ts[3 + 7] = dict(wo, raw=w.ravel().view(np.uint8))
         m = ggc.LlamaModel(hp, ts, max_ctx=8, ctx=ctx)
         try:
@@ -134,8 +147,11 @@ class NanJob:
         return None
 
 
-def test_tp2_nan_guard_same_on_every_rank(ggc):
+@pytest.mark.parametrize("allreduce", ["peer", "nccl"])
+def test_tp_nan_guard_same_on_every_rank(ggc, allreduce):
     _need_gpus()
-    res = run_ranks(NanJob())
+    if 2 % WORLD:
+        pytest.skip("the planted model has 2 kv heads")
+    res = run_ranks(NanJob(), allreduce=allreduce)
     for r in res:
         assert isinstance(r, str) and "NaN after layer 0 attention" in r, r
