@@ -27,6 +27,7 @@
 #include "attention.cuh"
 #include "noalloc.cuh"
 #include "stream.cuh"
+#include "prefill.cuh"
 
 using namespace ggc;
 
@@ -121,9 +122,10 @@ struct ggc_ctx {
     uint64_t launches = 0;
     // owner + one per live model / tensor: the context outlives everything made on it
     std::atomic<int> refs{1};
-    // staging buffers for host arguments
-    void* stage[3] = {nullptr, nullptr, nullptr};
-    size_t stage_cap[3] = {0, 0, 0};
+    // staging buffers for host arguments (0-2) and matmul operands (3-4)
+    void* stage[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+    size_t stage_cap[5] = {0, 0, 0, 0, 0};
+    int* errf = nullptr;   // device error flags of the context's own launches
 };
 
 namespace {
@@ -293,8 +295,9 @@ void ctx_release(ggc_ctx* ctx) {
     {
         DeviceGuard g(ctx->device);
         cudaStreamSynchronize(ctx->stream);
-        for (int i = 0; i < 3; ++i)
+        for (int i = 0; i < 5; ++i)
             if (ctx->stage[i]) cudaFree(ctx->stage[i]);
+        if (ctx->errf) cudaFree(ctx->errf);
         if (ctx->comm) nccl().CommDestroy(ctx->comm);
         cudaStreamDestroy(ctx->stream);
     }
@@ -774,6 +777,87 @@ extern "C" int ggc_tensor_dequantize(ggc_ctx* ctx, const ggc_tensor* t, float* o
     if (!ctx || !t || !out) return set_error(GGC_ERR_INVALID_ARG, "null argument");
     if (t->repacked) return set_error(GGC_ERR_INVALID_ARG, "tensor was uploaded in plane layout; upload with repack=0");
     return ggc_dequantize(ctx, t->dtype, t->raw, t->raw_bytes, t->n_elements, out);
+}
+
+namespace {
+
+template <int DT>
+struct RunMM {
+    static void run(ggc_ctx* ctx, const uint8_t* w, uint32_t n, uint32_t k, const __nv_bfloat16* xh,
+                    const __nv_bfloat16* xl, uint32_t m, uint32_t kpad, float* y, uint32_t ldy, const float* resid,
+                    int* errf, cudaError_t* err) {
+        static std::once_flag once;
+        static cudaError_t attr = cudaSuccess;
+        std::call_once(once, [] {
+            attr = cudaFuncSetAttribute(k_mm_tc<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MM_SMEM);
+        });
+        if (attr != cudaSuccess) { *err = attr; return; }
+        const dim3 grid(cdiv<uint32_t>(n, MM_BN), cdiv<uint32_t>(m, MM_TOKENS));
+        *err = launch(ctx, k_mm_tc<DT>, grid, dim3(MM_THREADS), MM_SMEM, w, n, k, xh, xl, m, kpad, y, ldy, resid, errf);
+    }
+};
+
+int ctx_errf(ggc_ctx* ctx, int** out) {
+    if (!ctx->errf) {
+        GGC_CUDA_TRY(cudaMalloc(&ctx->errf, sizeof(int) * ERRF_COUNT));
+        GGC_CUDA_TRY(cudaMemset(ctx->errf, 0, sizeof(int) * ERRF_COUNT));
+    }
+    *out = ctx->errf;
+    return GGC_OK;
+}
+
+// x [m][k] f32 (device) -> bf16 hi / lo [m][kpad] in staging buffers 3 / 4
+int split_rows(ggc_ctx* ctx, const float* x, const float* x2, uint32_t m, uint32_t k, uint32_t ldx, int pro,
+               __nv_bfloat16** xh, __nv_bfloat16** xl, uint32_t* kpad) {
+    *kpad = (k + MM_BK - 1) / MM_BK * MM_BK;
+    const size_t bytes = (size_t)m * *kpad * sizeof(__nv_bfloat16);
+    GGC_TRY(ensure_stage(ctx, 3, bytes));
+    GGC_TRY(ensure_stage(ctx, 4, bytes));
+    *xh = (__nv_bfloat16*)ctx->stage[3];
+    *xl = (__nv_bfloat16*)ctx->stage[4];
+    GGC_CUDA_TRY(launch(ctx, k_x_split, dim3(m), dim3(SPLIT_THREADS), 0, x, x2, m, k, ldx, *kpad, pro, *xh, *xl));
+    return GGC_OK;
+}
+
+}  // namespace
+
+// ops::matmul over a quantized weight (ops.rs:74 computes a @ b for f32
+// matrices; here b is an uploaded GGUF tensor used transposed, as every model
+// projection does): y[m][rows] = x[m][cols] . W^T on the tensor cores
+// (k_mm_tc, split-bf16 operands, f32 accumulation).
+extern "C" int ggc_tensor_matmul(ggc_ctx* ctx, const ggc_tensor* t, const float* x, uint64_t m, float* y) {
+    if (!ctx || !t || !x || !y) return set_error(GGC_ERR_INVALID_ARG, "null argument");
+    if (t->repacked) return set_error(GGC_ERR_INVALID_ARG, "tensor was uploaded in plane layout; upload with repack=0");
+    if (m == 0) return set_error(GGC_ERR_INFERENCE, "empty input");
+    const uint64_t cols = t->ne[0], rows = t->n_elements / (cols ? cols : 1);
+    if (m > 0xFFFFFFFFull / (cols ? cols : 1) || rows > 0xFFFFFFFFull) return set_error(GGC_ERR_INVALID_ARG, "matmul shape");
+    DeviceGuard g(ctx->device);
+    const void* dx;
+    void* dy;
+    bool staged;
+    GGC_TRY(dev_in(ctx, 0, x, m * cols * sizeof(float), &dx));
+    GGC_TRY(dev_out(ctx, 2, y, m * rows * sizeof(float), &dy, &staged));
+    int* errf = nullptr;
+    GGC_TRY(ctx_errf(ctx, &errf));
+    __nv_bfloat16 *xh, *xl;
+    uint32_t kpad = 0;
+    GGC_TRY(split_rows(ctx, (const float*)dx, nullptr, (uint32_t)m, (uint32_t)cols, (uint32_t)cols, MMP_PLAIN, &xh, &xl,
+                       &kpad));
+    cudaError_t err = cudaSuccess;
+    if (!dispatch_dtype<RunMM>(t->dtype, ctx, (const uint8_t*)t->raw, (uint32_t)rows, (uint32_t)cols,
+                               (const __nv_bfloat16*)xh, (const __nv_bfloat16*)xl, (uint32_t)m, kpad, (float*)dy,
+                               (uint32_t)rows, (const float*)nullptr, errf, &err))
+        return set_dequant_error(t->dtype, 0, 0, "matmul dtype");
+    GGC_CUDA_TRY(err);
+    int hf[ERRF_COUNT];
+    GGC_CUDA_TRY(cudaMemcpyAsync(hf, errf, sizeof(hf), cudaMemcpyDeviceToHost, ctx->stream));
+    if (staged) GGC_CUDA_TRY(cudaMemcpyAsync(y, dy, m * rows * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    if (hf[ERRF_TIMEOUT]) {
+        cudaMemset(errf, 0, sizeof(int) * ERRF_COUNT);
+        return set_error(GGC_ERR_TIMEOUT, "a bounded device wait expired");
+    }
+    return GGC_OK;
 }
 
 // ===========================================================================

@@ -137,6 +137,7 @@ SIGNATURES = {
     "ggc_tensor_matvec": (_i32, [_vp, _vp, _vp, _vp]),
     "ggc_tensor_matvec_batch": (_i32, [_vp, C.POINTER(_vp), _u64, _vp, _vp]),
     "ggc_tensor_dequantize": (_i32, [_vp, _vp, _vp]),
+    "ggc_tensor_matmul": (_i32, [_vp, _vp, _vp, _u64, _vp]),
     "ggc_infer_k_quant_dtype": (_i32, [_u64, _u64, _i32]),
     "ggc_tp_plan": (_i32, [C.POINTER(HParams), _i32, _i32, _i32, _i32, C.POINTER(TpShard)]),
     "ggc_model_create": (_i32, [_vp, C.POINTER(HParams), C.POINTER(TensorDesc), _u64, C.POINTER(_vp)]),

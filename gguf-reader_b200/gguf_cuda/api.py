@@ -164,6 +164,19 @@ class Tensor:
         check(lib().ggc_tensor_matvec_batch(ctx.h, arr, len(tensors), _ptr(x)[0], _ptr(y)[0]))
         return y
 
+    def matmul(self, x, m: int | None = None, y=None):
+        """ops::matmul with this tensor transposed: y[m][rows] = x[m][cols] . W^T on the
+        tensor cores (upload with repack=False)."""
+        if isinstance(x, np.ndarray):
+            x = np.ascontiguousarray(x, dtype=np.float32)
+            m = x.size // self.cols if m is None else m
+        elif m is None:
+            m = x.numel() // self.cols
+        if y is None:
+            y = np.zeros((m, self.rows), dtype=np.float32)
+        check(lib().ggc_tensor_matmul(self.ctx.h, self.h, _ptr(x)[0], m, _ptr(y)[0]))
+        return y
+
     def dequantize(self, out=None):
         if out is None:
             out = np.empty(self.rows * self.cols, dtype=np.float32)

@@ -131,6 +131,11 @@ int ggc_tensor_matvec(ggc_ctx* ctx, const ggc_tensor* t, const float* x, float* 
 int ggc_tensor_matvec_batch(ggc_ctx* ctx, const ggc_tensor* const* ts, uint64_t n, const float* x, float* y);
 /* Dequantises an uploaded tensor to f32 (n = all elements). */
 int ggc_tensor_dequantize(ggc_ctx* ctx, const ggc_tensor* t, float* out);
+/* ops::matmul (src/infer/ops.rs:74) with a quantized weight used transposed, as
+ * every model projection uses it: y[m][rows] = x[m][cols] . W^T, W uploaded with
+ * repack = 0.  Runs on the tensor cores (tcgen05, bf16 hi+lo split operands,
+ * f32 accumulation; ~1e-5 relative per product).  x / y host or device. */
+int ggc_tensor_matmul(ggc_ctx* ctx, const ggc_tensor* t, const float* x, uint64_t m, float* y);
 
 /* Replaces infer_k_quant_dtype (src/infer/model/llama.rs:656-710): the real
  * storage dtype of a tensor whose physical span disagrees with its marked dtype;
