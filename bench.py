@@ -53,6 +53,7 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=None, help="fewer layers (small profiling cases only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--parallel", choices=["tp", "replicas"], default="tp", help="multi-GPU mode (N > 1)")
+    ap.add_argument("--prefill", type=int, default=512, help="prompt tokens of the prefill measurement (0: skip)")
     return ap.parse_args()
 
 
@@ -238,6 +239,41 @@ def gemv_roofline(ggc, ctx, torch, stream, peak_gbs):
     return out
 
 
+def prefill_measure(args, model, hp, ts, stream, torch, barrier, max_over_ranks, world):
+    """A seeded prompt of args.prefill tokens through LlamaModel::forward on an
+    empty cache: its first n-1 tokens run through the batched tensor-core path
+    (k_mm_tc), the last through the decode step.  FLOPs: 2 x (layer weight
+    parameters) per token for the projections of every layer but the last (which
+    stops after K/V), plus attention 4 x hd x visible keys per head."""
+    n = args.prefill
+    L, d, f = hp["n_layers"], hp["embed_dim"], hp["ffn_dim"]
+    hd = d // hp["n_heads"]
+    kv = hp["n_kv_heads"] * hd
+    per_tok_full = 2 * (d * d + 2 * d * kv + d * d + 3 * d * f)
+    per_tok_last = 2 * (2 * d * kv)
+    attn = sum(4 * hd * (t + 1) * hp["n_heads"] for t in range(n - 1)) * (L - 1)
+    flops = (per_tok_full * (L - 1) + per_tok_last) * (n - 1) + attn
+    prompt = np.random.default_rng(21).integers(0, hp["vocab_size"], size=n).astype(np.uint32)
+    pos = np.arange(n, dtype=np.int64)
+    logits = np.zeros(hp["vocab_size"], dtype=np.float32)
+    times = []
+    for it in range(4):   # 1 warm-up + 3 timed
+        model.reset_cache()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        model.forward(prompt, pos, logits=logits)
+        e1.record(stream)
+        e1.synchronize()
+        if it:
+            times.append(max_over_ranks(e0.elapsed_time(e1) / 1e3))
+    t = float(np.median(times))
+    return {"tokens": n, "ms": t * 1e3, "tokens_per_s": n / t, "model_tflops": flops / t / 1e12,
+            "flops": flops, "n_gpus": world,
+            "api": "ggc_model_forward(n host tokens) on an empty cache -> host logits",
+            "path": "n-1 tokens batched (k_mm_tc tcgen05 split-bf16 products, k_attn_prefill), last token decode step"}
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import gguf_cuda as ggc
@@ -322,6 +358,9 @@ def run_ours(args, rank, world, local_rank):
     e2e_elapsed = max_over_ranks(f0.elapsed_time(f1) / 1e3)
     barrier()
 
+    prefill = prefill_measure(args, model, hp, ts, stream, torch, barrier, max_over_ranks, world) \
+        if args.prefill > 0 else None
+
     result = None
     if rank == 0:
         kv_bytes = synth.kv_bytes_per_token(hp, C - K // 2)
@@ -356,6 +395,7 @@ def run_ours(args, rank, world, local_rank):
                                "bytes_per_step_per_gpu": gpu_bytes, "achieved_gbs_per_gpu": model_gbs,
                                "frac": model_gbs / peak_gbs, "bound_tokens_s": peak_gbs * 1e9 / gpu_bytes * streams},
             "matvec": rl,
+            "prefill": prefill,
             "clocks": sampler.record(),
             "cpu_baseline": cpu,
         }

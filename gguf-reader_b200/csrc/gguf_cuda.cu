@@ -26,7 +26,6 @@
 #include "gemv_span.cuh"
 #include "attention.cuh"
 #include "noalloc.cuh"
-#include "stream.cuh"
 #include "prefill.cuh"
 
 using namespace ggc;
@@ -981,6 +980,14 @@ struct RunEmbed {
 
 }  // namespace
 
+// Raw GGUF rows of a weight (row-major blocks, the logical row order) for the
+// batched prefill product (k_mm_tc).
+struct RawMat {
+    int dtype = -1;
+    uint32_t rows = 0, cols = 0;
+    uint8_t* p = nullptr;
+};
+
 struct ModelLayer {
     float* attn_norm = nullptr;
     float* ffn_norm = nullptr;
@@ -990,6 +997,7 @@ struct ModelLayer {
     DevMat wq, wk, wv, wo, up, gate, down;
     DevMat ug;   // ffn_up / ffn_gate rows interleaved (same dtype): one GEMV with the SwiGLU epilogue
     uint32_t f_l = 0;   // ffn rows held (all of them, or this rank's shard)
+    RawMat rq, rk, rv, ro, rup, rgate, rdown;   // the same weights for the batched prefill
 };
 
 struct ggc_model {
@@ -1011,11 +1019,6 @@ struct ggc_model {
     float *hidden = nullptr, *q = nullptr, *o = nullptr, *ubuf = nullptr, *gbuf = nullptr, *logits = nullptr;
     float *scores = nullptr, *pmax = nullptr, *psum = nullptr, *opart = nullptr;
     AttnDecodeSel attn;   // fused decode attention, or null for the general pair
-    // the persistent decode step (k_stream), when every weight is a span format
-    bool stream = false;
-    StreamArgs sargs{};
-    size_t stream_smem = 0;
-    unsigned stream_grid = 0;
     float2* stats = nullptr;
     unsigned* tickets = nullptr;
     unsigned long long* argmax_key = nullptr;
@@ -1031,6 +1034,13 @@ struct ggc_model {
         int errf[ERRF_COUNT];
         unsigned long long key;
     }* rb = nullptr;
+    // batched prefill (prefill.cuh): raw weights in the layers, activations for
+    // PF_CHUNK tokens
+    bool prefill = false;
+    float *pf_h = nullptr, *pf_y = nullptr, *pf_q = nullptr, *pf_o = nullptr;
+    uint32_t* pf_tok = nullptr;
+    int64_t* pf_pos = nullptr;
+    uint32_t pf_ldy = 0;
     // tensor parallel: the fused all-reduce over peer memory (allreduce.cuh), else NCCL
     bool ar_p2p = false;
     ArGroup* ar = nullptr;                 // device copy
@@ -1164,14 +1174,6 @@ int enqueue_step(ggc_model* m) {
     cudaError_t err = cudaSuccess;
     dispatch_dtype<RunEmbed>(m->embd_dtype, ctx, (const uint8_t*)m->embd, m->embd_rows, d, m->st, m->hidden, m->errf, &err);
     GGC_CUDA_TRY(err);
-    if (m->stream) {
-        GGC_CUDA_TRY(stream_launch(m->hd, hp.kv_f16 != 0, hp.n_heads / hp.n_kv_heads, m->sargs, m->stream_grid,
-                                   m->stream_smem, ctx->stream));
-        ctx->launches++;
-        GGC_CUDA_TRY(launch(ctx, k_step_end, dim3(1), dim3(32), 0, m->st, (const unsigned long long*)m->argmax_key,
-                            m->out_ids, m->errf, (const float*)nullptr, 0u, 0));
-        return GGC_OK;
-    }
     GemvArgs base{};
     base.st_done = &m->st->done;
     base.slot = &m->st->slot;
@@ -1289,159 +1291,6 @@ int enqueue_step(ggc_model* m) {
     GGC_CUDA_TRY(launch(ctx, k_step_end, dim3(1), dim3(nccl_tp ? 256 : 32), 0, m->st,
                         (const unsigned long long*)m->argmax_key, m->out_ids, m->errf,
                         nccl_tp ? (const float*)m->hidden : nullptr, d, (int)hp.n_layers));
-    return GGC_OK;
-}
-
-// The op list of one decode step for k_stream (llama.rs:266-350): per layer the
-// Q/K/V GEMVs (RMSNorm prologue, bias + RoPE + cache-append epilogues), attention,
-// the output projection (+ residual), up/gate (RMSNorm), down (silu(gate) * up
-// prologue, + residual); then the final norm + lm_head with the greedy argmax.
-// Used only with GGC_DECODE_PATH=stream (the per-op kernels are the default);
-// leaves m->stream false when a weight is not a span format or the attention
-// shape has no fused kernel.
-int build_stream(ggc_model* m) {
-    const char* env = getenv("GGC_DECODE_PATH");
-    if (!env || strcmp(env, "stream") != 0 || m->ctx->world > 1) return GGC_OK;
-    const ggc_hparams& hp = m->hp;
-    const uint32_t G = hp.n_heads / hp.n_kv_heads;
-    const bool f16 = hp.kv_f16 != 0;
-    if (!m->attn.kernel || !stream_supported(m->hd, f16, G)) return GGC_OK;
-    for (auto& L : m->layers) {
-        if (!L.ug.base) return GGC_OK;   // the stream runs the fused up/gate GEMV
-        for (const DevMat* d : {&L.wq, &L.wk, &L.wv, &L.wo, &L.ug, &L.down})
-            if (!is_span_dt(d->dtype)) return GGC_OK;
-    }
-    if (!is_span_dt(m->output.dtype)) return GGC_OK;
-    ggc_ctx* ctx = m->ctx;
-    const unsigned grid = (unsigned)ctx->num_sms;
-    std::vector<StreamOp> ops;
-    uint32_t stage_bytes = 0, xl_bytes = 0, part_rows = 0;
-    GemvArgs base{};
-    base.slot = &m->st->slot;
-    base.pos = &m->st->pos;
-    base.rope = m->rope;
-    base.hd = m->hd;
-    base.kv_ctx = hp.max_ctx;
-    base.kv_f16 = f16 ? 1 : 0;
-    base.errf = m->errf;
-    base.argmax_key = m->argmax_key;
-    // GEMV ops over segments grouped by dtype (<= 3 per op), all depending on `dep`
-    auto add_gemv = [&](std::vector<std::pair<int, Seg>> segs, int pro, const float* x, const float* x2, uint32_t cols,
-                        uint32_t xcols, int err_slot, int err_val, int logits, int dep) {
-        while (!segs.empty()) {
-            const int dt = segs.front().first;
-            StreamOp op{};
-            op.kind = SOP_GEMV;
-            op.dtype = dt;
-            op.dep = dep;
-            op.logits = logits;
-            op.g = base;
-            op.g.nseg = 0;
-            std::vector<std::pair<int, Seg>> rest;
-            for (auto& sg : segs) {
-                if (sg.first == dt && op.g.nseg < 3) op.g.seg[op.g.nseg++] = sg.second;
-                else rest.push_back(sg);
-            }
-            op.g.pro = pro;
-            op.g.x = x;
-            op.g.x2 = x2;
-            op.g.cols = cols;
-            op.g.xcols = xcols;
-            op.g.err_slot = err_slot;
-            op.g.err_val = err_val;
-            const TileLayout L = make_layout(dt, TILE_ROWS, cols);
-            const SpanSpec sp = span_spec(dt);
-            uint32_t off = 0;
-            for (int p = 0; p < 4; ++p) {
-                op.poff[p] = off;
-                off += p < sp.n ? (TILE_ROWS * L.tp_full[p] + 127u) / 128u * 128u : 0u;
-            }
-            stage_bytes = std::max(stage_bytes, off);
-            xl_bytes = std::max(xl_bytes, L.nct * SPAN_LANES * (uint32_t)(GS_WORDS + GS_XF) * 4u);
-            uint32_t total_rb = 0;
-            for (int i = 0; i < op.g.nseg; ++i) total_rb += op.g.seg[i].m.L.nrb;
-            op.part_rows = L.nct > 1 ? (total_rb + grid - 1) / grid * TILE_ROWS : 0u;
-            part_rows = std::max(part_rows, op.part_rows);
-            ops.push_back(op);
-            segs.swap(rest);
-        }
-        return (int)ops.size() - 1;
-    };
-    const uint32_t d = hp.embed_dim, f = hp.ffn_dim;
-    const size_t layer_kv = (size_t)hp.max_ctx * m->kvdim * m->kv_elem;
-    int last = -1;
-    for (uint32_t l = 0; l < hp.n_layers; ++l) {
-        ModelLayer& L = m->layers[l];
-        void* kc = (uint8_t*)m->kcache + l * layer_kv;
-        void* vc = (uint8_t*)m->vcache + l * layer_kv;
-        const int qkv = add_gemv({{L.wq.dtype, make_seg(L.wq, EPI_ROPE_Q, m->q, nullptr, L.bq)},
-                                  {L.wk.dtype, make_seg(L.wk, EPI_ROPE_KC, nullptr, kc, L.bk)},
-                                  {L.wv.dtype, make_seg(L.wv, EPI_VC, nullptr, vc, L.bv)}},
-                                 PRO_RMSNORM, m->hidden, L.attn_norm, L.wq.cols, d, 0, 0, 0, last);
-        StreamOp at{};
-        at.kind = SOP_ATTN;
-        at.dep = qkv;
-        at.at.q = m->q;
-        at.at.kc = kc;
-        at.at.vc = vc;
-        at.at.pmax = m->pmax;
-        at.at.psum = m->psum;
-        at.at.opart = m->opart;
-        at.at.o = m->o;
-        at.at.tickets = m->tickets;
-        at.at.slot = &m->st->slot;
-        at.at.pos = &m->st->pos;
-        at.at.done = &m->st->done;
-        at.at.errf = m->errf;
-        at.at.n_heads = hp.n_heads;
-        at.at.kvh = hp.n_kv_heads;
-        at.at.hd = m->hd;
-        at.at.max_ctx = hp.max_ctx;
-        at.at.nsplit = m->nsplit;
-        at.at.inv = 1.0f / sqrtf((float)m->hd);
-        at.at.kv_f16 = f16 ? 1 : 0;
-        ops.push_back(at);
-        const int attn = (int)ops.size() - 1;
-        const int o = add_gemv({{L.wo.dtype, make_seg(L.wo, EPI_RESID, m->hidden, nullptr, nullptr)}}, PRO_PLAIN, m->o,
-                               nullptr, L.wo.cols, L.wo.xcols, ERRF_NAN_ATTN, (int)l + 1, 0, attn);
-        const int ug = add_gemv({{L.ug.dtype, make_seg(L.ug, EPI_SWIGLU, m->ubuf, nullptr, nullptr)}}, PRO_RMSNORM,
-                                m->hidden, L.ffn_norm, L.ug.cols, d, 0, 0, 0, o);
-        last = add_gemv({{L.down.dtype, make_seg(L.down, EPI_RESID, m->hidden, nullptr, nullptr)}}, PRO_PLAIN, m->ubuf,
-                        nullptr, L.down.cols, f, ERRF_NAN_FFN, (int)l + 1, 0, ug);
-    }
-    add_gemv({{m->output.dtype, make_seg(m->output, EPI_LOGITS, m->logits, nullptr, nullptr)}}, PRO_RMSNORM, m->hidden,
-             m->output_norm, m->output.cols, d, 0, 0, 1, last);
-    uint32_t attn_tile = 0, attn_scratch = 0;
-    stream_attn_geometry(m->hd, f16, G, &attn_tile, &attn_scratch);
-    auto r128 = [](uint32_t b) { return (b + 127u) / 128u * 128u; };
-    StreamArgs& P = m->sargs;
-    P.stage_bytes = r128(std::max(stage_bytes, attn_tile));
-    P.xl_bytes = r128(std::max(xl_bytes, attn_scratch));
-    P.part_bytes = r128(part_rows * 4u);
-    const size_t fixed = (size_t)P.xl_bytes + P.part_bytes + 128;
-    const size_t st = GEMV_SMEM_LIMIT > fixed ? (GEMV_SMEM_LIMIT - fixed) / P.stage_bytes : 0;
-    P.stages = (uint32_t)std::min<size_t>(st, GS_MAX_STAGES);
-    if (P.stages < 2) return GGC_OK;   // does not fit: per-op kernels
-    m->stream_smem = fixed + (size_t)P.stages * P.stage_bytes;
-    int per_sm = 0;
-    if (stream_prepare(m->hd, f16, G, m->stream_smem, &per_sm) != cudaSuccess || per_sm < 1) {
-        cudaGetLastError();
-        return GGC_OK;
-    }
-    StreamOp* dops = nullptr;
-    GGC_TRY(dalloc(m, &dops, ops.size()));
-    GGC_CUDA_TRY(cudaMemcpy(dops, ops.data(), ops.size() * sizeof(StreamOp), cudaMemcpyHostToDevice));
-    unsigned* done = nullptr;
-    GGC_TRY(dalloc(m, &done, ops.size() + 1));
-    P.ops = dops;
-    P.n_ops = (int)ops.size();
-    P.done = done;
-    P.st_done = &m->st->done;
-    P.st_skip = &m->st->in_idx;
-    P.errf = m->errf;
-    P.argmax_key = m->argmax_key;
-    m->stream_grid = grid;
-    m->stream = true;
     return GGC_OK;
 }
 
@@ -1638,6 +1487,19 @@ int slice_cols(const ggc_tensor_desc& t, uint64_t rows, uint64_t cols, uint64_t 
     return GGC_OK;
 }
 
+// Rows [r0, r0 + n) of a rows x cols block matrix `data` as a device RawMat.
+int upload_raw(ggc_model* m, const void* data, int dt, uint64_t r0, uint64_t n, uint64_t cols, RawMat& out) {
+    const uint64_t rb = cols / (uint64_t)block_size_of(dt) * (uint64_t)block_bytes_of(dt);
+    uint8_t* d = nullptr;
+    GGC_TRY(dalloc(m, &d, n * rb));
+    GGC_CUDA_TRY(cudaMemcpy(d, (const uint8_t*)data + r0 * rb, n * rb, cudaMemcpyHostToDevice));
+    out.dtype = dt;
+    out.rows = (uint32_t)n;
+    out.cols = (uint32_t)cols;
+    out.p = d;
+    return GGC_OK;
+}
+
 // Rows `rows` (source indices, in plane order) of a total_rows x cols matrix.
 int upload_rows(ggc_model* m, const ggc_tensor_desc& t, uint64_t total_rows, uint64_t cols,
                 const std::vector<uint32_t>& rows, DevMat& out, const char* what) {
@@ -1701,6 +1563,10 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
     GGC_TRY(upload_weight(m.get(), t[2], hp.vocab_size, d, nullptr, m->output, "output"));
     const std::vector<uint32_t> qorder = rope_row_order(hp.n_heads, hd), korder = rope_row_order(hp.n_kv_heads, hd);
     m->layers.resize(hp.n_layers);
+    {   // batched prefill: head dims with a k_attn_prefill instantiation; GGC_PREFILL=0 turns it off
+        const char* pe = getenv("GGC_PREFILL");
+        m->prefill = (hd == 64 || hd == 128) && !(pe && strcmp(pe, "0") == 0);
+    }
     for (uint32_t l = 0; l < hp.n_layers; ++l) {
         const ggc_tensor_desc* L = t + 3 + 12 * l;
         ModelLayer& ML = m->layers[l];
@@ -1719,6 +1585,15 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
                 return set_error(GGC_ERR_MISSING_TENSOR, "MissingTensor { name: blk.%u.ffn_norm, kind: tensor }", l);
             GGC_TRY(upload_ffn_up_gate(m.get(), L[9], L[10], f, d, 0, f, ML));
             GGC_TRY(upload_weight(m.get(), L[11], d, f, nullptr, ML.down, "ffn_down"));
+            if (m->prefill) {   // raw copies (shapes validated above)
+                GGC_TRY(upload_raw(m.get(), L[1].data, L[1].dtype, 0, m->qdim, d, ML.rq));
+                GGC_TRY(upload_raw(m.get(), L[3].data, L[3].dtype, 0, m->kvdim, d, ML.rk));
+                GGC_TRY(upload_raw(m.get(), L[5].data, L[5].dtype, 0, m->kvdim, d, ML.rv));
+                GGC_TRY(upload_raw(m.get(), L[7].data, L[7].dtype, 0, d, m->qdim, ML.ro));
+                GGC_TRY(upload_raw(m.get(), L[9].data, L[9].dtype, 0, f, d, ML.rup));
+                GGC_TRY(upload_raw(m.get(), L[10].data, L[10].dtype, 0, f, d, ML.rgate));
+                GGC_TRY(upload_raw(m.get(), L[11].data, L[11].dtype, 0, d, f, ML.rdown));
+            }
             continue;
         }
         // tensor-parallel shard (ggc_tp_plan): q/k/v rows and up/gate rows of this
@@ -1746,11 +1621,22 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
         std::vector<uint8_t> cols;
         GGC_TRY(slice_cols(L[7], d, qfull, (uint64_t)sh.head0 * hd, m->qdim, cols, "attn_output"));
         GGC_TRY(upload_mat(ctx, cols.data(), cols.size(), L[7].dtype, d, m->qdim, nullptr, ML.wo));
+        if (m->prefill) {
+            GGC_TRY(upload_raw(m.get(), L[1].data, L[1].dtype, (uint64_t)sh.head0 * hd, m->qdim, d, ML.rq));
+            GGC_TRY(upload_raw(m.get(), L[3].data, L[3].dtype, (uint64_t)sh.kv_head0 * hd, m->kvdim, d, ML.rk));
+            GGC_TRY(upload_raw(m.get(), L[5].data, L[5].dtype, (uint64_t)sh.kv_head0 * hd, m->kvdim, d, ML.rv));
+            GGC_TRY(upload_raw(m.get(), cols.data(), L[7].dtype, 0, d, m->qdim, ML.ro));
+        }
         GGC_TRY(upload_vec(m.get(), L[8], d, &ML.ffn_norm, "ffn_norm"));
         if (!ML.ffn_norm) return set_error(GGC_ERR_MISSING_TENSOR, "MissingTensor { name: blk.%u.ffn_norm, kind: tensor }", l);
         GGC_TRY(upload_ffn_up_gate(m.get(), L[9], L[10], f, d, sh.ffn0, sh.ffn_len, ML));
         GGC_TRY(slice_cols(L[11], d, f, sh.ffn0, sh.ffn_len, cols, "ffn_down"));
         GGC_TRY(upload_mat(ctx, cols.data(), cols.size(), L[11].dtype, d, sh.ffn_len, nullptr, ML.down));
+        if (m->prefill) {
+            GGC_TRY(upload_raw(m.get(), L[9].data, L[9].dtype, sh.ffn0, sh.ffn_len, d, ML.rup));
+            GGC_TRY(upload_raw(m.get(), L[10].data, L[10].dtype, sh.ffn0, sh.ffn_len, d, ML.rgate));
+            GGC_TRY(upload_raw(m.get(), cols.data(), L[11].dtype, 0, d, sh.ffn_len, ML.rdown));
+        }
     }
     // KV cache resident in HBM, head-major: [layer][n_kv][max_ctx][hd]
     const size_t kv_bytes = (size_t)hp.n_layers * hp.max_ctx * m->kvdim * m->kv_elem;
@@ -1802,7 +1688,6 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
     s0.done = 1;
     s0.max_ctx = hp.max_ctx;
     GGC_CUDA_TRY(cudaMemcpy(m->st, &s0, sizeof(s0), cudaMemcpyHostToDevice));
-    GGC_TRY(build_stream(m.get()));
     GGC_TRY(setup_allreduce(m.get()));
     GGC_TRY(build_graph(m.get()));
     GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
@@ -1834,9 +1719,8 @@ int run_steps(ggc_model* m, uint64_t n_in, uint64_t max_new, int64_t eos, uint64
     return GGC_OK;
 }
 
-int check_run(ggc_model* m) {
-    const int* e = m->rb->errf;
-    m->cache_len = m->rb->st.slot;
+// The error of a set of device flags (GgufError variant + message), GGC_OK if none.
+int errf_status(const ggc_model* m, const int* e) {
     int status = GGC_OK;
     if (e[ERRF_EMBED_OOB]) status = set_error(GGC_ERR_INFERENCE, "embed out of bounds: tok=%d", e[ERRF_EMBED_OOB] - 1);
     // the earliest NaN site: attention of layer l runs before the ffn of layer l
@@ -1849,13 +1733,160 @@ int check_run(ggc_model* m) {
                            m->hp.max_ctx);
     } else if (e[ERRF_BAD_POS]) status = set_error(GGC_ERR_INFERENCE, "position outside [0, %u)", m->hp.max_ctx);
     else if (e[ERRF_TIMEOUT]) status = set_error(GGC_ERR_TIMEOUT, "a bounded device wait expired");
+    return status;
+}
+
+int check_run(ggc_model* m) {
+    m->cache_len = m->rb->st.slot;
+    const int status = errf_status(m, m->rb->errf);
     if (status != GGC_OK) {
         cudaMemsetAsync(m->errf, 0, sizeof(int) * ERRF_COUNT, m->ctx->stream);
-        if (m->stream)   // an abandoned launch may leave completion counters behind
-            cudaMemsetAsync(m->sargs.done, 0, sizeof(unsigned) * (m->sargs.n_ops + 1), m->ctx->stream);
         cudaStreamSynchronize(m->ctx->stream);
     }
     return status;
+}
+
+// ---- batched prefill (prefill.cuh) -------------------------------------------
+constexpr uint32_t PF_CHUNK = MM_TOKENS;     // tokens per pass (one k_mm_tc grid row)
+constexpr uint64_t PREFILL_MIN = 64;          // batch the prompt prefix from this many tokens on
+
+template <int DT>
+struct RunEmbedRows {
+    static void run(ggc_ctx* ctx, const uint8_t* raw, uint64_t rows, uint32_t d, const uint32_t* tok, uint32_t n,
+                    float* h, int* errf, cudaError_t* err) {
+        *err = launch(ctx, k_embed_rows<DT>, dim3(n), dim3(256), 0, raw, rows, d, tok, h, errf);
+    }
+};
+
+int ensure_prefill_buffers(ggc_model* m) {
+    if (m->pf_h) return GGC_OK;
+    const ggc_hparams& hp = m->hp;
+    uint32_t fmax = 0;
+    for (auto& L : m->layers) fmax = std::max(fmax, L.f_l);
+    m->pf_ldy = std::max(m->qdim + 2 * m->kvdim, 2 * fmax);
+    GGC_TRY(dalloc(m, &m->pf_h, (size_t)PF_CHUNK * hp.embed_dim));
+    GGC_TRY(dalloc(m, &m->pf_y, (size_t)PF_CHUNK * m->pf_ldy));
+    GGC_TRY(dalloc(m, &m->pf_q, (size_t)PF_CHUNK * m->qdim));
+    GGC_TRY(dalloc(m, &m->pf_o, (size_t)PF_CHUNK * m->qdim));
+    GGC_TRY(dalloc(m, &m->pf_tok, PF_CHUNK));
+    GGC_TRY(dalloc(m, &m->pf_pos, PF_CHUNK));
+    return GGC_OK;
+}
+
+// y[:, 0:rows] (ldy) (+)= rmsnorm / swiglu / plain(x) . W^T for a raw weight
+int mm_raw(ggc_model* m, const RawMat& w, const float* x, const float* x2, uint32_t n, uint32_t ldx, int pro, float* y,
+           uint32_t ldy, const float* resid) {
+    ggc_ctx* ctx = m->ctx;
+    __nv_bfloat16 *xh, *xl;
+    uint32_t kpad = 0;
+    GGC_TRY(split_rows(ctx, x, x2, n, w.cols, ldx, pro, &xh, &xl, &kpad));
+    cudaError_t err = cudaSuccess;
+    if (!dispatch_dtype<RunMM>(w.dtype, ctx, (const uint8_t*)w.p, w.rows, w.cols, (const __nv_bfloat16*)xh,
+                               (const __nv_bfloat16*)xl, n, kpad, y, ldy, resid, m->errf, &err))
+        return set_dequant_error(w.dtype, 0, 0, "prefill dtype");
+    GGC_CUDA_TRY(err);
+    return GGC_OK;
+}
+
+// K/V of `count` prompt tokens at cache slots [cache_len, cache_len + count)
+// through every layer in passes of PF_CHUNK tokens: embed, then per layer
+// RMSNorm -> q/k/v (k_mm_tc) -> bias + RoPE + cache append -> causal attention
+// -> attn_output (+ residual) -> RMSNorm -> up, gate -> silu(gate) * up -> down
+// (+ residual), with the NaN guards (llama.rs:266-350).  The last layer stops
+// after its K/V: nothing of these tokens but the cache is used later (the last
+// prompt token runs through the decode step for its logits).  Tensor parallel:
+// the attn_output / ffn_down partials are all-reduced with NCCL (rank 0 adds
+// the residual).
+int prefill_batch(ggc_model* m, const uint32_t* tokens, const int64_t* positions, uint64_t count) {
+    ggc_ctx* ctx = m->ctx;
+    const ggc_hparams& hp = m->hp;
+    const uint32_t d = hp.embed_dim, hd = m->hd;
+    const bool tp = ctx->world > 1;
+    const bool lead = !tp || ctx->rank == 0;
+    GGC_TRY(ensure_prefill_buffers(m));
+    std::vector<uint32_t> htok(count);
+    std::vector<int64_t> hpos(count);
+    GGC_CUDA_TRY(cudaMemcpy(htok.data(), tokens, count * sizeof(uint32_t), cudaMemcpyDefault));
+    GGC_CUDA_TRY(cudaMemcpy(hpos.data(), positions, count * sizeof(int64_t), cudaMemcpyDefault));
+    for (uint64_t i = 0; i < count; ++i)
+        if (hpos[i] < 0 || hpos[i] >= (int64_t)hp.max_ctx)
+            return set_error(GGC_ERR_INFERENCE, "position outside [0, %u)", hp.max_ctx);
+    GGC_CUDA_TRY(cudaMemsetAsync(m->errf, 0, sizeof(int) * ERRF_COUNT, ctx->stream));
+    const uint64_t base = m->cache_len;
+    const size_t layer_kv = (size_t)hp.max_ctx * m->kvdim * m->kv_elem;
+    const float inv = 1.0f / sqrtf((float)hd);
+    auto allreduce_h = [&](uint32_t n) -> int {
+        if (!tp) return GGC_OK;
+        const ncclResult_t r = nccl().AllReduce(m->pf_h, m->pf_h, (size_t)n * d, ncclFloat, ncclSum, ctx->comm, ctx->stream);
+        return r == ncclSuccess ? GGC_OK : nccl_error("ncclAllReduce", r);
+    };
+    auto nan_scan = [&](uint32_t n, int slot, int val) -> int {
+        GGC_CUDA_TRY(launch(ctx, k_nan_scan, dim3((unsigned)std::min<uint64_t>(cdiv<uint64_t>((uint64_t)n * d, 256), 1024)),
+                            dim3(256), 0, (const float*)m->pf_h, (uint64_t)n * d, m->errf, slot, val));
+        return GGC_OK;
+    };
+    for (uint64_t done = 0; done < count; done += PF_CHUNK) {
+        const uint32_t n = (uint32_t)std::min<uint64_t>(PF_CHUNK, count - done);
+        const uint32_t slot0 = (uint32_t)(base + done);
+        GGC_CUDA_TRY(cudaMemcpyAsync(m->pf_tok, htok.data() + done, n * sizeof(uint32_t), cudaMemcpyHostToDevice,
+                                     ctx->stream));
+        GGC_CUDA_TRY(cudaMemcpyAsync(m->pf_pos, hpos.data() + done, n * sizeof(int64_t), cudaMemcpyHostToDevice,
+                                     ctx->stream));
+        cudaError_t err = cudaSuccess;
+        dispatch_dtype<RunEmbedRows>(m->embd_dtype, ctx, (const uint8_t*)m->embd, m->embd_rows, d,
+                                     (const uint32_t*)m->pf_tok, n, m->pf_h, m->errf, &err);
+        GGC_CUDA_TRY(err);
+        for (uint32_t l = 0; l < hp.n_layers; ++l) {
+            ModelLayer& L = m->layers[l];
+            const bool last = l + 1 == hp.n_layers;
+            void* kc = (uint8_t*)m->kcache + l * layer_kv;
+            void* vc = (uint8_t*)m->vcache + l * layer_kv;
+            float* yq = m->pf_y;
+            float* yk = m->pf_y + m->qdim;
+            float* yv = yk + m->kvdim;
+            const uint32_t ldy = m->qdim + 2 * m->kvdim;
+            if (!last) GGC_TRY(mm_raw(m, L.rq, m->pf_h, L.attn_norm, n, d, MMP_RMSNORM, yq, ldy, nullptr));
+            GGC_TRY(mm_raw(m, L.rk, m->pf_h, L.attn_norm, n, d, MMP_RMSNORM, yk, ldy, nullptr));
+            GGC_TRY(mm_raw(m, L.rv, m->pf_h, L.attn_norm, n, d, MMP_RMSNORM, yv, ldy, nullptr));
+            GGC_CUDA_TRY(launch(ctx, k_qkv_post, dim3(n), dim3(256), 0, (const float*)m->pf_y, ldy, m->qdim, m->kvdim, hd,
+                                (const float*)L.bq, (const float*)L.bk, (const float*)L.bv, (const int64_t*)m->pf_pos,
+                                (const float2*)m->rope, slot0, last ? (float*)nullptr : m->pf_q, kc, vc, hp.max_ctx,
+                                hp.kv_f16 ? 1 : 0));
+            if (last) break;
+            const dim3 ag(m->heads_l, cdiv<uint32_t>(n, PA_Q));
+            if (hd == 64)
+                GGC_CUDA_TRY(launch(ctx, k_attn_prefill<64>, ag, dim3(PA_WARPS * 32), 0, (const float*)m->pf_q,
+                                    (const void*)kc, (const void*)vc, (const int64_t*)m->pf_pos, slot0, n, m->heads_l,
+                                    m->kv_heads_l, hp.max_ctx, hp.kv_f16 ? 1 : 0, inv, m->pf_o));
+            else
+                GGC_CUDA_TRY(launch(ctx, k_attn_prefill<128>, ag, dim3(PA_WARPS * 32), 0, (const float*)m->pf_q,
+                                    (const void*)kc, (const void*)vc, (const int64_t*)m->pf_pos, slot0, n, m->heads_l,
+                                    m->kv_heads_l, hp.max_ctx, hp.kv_f16 ? 1 : 0, inv, m->pf_o));
+            // attn_output + residual (rank 0 alone under tensor parallelism), all-reduce, NaN guard
+            GGC_TRY(mm_raw(m, L.ro, m->pf_o, nullptr, n, m->qdim, MMP_PLAIN, m->pf_h, d, lead ? m->pf_h : nullptr));
+            GGC_TRY(allreduce_h(n));
+            GGC_TRY(nan_scan(n, ERRF_NAN_ATTN, (int)l + 1));
+            // ffn: up | gate side by side in pf_y, then down (+ residual)
+            const uint32_t fl = L.f_l, ldu = 2 * fl;
+            GGC_TRY(mm_raw(m, L.rup, m->pf_h, L.ffn_norm, n, d, MMP_RMSNORM, m->pf_y, ldu, nullptr));
+            GGC_TRY(mm_raw(m, L.rgate, m->pf_h, L.ffn_norm, n, d, MMP_RMSNORM, m->pf_y + fl, ldu, nullptr));
+            GGC_TRY(mm_raw(m, L.rdown, m->pf_y + fl, m->pf_y, n, ldu, MMP_SWIGLU, m->pf_h, d, lead ? m->pf_h : nullptr));
+            GGC_TRY(allreduce_h(n));
+            GGC_TRY(nan_scan(n, ERRF_NAN_FFN, (int)l + 1));
+        }
+    }
+    int hf[ERRF_COUNT];
+    GGC_CUDA_TRY(cudaMemcpyAsync(hf, m->errf, sizeof(hf), cudaMemcpyDeviceToHost, ctx->stream));
+    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    const int status = errf_status(m, hf);
+    if (status != GGC_OK) {
+        cudaMemset(m->errf, 0, sizeof(int) * ERRF_COUNT);
+        return status;
+    }
+    const uint32_t slot = (uint32_t)(base + count);
+    GGC_CUDA_TRY(cudaMemcpy(&m->st->slot, &slot, sizeof(slot), cudaMemcpyHostToDevice));
+    m->cache_len = base + count;
+    return GGC_OK;
 }
 
 }  // namespace
@@ -1871,11 +1902,18 @@ extern "C" int ggc_model_forward(ggc_model* m, const uint32_t* tokens, const int
     if (m->cache_len + n > m->hp.max_ctx)
         return set_error(GGC_ERR_KV_CACHE_OVERFLOW, "KvCacheOverflow { seq_len: %llu, max_seq: %u }",
                          (unsigned long long)(m->cache_len + n), m->hp.max_ctx);
+    // a long prompt prefix goes through the batched tensor-core path; the last
+    // token (whose logits are returned) through the decode step
+    uint64_t first = 0;
+    if (m->prefill && n > PREFILL_MIN) {
+        GGC_TRY(prefill_batch(m, tokens, positions, n - 1));
+        first = n - 1;
+    }
     const cudaMemcpyKind k1 = is_device_ptr(tokens) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
     const cudaMemcpyKind k2 = is_device_ptr(positions) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
-    GGC_CUDA_TRY(cudaMemcpyAsync(m->in_tok, tokens, n * sizeof(uint32_t), k1, ctx->stream));
-    GGC_CUDA_TRY(cudaMemcpyAsync(m->in_pos, positions, n * sizeof(int64_t), k2, ctx->stream));
-    GGC_TRY(run_steps(m, n, 0, -1, n));
+    GGC_CUDA_TRY(cudaMemcpyAsync(m->in_tok, tokens + first, (n - first) * sizeof(uint32_t), k1, ctx->stream));
+    GGC_CUDA_TRY(cudaMemcpyAsync(m->in_pos, positions + first, (n - first) * sizeof(int64_t), k2, ctx->stream));
+    GGC_TRY(run_steps(m, n - first, 0, -1, n - first));
     if (logits) {
         const cudaMemcpyKind k = is_device_ptr(logits) ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
         GGC_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, (size_t)m->hp.vocab_size * sizeof(float), k, ctx->stream));
@@ -1903,10 +1941,17 @@ extern "C" int ggc_model_generate_greedy(ggc_model* m, const uint32_t* prompt, u
                          (unsigned long long)(m->cache_len + n_prompt + max_tokens), m->hp.max_ctx);
     std::vector<int64_t> pos(n_prompt);
     for (uint64_t i = 0; i < n_prompt; ++i) pos[i] = start_pos + (int64_t)i;
+    uint64_t first = 0;   // prompt prefix through the batched path (as ggc_model_forward)
+    if (m->prefill && n_prompt > PREFILL_MIN) {
+        GGC_TRY(prefill_batch(m, prompt, pos.data(), n_prompt - 1));
+        first = n_prompt - 1;
+    }
+    const uint64_t rest = n_prompt - first;
     const cudaMemcpyKind k1 = is_device_ptr(prompt) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
-    GGC_CUDA_TRY(cudaMemcpyAsync(m->in_tok, prompt, n_prompt * sizeof(uint32_t), k1, ctx->stream));
-    GGC_CUDA_TRY(cudaMemcpyAsync(m->in_pos, pos.data(), n_prompt * sizeof(int64_t), cudaMemcpyHostToDevice, ctx->stream));
-    GGC_TRY(run_steps(m, n_prompt, max_tokens, eos, n_prompt + max_tokens));
+    GGC_CUDA_TRY(cudaMemcpyAsync(m->in_tok, prompt + first, rest * sizeof(uint32_t), k1, ctx->stream));
+    GGC_CUDA_TRY(cudaMemcpyAsync(m->in_pos, pos.data() + first, rest * sizeof(int64_t), cudaMemcpyHostToDevice,
+                                 ctx->stream));
+    GGC_TRY(run_steps(m, rest, max_tokens, eos, rest + max_tokens));
     GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
     const uint64_t got = (uint64_t)m->rb->st.n_out;
     if (got) GGC_CUDA_TRY(cudaMemcpy(out_ids, m->out_ids, got * sizeof(uint32_t), cudaMemcpyDeviceToHost));

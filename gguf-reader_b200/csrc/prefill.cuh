@@ -276,4 +276,203 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
     }
 }
 
+
+// ---- the per-token kernels of the batched forward ---------------------------
+
+// embed (llama.rs:367-380): row tok[t] of token_embd, dequantised, into h[t][:]
+template <int DT>
+__global__ void __launch_bounds__(256) k_embed_rows(const uint8_t* __restrict__ raw, uint64_t n_rows, uint32_t d,
+                                                    const uint32_t* __restrict__ tok, float* __restrict__ h,
+                                                    int* __restrict__ errf) {
+    constexpr int BS = block_size_of(DT), BB = block_bytes_of(DT);
+    pdl_trigger();
+    pdl_wait();
+    const uint32_t t = blockIdx.x, id = tok[t];
+    if ((uint64_t)id >= n_rows) {
+        if (threadIdx.x == 0) atomicCAS(&errf[ERRF_EMBED_OOB], 0, (int)id + 1);
+        return;
+    }
+    const uint8_t* row = raw + (uint64_t)id * (uint64_t)(d / BS) * BB;
+    for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) {
+        const uint32_t blk = i / BS;
+        h[(size_t)t * d + i] = deq_elem<DT>(row + (uint64_t)blk * BB, (int)(i - blk * BS));
+    }
+}
+
+// Q/K/V of the batch (one row per token, columns [q | k | v] at ldy): bias,
+// RoPE (ops.rs:318-337, pairs (j, j + hd/2), the decode path's table and
+// arithmetic), q into qo[t], k / v into the cache at slot base + t
+// (llama.rs:441-479, cache.rs:46-54).  q is skipped when qo is null.
+__global__ void __launch_bounds__(256) k_qkv_post(const float* __restrict__ y, uint32_t ldy, uint32_t qdim,
+                                                  uint32_t kvdim, uint32_t hd, const float* __restrict__ bq,
+                                                  const float* __restrict__ bk, const float* __restrict__ bv,
+                                                  const int64_t* __restrict__ pos, const float2* __restrict__ rope,
+                                                  uint32_t base, float* __restrict__ qo, void* kc, void* vc,
+                                                  uint32_t kv_ctx, int kv_f16) {
+    pdl_trigger();
+    pdl_wait();
+    const uint32_t t = blockIdx.x, half = hd / 2;
+    const float* yr = y + (size_t)t * ldy;
+    const int64_t p = pos[t];
+    const float2* cs = rope + (uint64_t)p * half;
+    // RoPE pairs: q (qdim / 2 pairs), then k (kvdim / 2 pairs); then v elements
+    const uint32_t nq = qo ? qdim / 2 : 0, nk = kvdim / 2;
+    for (uint32_t i = threadIdx.x; i < nq + nk + kvdim; i += blockDim.x) {
+        if (i < nq + nk) {
+            const bool isq = i < nq;
+            const uint32_t pm = isq ? i : i - nq, head = pm / half, j = pm % half;
+            const uint32_t l0 = head * hd + j, l1 = l0 + half;
+            const float* src = isq ? yr : yr + qdim;
+            const float* b = isq ? bq : bk;
+            float v0 = src[l0], v1 = src[l1];
+            if (b) { v0 = __fadd_rn(v0, b[l0]); v1 = __fadd_rn(v1, b[l1]); }
+            const float2 c = cs[j];
+            const float n0 = __fsub_rn(__fmul_rn(v0, c.x), __fmul_rn(v1, c.y));
+            const float n1 = __fadd_rn(__fmul_rn(v1, c.x), __fmul_rn(v0, c.y));
+            if (isq) {
+                qo[(size_t)t * qdim + l0] = n0;
+                qo[(size_t)t * qdim + l1] = n1;
+            } else {
+                const uint64_t o = ((uint64_t)head * kv_ctx + base + t) * hd;
+                if (kv_f16) {
+                    reinterpret_cast<__half*>(kc)[o + j] = __float2half_rn(n0);
+                    reinterpret_cast<__half*>(kc)[o + j + half] = __float2half_rn(n1);
+                } else {
+                    reinterpret_cast<float*>(kc)[o + j] = n0;
+                    reinterpret_cast<float*>(kc)[o + j + half] = n1;
+                }
+            }
+        } else {
+            const uint32_t lr = i - nq - nk, head = lr / hd;
+            float v = yr[qdim + kvdim + lr];
+            if (bv) v = __fadd_rn(v, bv[lr]);
+            const uint64_t o = ((uint64_t)head * kv_ctx + base + t) * hd + (lr - head * hd);
+            if (kv_f16) reinterpret_cast<__half*>(vc)[o] = __float2half_rn(v);
+            else reinterpret_cast<float*>(vc)[o] = v;
+        }
+    }
+}
+
+// Causal attention of the batch (llama.rs:499-545) on the CUDA cores: CTA = one
+// q head x PA_Q tokens (4 warps x 4 tokens), K/V tiles of 32 cache rows in
+// shared memory (K rows padded by one float: lane j reads row j without bank
+// conflicts).  Token t (cache slot base + t, position pos[t]) sees the rows
+// s < min(pos[t] + 1, base + t + 1), as the decode kernels do; the softmax runs
+// online (running max / sum, o rescaled per tile) and o is divided by the sum
+// at the end.  Output o[t][head * hd + i].
+constexpr int PA_WARPS = 4, PA_QW = 4, PA_Q = PA_WARPS * PA_QW, PA_KT = 32;
+
+template <int HD>
+__global__ void __launch_bounds__(PA_WARPS * 32) k_attn_prefill(const float* __restrict__ q, const void* kc,
+                                                                 const void* vc, const int64_t* __restrict__ pos,
+                                                                 uint32_t base, uint32_t m, uint32_t n_heads,
+                                                                 uint32_t kvh, uint32_t kv_ctx, int kv_f16, float inv,
+                                                                 float* __restrict__ o) {
+    constexpr int NI = HD / 32;
+    __shared__ float sk[PA_KT][HD + 1];
+    __shared__ float sv[PA_KT][HD];
+    __shared__ float sq[PA_Q][HD];
+    pdl_trigger();
+    pdl_wait();
+    const uint32_t head = blockIdx.x, t0 = blockIdx.y * PA_Q, kvhead = head / (n_heads / kvh);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t qdim = n_heads * HD;
+    for (uint32_t i = tid; i < PA_Q * HD; i += blockDim.x) {
+        const uint32_t r = i / HD, t = t0 + r;
+        sq[r][i % HD] = t < m ? q[(size_t)t * qdim + head * HD + i % HD] : 0.f;
+    }
+    // visible rows per token of this warp, and of the whole CTA
+    uint32_t vis[PA_QW];
+    uint32_t vmax = 0;
+    for (int k = 0; k < PA_QW; ++k) {
+        const uint32_t t = t0 + warp * PA_QW + k;
+        uint32_t v = 0;
+        if (t < m) {
+            const int64_t p = pos[t];
+            const uint32_t seq = base + t + 1;
+            v = (p + 1 < (int64_t)seq) ? (uint32_t)(p + 1) : seq;
+        }
+        vis[k] = v;
+    }
+    for (uint32_t r = 0; r < PA_Q; ++r) {
+        const uint32_t t = t0 + r;
+        if (t < m) {
+            const int64_t p = pos[t];
+            const uint32_t seq = base + t + 1, v = (p + 1 < (int64_t)seq) ? (uint32_t)(p + 1) : seq;
+            vmax = v > vmax ? v : vmax;
+        }
+    }
+    float mx[PA_QW], sum[PA_QW], acc[PA_QW][NI];
+#pragma unroll
+    for (int k = 0; k < PA_QW; ++k) {
+        mx[k] = -INFINITY;
+        sum[k] = 0.f;
+#pragma unroll
+        for (int c = 0; c < NI; ++c) acc[k][c] = 0.f;
+    }
+    const uint64_t hb = (uint64_t)kvhead * kv_ctx * HD;
+    for (uint32_t s0 = 0; s0 < vmax; s0 += PA_KT) {
+        __syncthreads();   // previous tile consumed (and sq written, first time)
+        for (uint32_t i = tid; i < PA_KT * HD; i += blockDim.x) {
+            const uint32_t r = i / HD, c = i % HD, s = s0 + r;
+            float kv = 0.f, vv = 0.f;
+            if (s < vmax) {
+                const uint64_t idx = hb + (uint64_t)s * HD + c;
+                kv = kv_f16 ? __half2float(reinterpret_cast<const __half*>(kc)[idx]) : reinterpret_cast<const float*>(kc)[idx];
+                vv = kv_f16 ? __half2float(reinterpret_cast<const __half*>(vc)[idx]) : reinterpret_cast<const float*>(vc)[idx];
+            }
+            sk[r][c] = kv;
+            sv[r][c] = vv;
+        }
+        __syncthreads();
+        const uint32_t s = s0 + lane;   // this lane's key
+#pragma unroll
+        for (int k = 0; k < PA_QW; ++k) {
+            if (s0 >= vis[k]) continue;   // warp-uniform
+            const float* qr = sq[warp * PA_QW + k];
+            float dot = 0.f;
+#pragma unroll 8
+            for (int i = 0; i < HD; ++i) dot = fmaf(qr[i], sk[lane][i], dot);
+            const float sc = s < vis[k] ? __fmul_rn(dot, inv) : -INFINITY;
+            float tmax = sc;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
+            const float mnew = fmaxf(mx[k], tmax);
+            const float scale = expf(mx[k] - mnew);   // 0 on the first tile (mx = -inf)
+            const float pj = s < vis[k] ? expf(sc - mnew) : 0.f;
+            float ps = pj;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+            sum[k] = sum[k] * scale + ps;
+            mx[k] = mnew;
+#pragma unroll
+            for (int c = 0; c < NI; ++c) acc[k][c] *= scale;
+            for (int j = 0; j < PA_KT; ++j) {
+                const float pb = __shfl_sync(0xffffffffu, pj, j);
+#pragma unroll
+                for (int c = 0; c < NI; ++c) acc[k][c] = fmaf(pb, sv[j][lane + 32 * c], acc[k][c]);
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < PA_QW; ++k) {
+        const uint32_t t = t0 + warp * PA_QW + k;
+        if (t >= m) continue;
+        const float rs = vis[k] ? 1.0f / sum[k] : 0.f;
+#pragma unroll
+        for (int c = 0; c < NI; ++c) o[(size_t)t * qdim + head * HD + lane + 32 * c] = acc[k][c] * rs;
+    }
+}
+
+// NaN anywhere in x[0, n) -> errf[slot] = val (first wins); the NaN guards of
+// llama.rs:300-307 for the batch
+__global__ void __launch_bounds__(256) k_nan_scan(const float* __restrict__ x, uint64_t n, int* errf, int slot, int val) {
+    pdl_trigger();
+    pdl_wait();
+    bool nan = false;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+        nan |= isnan(x[i]);
+    if (__any_sync(0xffffffffu, nan) && (threadIdx.x & 31) == 0) atomicCAS(&errf[slot], 0, val);
+}
+
 }  // namespace ggc

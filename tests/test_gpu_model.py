@@ -9,13 +9,6 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(autouse=True, params=["ops", "stream"])
-def decode_path(request, monkeypatch):
-    """Every model test runs on both decode paths: the per-op kernels and the
-    persistent stream (chosen when the model is created)."""
-    monkeypatch.setenv("GGC_DECODE_PATH", request.param)
-    return request.param
-
 from gguf_cuda import synth
 from tiny_models import forward_runs_hp, forward_runs_tensors, min_llama_hp, min_llama_tensors
 

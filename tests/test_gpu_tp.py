@@ -130,6 +130,37 @@ def test_tp_matches_oracle(ggc, orc, name, cfg, n_layers, vocab, allreduce):
         assert np.array_equal(res[0]["logits"], r["logits"])
 
 
+class LongPromptJob:
+    """An 80-token prompt: its prefix runs through the batched prefill (NCCL
+    all-reduce of the partial products), the last token and the decode through
+    the step graph."""
+
+    def __call__(self, ggc, ctx):
+        hp, ts = synth.make_model("llama2-7b-q4_k_m", n_layers=2, seed=3)
+        m = ggc.LlamaModel(hp, ts, max_ctx=256, ctx=ctx)
+        prompt = np.random.default_rng(11).integers(0, hp["vocab_size"], size=80).astype(np.uint32)
+        logits = m.forward(prompt, np.arange(80, dtype=np.int64))
+        ids = m.decode(16)
+        return dict(logits=logits, ids=ids)
+
+
+def test_tp_long_prompt_prefill_matches_oracle(ggc, orc):
+    _need_gpus()
+    res = run_ranks(LongPromptJob())
+    for r in res:
+        if isinstance(r, Exception):
+            raise r
+    hp, ts = synth.make_model("llama2-7b-q4_k_m", n_layers=2, seed=3)
+    o = orc.Model(hp, ts)
+    prompt = np.random.default_rng(11).integers(0, hp["vocab_size"], size=80).astype(np.uint32)
+    want = o.forward(prompt, np.arange(80, dtype=np.int64))
+    for r in res:
+        assert rel_l2(r["logits"], want) <= REL_L2, rel_l2(r["logits"], want)
+    assert all(np.array_equal(res[0]["logits"], r["logits"]) for r in res[1:])
+    assert all(r["ids"] == res[0]["ids"] for r in res[1:]) and len(res[0]["ids"]) == 16
+    assert res[0]["ids"][0] == orc.greedy(want)
+
+
 class NanJob:
     """NaN planted in the attn_output columns that only the last rank holds."""
 
