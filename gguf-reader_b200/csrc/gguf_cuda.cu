@@ -780,19 +780,28 @@ extern "C" int ggc_tensor_dequantize(ggc_ctx* ctx, const ggc_tensor* t, float* o
 
 namespace {
 
+// 64 weight rows per CTA, or 32 when 64-row CTAs would leave SMs idle
 template <int DT>
 struct RunMM {
-    static void run(ggc_ctx* ctx, const uint8_t* w, uint32_t n, uint32_t k, const __nv_bfloat16* xh,
-                    const __nv_bfloat16* xl, uint32_t m, uint32_t kpad, float* y, uint32_t ldy, const float* resid,
-                    int* errf, cudaError_t* err) {
+    static void run(ggc_ctx* ctx, const uint8_t* w, uint32_t n, uint32_t k, const uint8_t* xh, const uint8_t* xl,
+                    uint32_t m, uint32_t kpad, float* y, uint32_t ldy, const float* resid, int* errf,
+                    cudaError_t* err) {
         static std::once_flag once;
         static cudaError_t attr = cudaSuccess;
         std::call_once(once, [] {
-            attr = cudaFuncSetAttribute(k_mm_tc<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MM_SMEM);
+            attr = cudaFuncSetAttribute(k_mm_tc<DT, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mm_smem(64));
+            if (attr == cudaSuccess)
+                attr = cudaFuncSetAttribute(k_mm_tc<DT, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)mm_smem(32));
         });
         if (attr != cudaSuccess) { *err = attr; return; }
-        const dim3 grid(cdiv<uint32_t>(n, MM_BN), cdiv<uint32_t>(m, MM_TOKENS));
-        *err = launch(ctx, k_mm_tc<DT>, grid, dim3(MM_THREADS), MM_SMEM, w, n, k, xh, xl, m, kpad, y, ldy, resid, errf);
+        const uint32_t mblocks = cdiv<uint32_t>(m, MM_BM), gy = cdiv<uint32_t>(mblocks, MM_MB);
+        if (cdiv<uint32_t>(n, 64) * gy >= (uint32_t)ctx->num_sms)
+            *err = launch(ctx, k_mm_tc<DT, 64>, dim3(cdiv<uint32_t>(n, 64), gy), dim3(MM_THREADS), mm_smem(64), w, n, k,
+                          xh, xl, m, kpad, y, ldy, resid, errf);
+        else
+            *err = launch(ctx, k_mm_tc<DT, 32>, dim3(cdiv<uint32_t>(n, 32), gy), dim3(MM_THREADS), mm_smem(32), w, n, k,
+                          xh, xl, m, kpad, y, ldy, resid, errf);
     }
 };
 
@@ -805,16 +814,18 @@ int ctx_errf(ggc_ctx* ctx, int** out) {
     return GGC_OK;
 }
 
-// x [m][k] f32 (device) -> bf16 hi / lo [m][kpad] in staging buffers 3 / 4
+// x [m][k] f32 (device) -> bf16 hi / lo tiles (k_x_split's blocked layout,
+// rows padded to 128, columns to 64) in staging buffers 3 / 4
 int split_rows(ggc_ctx* ctx, const float* x, const float* x2, uint32_t m, uint32_t k, uint32_t ldx, int pro,
-               __nv_bfloat16** xh, __nv_bfloat16** xl, uint32_t* kpad) {
+               uint8_t** xh, uint8_t** xl, uint32_t* kpad) {
     *kpad = (k + MM_BK - 1) / MM_BK * MM_BK;
-    const size_t bytes = (size_t)m * *kpad * sizeof(__nv_bfloat16);
+    const uint32_t mpad = (m + MM_BM - 1) / MM_BM * MM_BM;
+    const size_t bytes = (size_t)mpad * *kpad * 2;
     GGC_TRY(ensure_stage(ctx, 3, bytes));
     GGC_TRY(ensure_stage(ctx, 4, bytes));
-    *xh = (__nv_bfloat16*)ctx->stage[3];
-    *xl = (__nv_bfloat16*)ctx->stage[4];
-    GGC_CUDA_TRY(launch(ctx, k_x_split, dim3(m), dim3(SPLIT_THREADS), 0, x, x2, m, k, ldx, *kpad, pro, *xh, *xl));
+    *xh = (uint8_t*)ctx->stage[3];
+    *xl = (uint8_t*)ctx->stage[4];
+    GGC_CUDA_TRY(launch(ctx, k_x_split, dim3(mpad), dim3(SPLIT_THREADS), 0, x, x2, m, k, ldx, *kpad, pro, *xh, *xl));
     return GGC_OK;
 }
 
@@ -838,13 +849,13 @@ extern "C" int ggc_tensor_matmul(ggc_ctx* ctx, const ggc_tensor* t, const float*
     GGC_TRY(dev_out(ctx, 2, y, m * rows * sizeof(float), &dy, &staged));
     int* errf = nullptr;
     GGC_TRY(ctx_errf(ctx, &errf));
-    __nv_bfloat16 *xh, *xl;
+    uint8_t *xh, *xl;
     uint32_t kpad = 0;
     GGC_TRY(split_rows(ctx, (const float*)dx, nullptr, (uint32_t)m, (uint32_t)cols, (uint32_t)cols, MMP_PLAIN, &xh, &xl,
                        &kpad));
     cudaError_t err = cudaSuccess;
     if (!dispatch_dtype<RunMM>(t->dtype, ctx, (const uint8_t*)t->raw, (uint32_t)rows, (uint32_t)cols,
-                               (const __nv_bfloat16*)xh, (const __nv_bfloat16*)xl, (uint32_t)m, kpad, (float*)dy,
+                               (const uint8_t*)xh, (const uint8_t*)xl, (uint32_t)m, kpad, (float*)dy,
                                (uint32_t)rows, (const float*)nullptr, errf, &err))
         return set_dequant_error(t->dtype, 0, 0, "matmul dtype");
     GGC_CUDA_TRY(err);
@@ -1747,7 +1758,7 @@ int check_run(ggc_model* m) {
 }
 
 // ---- batched prefill (prefill.cuh) -------------------------------------------
-constexpr uint32_t PF_CHUNK = MM_TOKENS;     // tokens per pass (one k_mm_tc grid row)
+constexpr uint32_t PF_CHUNK = MM_TOKENS;     // tokens per pass (one k_mm_tc grid row: W dequantised once)
 constexpr uint64_t PREFILL_MIN = 64;          // batch the prompt prefix from this many tokens on
 
 template <int DT>
@@ -1777,12 +1788,12 @@ int ensure_prefill_buffers(ggc_model* m) {
 int mm_raw(ggc_model* m, const RawMat& w, const float* x, const float* x2, uint32_t n, uint32_t ldx, int pro, float* y,
            uint32_t ldy, const float* resid) {
     ggc_ctx* ctx = m->ctx;
-    __nv_bfloat16 *xh, *xl;
+    uint8_t *xh, *xl;
     uint32_t kpad = 0;
     GGC_TRY(split_rows(ctx, x, x2, n, w.cols, ldx, pro, &xh, &xl, &kpad));
     cudaError_t err = cudaSuccess;
-    if (!dispatch_dtype<RunMM>(w.dtype, ctx, (const uint8_t*)w.p, w.rows, w.cols, (const __nv_bfloat16*)xh,
-                               (const __nv_bfloat16*)xl, n, kpad, y, ldy, resid, m->errf, &err))
+    if (!dispatch_dtype<RunMM>(w.dtype, ctx, (const uint8_t*)w.p, w.rows, w.cols, (const uint8_t*)xh,
+                               (const uint8_t*)xl, n, kpad, y, ldy, resid, m->errf, &err))
         return set_dequant_error(w.dtype, 0, 0, "prefill dtype");
     GGC_CUDA_TRY(err);
     return GGC_OK;

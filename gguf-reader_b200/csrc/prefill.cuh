@@ -1,24 +1,23 @@
 // prefill.cuh -- the batched (prompt / prefill) path: a quantized-weight matrix
 // product on the 5th-generation tensor cores, and the per-token kernels around it.
 //
-// k_mm_tc<DT>: Y[m][n] (+)= X[m][k] . W[n][k]^T with W in raw GGUF blocks.
-//   * CTA = 64 weight rows (MM_BN) x up to 512 tokens (MM_MB M-blocks of 128):
-//     the f32 accumulators of all its tokens live in tensor memory (4 x 64
-//     columns of 128 lanes), so each W tile is read from HBM and dequantised
-//     (bit-exact, dequant.cuh) once per CTA and X tiles come from L2.
+// k_mm_tc<DT, BN>: Y[m][n] (+)= X[m][k] . W[n][k]^T with W in raw GGUF blocks.
+//   * CTA = BN (64, or 32 for narrow W) weight rows x up to 512 tokens (MM_MB
+//     M-blocks of 128): the f32 accumulators of all its tokens live in tensor
+//     memory (4 x BN columns of 128 lanes), so each W tile is read from HBM and
+//     dequantised (bit-exact, dequant.cuh) once per CTA and X tiles come from L2.
 //   * Precision: W and X are each split into bf16 hi + lo (v = hi + lo to ~16
 //     mantissa bits) and D accumulates hi.hi + hi.lo + lo.hi in f32
 //     (tcgen05.mma kind::f16, bf16 operands): ~1e-5 relative per product, within
 //     the 1e-4 relative-L2 parity bar that plain bf16 (~1e-3) misses.
-//   * Per K step of 64: the 256 threads dequantise the W tile and copy the X
-//     tiles into shared memory in the canonical K-major layout without swizzle
+//   * Shared-memory operands use the canonical K-major layout without swizzle
 //     (8-row x 16-byte core matrices: byte (row, kchunk) = kchunk*rows*16 +
-//     row*16, so LBO = rows*16 between K chunks, SBO = 128 between 8-row groups),
-//     then one thread issues 3 MMAs of K = 16 per M-block and K/16 step and
-//     commits them to an mbarrier, which the threads wait on (bounded) before
-//     overwriting the tiles.
-//   * Epilogue: warps 0-3 read their 32 TMEM lanes (tokens) with tcgen05.ld and
-//     write Y rows (+ the residual when given).  TMEM is freed on every path.
+//     row*16, so LBO = rows*16 between K chunks, SBO = 128 between 8-row
+//     groups); X arrives in that layout by bulk copy (k_x_split writes it so),
+//     W is dequantised into it by 8 warps while one issuer thread keeps the X
+//     copies and the MMAs going (mbarrier rings, see the kernel).
+//   * Epilogue: tcgen05.ld of the TMEM rows (tokens), Y (+ residual) stores.
+//     TMEM is freed on every path; every wait is bounded.
 #pragma once
 #include <cuda_bf16.h>
 #include "common.cuh"
@@ -28,19 +27,20 @@
 
 namespace ggc {
 
-constexpr int MM_BN = 64;                  // weight rows per CTA (UMMA N)
 constexpr int MM_BM = 128;                 // tokens per M-block (UMMA M, TMEM lanes)
-constexpr int MM_MB = 4;                   // M-blocks per CTA
+constexpr int MM_MB = 4;                   // M-blocks per CTA (512 tokens: W dequantised once)
 constexpr int MM_BK = 64;                  // K per stage
-constexpr int MM_THREADS = 256;
+constexpr int MM_DQ_THREADS = 256;         // 8 dequantising / epilogue warps
+constexpr int MM_THREADS = MM_DQ_THREADS + 32;   // + the issuer warp (TMEM owner, X copies, MMAs)
+constexpr int MM_XS = 4;                   // X tile ring slots
 constexpr uint32_t MM_TOKENS = MM_BM * MM_MB;
-constexpr uint32_t MM_TMEM_COLS = MM_MB * MM_BN;            // 256 (a power of two >= 32)
-constexpr uint32_t MM_W_BYTES = MM_BN * MM_BK * 2;          // one bf16 W tile
-constexpr uint32_t MM_X_BYTES = MM_BM * MM_BK * 2;          // one bf16 X tile
-constexpr uint32_t MM_SMEM = 2 * MM_W_BYTES + 2 * MM_MB * MM_X_BYTES;   // 144 KB
-// instruction descriptor: D f32, A/B bf16, both K-major, N = 64, M = 128
-constexpr uint32_t MM_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(MM_BN >> 3) << 17) |
-                              ((uint32_t)(MM_BM >> 4) << 24);
+constexpr uint32_t MM_X_BYTES = MM_BM * MM_BK * 2;          // one bf16 X tile (hi or lo), 16 KB
+constexpr uint32_t mm_w_bytes(int bn) { return (uint32_t)bn * MM_BK * 2; }
+constexpr uint32_t mm_smem(int bn) { return 2 * 2 * mm_w_bytes(bn) + MM_XS * 2 * MM_X_BYTES; }
+// instruction descriptor: D f32, A/B bf16, both K-major, N = bn, M = 128
+constexpr uint32_t mm_idesc(int bn) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(MM_BM >> 4) << 24);
+}
 
 // shared-memory matrix descriptor: K-major, no swizzle, version 1
 __device__ __forceinline__ uint64_t mm_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -92,18 +92,91 @@ __device__ __forceinline__ void split8(const float* v, uint4& hi, uint4& lo) {
     lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
-// X rows -> bf16 hi / lo [mpad][kpad] (zero beyond m and k), with the row's
-// RMSNorm (ops.rs:262-274, f64 sum of squares) or silu(gate) * up applied first.
+// Elements e0 .. e0+7 (e0 % 8 == 0) of one block of >= 8 elements: the deq_elem arithmetic with
+// the per-sub-block factors computed once (the same operations per element, so
+// the values are bit-identical to deq_elem's).
+template <int DT>
+__device__ __forceinline__ void deq8(const uint8_t* b, int e0, float* v) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = deq_elem<DT>(b, e0 + j);
+}
+// (blocks of 18 / 34 / 210 bytes start 2-byte aligned in a raw row, 144-byte
+// blocks 16-byte aligned: the loads below use the widest access that allows)
+__device__ __forceinline__ uint16_t ld_a16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
+template <> __device__ __forceinline__ void deq8<GGC_Q4_0>(const uint8_t* b, int e0, float* v) {
+    const float d = f16_ref(ld_a16(b));
+    const uint32_t w = (uint32_t)ld_a16(b + 2 + (e0 >> 1)) | ((uint32_t)ld_a16(b + 4 + (e0 >> 1)) << 16);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t byte = (w >> (8 * j)) & 0xFF;
+        v[2 * j] = __fmul_rn(d, (float)((int)(byte & 0xF) - 8));
+        v[2 * j + 1] = __fmul_rn(d, (float)((int)(byte >> 4) - 8));
+    }
+}
+template <> __device__ __forceinline__ void deq8<GGC_Q8_0>(const uint8_t* b, int e0, float* v) {
+    const float d = f16_ref(ld_a16(b));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint16_t h = ld_a16(b + 2 + e0 + 2 * j);
+        v[2 * j] = __fmul_rn(d, (float)(int8_t)(h & 0xFF));
+        v[2 * j + 1] = __fmul_rn(d, (float)(int8_t)(h >> 8));
+    }
+}
+template <> __device__ __forceinline__ void deq8<GGC_Q4_K>(const uint8_t* b, int e0, float* v) {
+    const uint4 h = *reinterpret_cast<const uint4*>(b);   // d, dmin, 12 scale bytes
+    const float d = f16_ref((uint16_t)(h.x & 0xFFFF)), dmin = f16_ref((uint16_t)(h.x >> 16));
+    const int group = e0 >> 6, in_grp = e0 & 63, is_high = in_grp >> 5, j = group * 2 + is_high;
+    const uint32_t sw[3] = {h.y, h.z, h.w};
+    auto sb = [&](int i) { return (sw[i >> 2] >> (8 * (i & 3))) & 0xFFu; };   // scale byte i (quant.rs:116-124)
+    uint32_t sc, mn;
+    if (j < 4) {
+        sc = sb(j) & 0x3F;
+        mn = sb(j + 4) & 0x3F;
+    } else {
+        sc = (sb(j + 4) & 0x0F) | ((sb(j - 4) >> 6) << 4);
+        mn = (sb(j + 4) >> 4) | ((sb(j) >> 6) << 4);
+    }
+    const float s1 = __fmul_rn((float)sc, d), s2 = __fmul_rn((float)mn, dmin);
+    const uint2 q8 = *reinterpret_cast<const uint2*>(b + 16 + group * 32 + (in_grp & 31));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t byte = ((i < 4 ? q8.x : q8.y) >> (8 * (i & 3))) & 0xFF;
+        const uint32_t val = is_high ? (byte >> 4) : (byte & 0x0F);
+        v[i] = __fsub_rn(__fmul_rn(s1, (float)val), s2);
+    }
+}
+template <> __device__ __forceinline__ void deq8<GGC_Q6_K>(const uint8_t* b, int e0, float* v) {
+    const float d = f16_ref(ld_a16(b + 208));
+    const int n = e0 >> 7, r = e0 & 127, t = r >> 5, l = r & 31, is = l / 16;
+    const uint8_t* ql = b + n * 64 + ((t & 1) ? 32 : 0) + l;
+    const uint8_t* qh = b + 128 + n * 32 + l;
+    const float ds = __fmul_rn(d, (float)(int8_t)b[192 + n * 8 + is + 2 * t]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint16_t lw = ld_a16(ql + 2 * j), hw = ld_a16(qh + 2 * j);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const uint32_t lb = (lw >> (8 * k)) & 0xFF, hb = (hw >> (8 * k)) & 0xFF;
+            const uint32_t q = ((t < 2) ? (lb & 0xF) : (lb >> 4)) | (((hb >> (2 * t)) & 3) << 4);
+            v[2 * j + k] = __fmul_rn(ds, (float)((int32_t)q - 32));
+        }
+    }
+}
+
+// X rows -> bf16 hi / lo in the blocked tile layout the product loads with one
+// bulk copy per tile: tile (M-block g, K step kb) is 16 KB at ((g * nk + kb) *
+// 16 KB), inside it byte kchunk * 2048 + row * 16 (the no-swizzle core-matrix
+// layout).  Rows m .. mpad-1 and columns k .. kpad-1 are zero.  The row's
+// RMSNorm (ops.rs:262-274, f64 sum of squares) or silu(gate) * up comes first.
 enum MmPro : int { MMP_PLAIN = 0, MMP_RMSNORM = 1, MMP_SWIGLU = 2 };
 constexpr int SPLIT_THREADS = 256;
 
 __global__ void __launch_bounds__(SPLIT_THREADS) k_x_split(const float* __restrict__ x, const float* __restrict__ x2,
                                                            uint32_t m, uint32_t k, uint32_t ldx, uint32_t kpad, int pro,
-                                                           __nv_bfloat16* __restrict__ xh,
-                                                           __nv_bfloat16* __restrict__ xl) {
+                                                           uint8_t* __restrict__ xh, uint8_t* __restrict__ xl) {
     pdl_trigger();
     pdl_wait();
-    const uint32_t row = blockIdx.x;
+    const uint32_t row = blockIdx.x, nk = kpad / MM_BK;
     __shared__ double red[SPLIT_THREADS / 32];
     __shared__ float s_scale;
     const float* xr = x + (size_t)row * ldx;
@@ -123,6 +196,7 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_x_split(const float* __restri
         __syncthreads();
         scale = s_scale;
     }
+    const size_t tile0 = (size_t)(row / MM_BM) * nk * MM_X_BYTES + (row % MM_BM) * 16;
     for (uint32_t c = threadIdx.x; c < kpad / 8; c += SPLIT_THREADS) {
         float v[8];
 #pragma unroll
@@ -138,37 +212,52 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_x_split(const float* __restri
         }
         uint4 h, l;
         split8(v, h, l);
-        *reinterpret_cast<uint4*>(xh + (size_t)row * kpad + c * 8) = h;
-        *reinterpret_cast<uint4*>(xl + (size_t)row * kpad + c * 8) = l;
+        const size_t off = tile0 + (size_t)(c / 8) * MM_X_BYTES + (c % 8) * (MM_BM * 16);
+        *reinterpret_cast<uint4*>(xh + off) = h;
+        *reinterpret_cast<uint4*>(xl + off) = l;
     }
 }
 
-template <int DT>
+// Y[m][n] (+)= X . W^T.  Block = 8 dequantising warps + 1 issuer warp.
+//   dequant warps: W tile of K step kb (BN rows x 64) -> bf16 hi / lo into W
+//     slot kb % 2 (after the MMAs of kb - 2 freed it: wfree), arrive on wfull;
+//   issuer (warp 8, one lane): keeps MM_XS X tiles (one M-block x K step, hi +
+//     lo) in flight by bulk copy (xfull; a slot is refilled after the MMAs that
+//     read it completed: xfree), and for each K step waits for the W slot, then
+//     per M-block for its X tile, issues 4 x 3 MMAs into the M-block's TMEM
+//     columns and commits them to xfree; the step's commit frees the W slot, the
+//     last one signals `done`;
+//   epilogue: the 8 warps read TMEM (warp w: lanes 32 (w % 4).., M-blocks of
+//     half w / 4) and write Y (+ the residual).
+// Every wait is bounded (ERRF_TIMEOUT); no thread leaves early, warp 8 frees TMEM.
+template <int DT, int BN>
 __global__ void __launch_bounds__(MM_THREADS, 1)
-    k_mm_tc(const uint8_t* __restrict__ w, uint32_t n_rows, uint32_t k_cols, const __nv_bfloat16* __restrict__ xh,
-            const __nv_bfloat16* __restrict__ xl, uint32_t m, uint32_t kpad, float* y, uint32_t ldy,
-            const float* resid, int* errf) {
+    k_mm_tc(const uint8_t* __restrict__ w, uint32_t n_rows, uint32_t k_cols, const uint8_t* __restrict__ xh,
+            const uint8_t* __restrict__ xl, uint32_t m, uint32_t kpad, float* y, uint32_t ldy, const float* resid,
+            int* errf) {
     constexpr int BS = block_size_of(DT), BB = block_bytes_of(DT);
+    constexpr uint32_t WB = mm_w_bytes(BN), TCOLS = MM_MB * BN, IDESC = mm_idesc(BN);
     extern __shared__ __align__(128) uint8_t smem[];   // no-swizzle descriptors need 16-byte alignment
-    __shared__ uint64_t mbar;
+    __shared__ uint64_t wfull[2], wfree[2], xfull[MM_XS], xfree[MM_XS], done;
     __shared__ uint32_t s_tmem;
-    uint8_t* wsh = smem;
-    uint8_t* wsl = smem + MM_W_BYTES;
-    uint8_t* xsh = smem + 2 * MM_W_BYTES;
-    uint8_t* xsl = xsh + MM_MB * MM_X_BYTES;
+    uint8_t* wsm = smem;                  // [2 slots][hi, lo][WB]
+    uint8_t* xsm = smem + 4 * WB;         // [MM_XS slots][hi, lo][MM_X_BYTES]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t n0 = blockIdx.x * MM_BN, m0 = blockIdx.y * MM_TOKENS;
-    const uint32_t left = m - m0, nmb = min((uint32_t)MM_MB, (left + MM_BM - 1) / MM_BM);
+    const uint32_t n0 = blockIdx.x * BN, gmb0 = blockIdx.y * MM_MB;
+    const uint32_t mpad = (m + MM_BM - 1) / MM_BM * MM_BM, nmb = min((uint32_t)MM_MB, mpad / MM_BM - gmb0);
+    const uint32_t nk = kpad / MM_BK;
     const uint64_t row_bytes = (uint64_t)(k_cols / BS) * BB;
 
-    if (warp == 0) {
+    if (warp == 8) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&s_tmem)),
-                     "r"(MM_TMEM_COLS)
+                     "r"(TCOLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (tid == 0) {
-        mbar_init(&mbar, 1);
+        for (int i = 0; i < 2; ++i) { mbar_init(&wfull[i], MM_DQ_THREADS); mbar_init(&wfree[i], 1); }
+        for (int i = 0; i < MM_XS; ++i) { mbar_init(&xfull[i], 1); mbar_init(&xfree[i], 1); }
+        mbar_init(&done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     tc_fence_before();
@@ -178,104 +267,120 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
     pdl_trigger();
     pdl_wait();
 
-    const uint32_t nk = kpad / MM_BK;
-    bool ok = true;
-    uint32_t commits = 0;   // commit groups issued (one per K step)
-    for (uint32_t kb = 0; kb < nk; ++kb) {
-        if (kb > 0 && !__syncthreads_and(mbar_wait(&mbar, (kb - 1) & 1, errf))) {   // previous MMAs read the tiles
-            ok = false;
-            break;
-        }
-        // W tile: 64 rows x 8 chunks of 8 consecutive elements, dequantised and split
-        for (uint32_t it = tid; it < MM_BN * 8; it += MM_THREADS) {
-            const uint32_t r = it >> 3, kc = it & 7, n = n0 + r, k0 = kb * MM_BK + kc * 8;
-            float v[8];
-            if (n < n_rows && k0 < k_cols) {
-                const uint8_t* rowp = w + (uint64_t)n * row_bytes;
+    if (warp < 8) {
+        // ---------------- dequantising warps ----------------
+        for (uint32_t kb = 0; kb < nk; ++kb) {
+            const uint32_t slot = kb & 1, use = kb >> 1;
+            if (use > 0) mbar_wait(&wfree[slot], (use - 1) & 1, errf);
+            uint8_t* wh = wsm + slot * 2 * WB;
+            uint8_t* wl = wh + WB;
+            for (uint32_t it = tid; it < (uint32_t)BN * 8; it += MM_DQ_THREADS) {
+                const uint32_t r = it % BN, kc = it / BN, n = n0 + r, k0 = kb * MM_BK + kc * 8;
+                float v[8];
+                if (BS >= 8 && n < n_rows && k0 + 8 <= k_cols) {   // the 8 elements share one block
+                    deq8<DT>(w + (uint64_t)n * row_bytes + (uint64_t)(k0 / BS) * BB, (int)(k0 % BS), v);
+                } else {
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const uint32_t e = k0 + j;
-                    v[j] = e < k_cols ? deq_elem<DT>(rowp + (uint64_t)(e / BS) * BB, (int)(e % BS)) : 0.f;
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t e = k0 + j;
+                        v[j] = (n < n_rows && e < k_cols)
+                                   ? deq_elem<DT>(w + (uint64_t)n * row_bytes + (uint64_t)(e / BS) * BB, (int)(e % BS))
+                                   : 0.f;
+                    }
                 }
-            } else {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) v[j] = 0.f;
+                uint4 h, l;
+                split8(v, h, l);
+                *reinterpret_cast<uint4*>(wh + kc * (BN * 16) + r * 16) = h;
+                *reinterpret_cast<uint4*>(wl + kc * (BN * 16) + r * 16) = l;
             }
-            uint4 h, l;
-            split8(v, h, l);
-            *reinterpret_cast<uint4*>(wsh + kc * (MM_BN * 16) + r * 16) = h;
-            *reinterpret_cast<uint4*>(wsl + kc * (MM_BN * 16) + r * 16) = l;
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic stores -> tensor-core reads
+            mbar_arrive(&wfull[slot]);
         }
-        // X tiles of the CTA's M-blocks
-        for (uint32_t it = tid; it < nmb * MM_BM * 8; it += MM_THREADS) {
-            const uint32_t mb = it / (MM_BM * 8), rem = it % (MM_BM * 8), r = rem >> 3, kc = rem & 7;
-            const uint32_t row = m0 + mb * MM_BM + r;
-            uint4 h = make_uint4(0, 0, 0, 0), l = h;
-            if (row < m) {
-                const size_t off = (size_t)row * kpad + kb * MM_BK + kc * 8;
-                h = *reinterpret_cast<const uint4*>(xh + off);
-                l = *reinterpret_cast<const uint4*>(xl + off);
+    } else if (lane == 0) {
+        // ---------------- issuer ----------------
+        const uint32_t total = nk * nmb;   // X tiles, K-step-major
+        auto load_x = [&](uint32_t seq) {
+            const uint32_t q = seq % MM_XS, kb = seq / nmb, mb = seq % nmb;
+            if (seq >= (uint32_t)MM_XS) mbar_wait(&xfree[q], ((seq / MM_XS) - 1) & 1, errf);
+            mbar_arrive_expect_tx(&xfull[q], 2 * MM_X_BYTES);
+            const size_t src = ((size_t)(gmb0 + mb) * nk + kb) * MM_X_BYTES;
+            bulk_g2s(xsm + q * 2 * MM_X_BYTES, xh + src, MM_X_BYTES, &xfull[q]);
+            bulk_g2s(xsm + q * 2 * MM_X_BYTES + MM_X_BYTES, xl + src, MM_X_BYTES, &xfull[q]);
+        };
+        // the CTA's weight rows into L2 ahead of the dequantising warps: one bulk
+        // prefetch per row (16-byte aligned, clipped to the matrix)
+        {
+            const uintptr_t wend = ((uintptr_t)w + (uint64_t)n_rows * row_bytes) & ~(uintptr_t)15;
+            for (uint32_t r = 0; r < (uint32_t)BN && n0 + r < n_rows; ++r) {
+                const uintptr_t a = ((uintptr_t)w + (uint64_t)(n0 + r) * row_bytes) & ~(uintptr_t)15;
+                uintptr_t e = ((uintptr_t)w + (uint64_t)(n0 + r + 1) * row_bytes + 15) & ~(uintptr_t)15;
+                e = e < wend ? e : wend;
+                if (e > a)
+                    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"((uint32_t)(e - a)) : "memory");
             }
-            const uint32_t so = mb * MM_X_BYTES + kc * (MM_BM * 16) + r * 16;
-            *reinterpret_cast<uint4*>(xsh + so) = h;
-            *reinterpret_cast<uint4*>(xsl + so) = l;
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic stores -> tensor-core reads
-        __syncthreads();
-        if (tid == 0) {
+        for (uint32_t seq = 0; seq + 1 < (uint32_t)MM_XS && seq < total; ++seq) load_x(seq);
+        const uint32_t w0 = smem_addr(wsm), x0 = smem_addr(xsm);
+        for (uint32_t kb = 0; kb < nk; ++kb) {
+            const uint32_t slot = kb & 1;
+            mbar_wait(&wfull[slot], (kb >> 1) & 1, errf);
             tc_fence_after();
-            const uint32_t a_h = smem_addr(xsh), a_l = smem_addr(xsl), b_h = smem_addr(wsh), b_l = smem_addr(wsl);
+            const uint32_t bh = w0 + slot * 2 * WB, bl = bh + WB;
             for (uint32_t mb = 0; mb < nmb; ++mb) {
-                const uint32_t d = tmem + mb * MM_BN;
+                const uint32_t seq = kb * nmb + mb, q = seq % MM_XS;
+                mbar_wait(&xfull[q], (seq / MM_XS) & 1, errf);
+                tc_fence_after();
+                const uint32_t ah = x0 + q * 2 * MM_X_BYTES, al = ah + MM_X_BYTES;
+                const uint32_t d = tmem + mb * BN;
 #pragma unroll
                 for (uint32_t j = 0; j < MM_BK / 16; ++j) {
-                    const uint32_t ao = mb * MM_X_BYTES + 2 * j * (MM_BM * 16), bo = 2 * j * (MM_BN * 16);
-                    const uint64_t ah = mm_desc(a_h + ao, MM_BM * 16, 128), al = mm_desc(a_l + ao, MM_BM * 16, 128);
-                    const uint64_t bh = mm_desc(b_h + bo, MM_BN * 16, 128), bl = mm_desc(b_l + bo, MM_BN * 16, 128);
-                    tc_mma(d, ah, bh, MM_IDESC, (kb > 0 || j > 0) ? 1u : 0u);
-                    tc_mma(d, ah, bl, MM_IDESC, 1u);
-                    tc_mma(d, al, bh, MM_IDESC, 1u);
+                    const uint64_t dah = mm_desc(ah + 2 * j * (MM_BM * 16), MM_BM * 16, 128);
+                    const uint64_t dal = mm_desc(al + 2 * j * (MM_BM * 16), MM_BM * 16, 128);
+                    const uint64_t dbh = mm_desc(bh + 2 * j * (BN * 16), BN * 16, 128);
+                    const uint64_t dbl = mm_desc(bl + 2 * j * (BN * 16), BN * 16, 128);
+                    tc_mma(d, dah, dbh, IDESC, (kb > 0 || j > 0) ? 1u : 0u);
+                    tc_mma(d, dah, dbl, IDESC, 1u);
+                    tc_mma(d, dal, dbh, IDESC, 1u);
                 }
+                tc_commit(&xfree[q]);
+                if (seq + MM_XS - 1 < total) load_x(seq + MM_XS - 1);   // into the slot of tile seq - 1
             }
-            tc_commit(&mbar);
+            tc_commit(&wfree[slot]);
         }
-        commits = kb + 1;
+        tc_commit(&done);
     }
-    if (ok && commits > 0) ok = __syncthreads_and(mbar_wait(&mbar, (commits - 1) & 1, errf));
-    if (ok) {
+    // ---------------- epilogue ----------------
+    if (warp < 8) {
+        mbar_wait(&done, 0, errf);
         tc_fence_after();
-        if (warp < 4) {
-            for (uint32_t mb = 0; mb < nmb; ++mb) {
-                const uint32_t row = m0 + mb * MM_BM + warp * 32 + lane;
+        const uint32_t quarter = warp & 3, half = warp >> 2;
+        for (uint32_t mb = half * 2; mb < half * 2 + 2 && mb < nmb; ++mb) {
+            const uint32_t row = (gmb0 + mb) * MM_BM + quarter * 32 + lane;
 #pragma unroll 1
-                for (uint32_t c0 = 0; c0 < MM_BN; c0 += 16) {
-                    float v[16];
-                    tc_ld16(tmem + ((uint32_t)(warp * 32) << 16) + mb * MM_BN + c0, v);
-                    if (row < m) {
+            for (uint32_t c0 = 0; c0 < (uint32_t)BN; c0 += 16) {
+                float v[16];
+                tc_ld16(tmem + ((quarter * 32) << 16) + mb * BN + c0, v);
+                if (row < m) {
 #pragma unroll
-                        for (int c = 0; c < 16; ++c) {
-                            const uint32_t n = n0 + c0 + c;
-                            if (n < n_rows) {
-                                const size_t idx = (size_t)row * ldy + n;
-                                y[idx] = resid ? __fadd_rn(resid[idx], v[c]) : v[c];
-                            }
+                    for (int c = 0; c < 16; ++c) {
+                        const uint32_t n = n0 + c0 + c;
+                        if (n < n_rows) {
+                            const size_t idx = (size_t)row * ldy + n;
+                            y[idx] = resid ? __fadd_rn(resid[idx], v[c]) : v[c];
                         }
                     }
                 }
             }
         }
-    } else if (commits > 0) {
-        // a wait gave up: wait once more (bounded) for the MMAs in flight before freeing TMEM
-        mbar_wait(&mbar, (commits - 1) & 1, errf);
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) {
+    if (warp == 8) {
+        __syncwarp();   // .sync.aligned: the whole warp, converged
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(MM_TMEM_COLS) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS) : "memory");
     }
 }
-
 
 // ---- the per-token kernels of the batched forward ---------------------------
 
