@@ -121,9 +121,9 @@ struct ggc_ctx {
     uint64_t launches = 0;
     // owner + one per live model / tensor: the context outlives everything made on it
     std::atomic<int> refs{1};
-    // staging buffers for host arguments (0-2) and matmul operands (3-4)
-    void* stage[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
-    size_t stage_cap[5] = {0, 0, 0, 0, 0};
+    // staging buffers for host arguments (0-2), matmul operands (3-4) and split-K partials (5)
+    void* stage[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+    size_t stage_cap[6] = {0, 0, 0, 0, 0, 0};
     int* errf = nullptr;   // device error flags of the context's own launches
 };
 
@@ -294,7 +294,7 @@ void ctx_release(ggc_ctx* ctx) {
     {
         DeviceGuard g(ctx->device);
         cudaStreamSynchronize(ctx->stream);
-        for (int i = 0; i < 5; ++i)
+        for (int i = 0; i < 6; ++i)
             if (ctx->stage[i]) cudaFree(ctx->stage[i]);
         if (ctx->errf) cudaFree(ctx->errf);
         if (ctx->comm) nccl().CommDestroy(ctx->comm);
@@ -780,7 +780,8 @@ extern "C" int ggc_tensor_dequantize(ggc_ctx* ctx, const ggc_tensor* t, float* o
 
 namespace {
 
-// 64 weight rows per CTA, or 32 when 64-row CTAs would leave SMs idle
+// 128 weight rows x 512 tokens per CTA; K split over enough CTAs to fill the
+// SMs (partials summed in split order by k_mm_reduce)
 template <int DT>
 struct RunMM {
     static void run(ggc_ctx* ctx, const uint8_t* w, uint32_t n, uint32_t k, const uint8_t* xh, const uint8_t* xl,
@@ -789,19 +790,31 @@ struct RunMM {
         static std::once_flag once;
         static cudaError_t attr = cudaSuccess;
         std::call_once(once, [] {
-            attr = cudaFuncSetAttribute(k_mm_tc<DT, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mm_smem(64));
-            if (attr == cudaSuccess)
-                attr = cudaFuncSetAttribute(k_mm_tc<DT, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            (int)mm_smem(32));
+            attr = cudaFuncSetAttribute(k_mm_tc<DT, MM_BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)mm_smem(MM_BN));
         });
         if (attr != cudaSuccess) { *err = attr; return; }
-        const uint32_t mblocks = cdiv<uint32_t>(m, MM_BM), gy = cdiv<uint32_t>(mblocks, MM_MB);
-        if (cdiv<uint32_t>(n, 64) * gy >= (uint32_t)ctx->num_sms)
-            *err = launch(ctx, k_mm_tc<DT, 64>, dim3(cdiv<uint32_t>(n, 64), gy), dim3(MM_THREADS), mm_smem(64), w, n, k,
-                          xh, xl, m, kpad, y, ldy, resid, errf);
-        else
-            *err = launch(ctx, k_mm_tc<DT, 32>, dim3(cdiv<uint32_t>(n, 32), gy), dim3(MM_THREADS), mm_smem(32), w, n, k,
-                          xh, xl, m, kpad, y, ldy, resid, errf);
+        const uint32_t gx = cdiv<uint32_t>(n, MM_BN), gy = cdiv<uint32_t>(cdiv<uint32_t>(m, MM_BM), MM_MB);
+        const uint32_t nk = kpad / MM_BK;
+        uint32_t ks = cdiv<uint32_t>((uint32_t)ctx->num_sms, gx * gy);
+        ks = ks < 1 ? 1 : (ks > nk ? nk : ks);
+        const uint32_t kb_per = cdiv<uint32_t>(nk, ks);
+        ks = cdiv<uint32_t>(nk, kb_per);   // no empty split
+        if (ks == 1) {
+            *err = launch(ctx, k_mm_tc<DT, MM_BN>, dim3(gx, gy, 1), dim3(MM_THREADS), mm_smem(MM_BN), w, n, k, xh, xl,
+                          m, kpad, kb_per, y, ldy, resid, errf);
+            return;
+        }
+        const size_t pbytes = (size_t)ks * m * n * sizeof(float);
+        int st = ensure_stage(ctx, 5, pbytes);
+        if (st != GGC_OK) { *err = cudaErrorMemoryAllocation; return; }
+        float* part = (float*)ctx->stage[5];
+        *err = launch(ctx, k_mm_tc<DT, MM_BN>, dim3(gx, gy, ks), dim3(MM_THREADS), mm_smem(MM_BN), w, n, k, xh, xl, m,
+                      kpad, kb_per, part, n, (const float*)nullptr, errf);
+        if (*err != cudaSuccess) return;
+        const uint64_t total = (uint64_t)m * n;
+        const unsigned grid = (unsigned)std::min<uint64_t>(cdiv<uint64_t>(total, 256), (uint64_t)ctx->num_sms * 8);
+        *err = launch(ctx, k_mm_reduce, dim3(grid), dim3(256), 0, (const float*)part, ks, m, n, y, ldy, resid);
     }
 };
 

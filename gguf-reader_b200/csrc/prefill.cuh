@@ -35,8 +35,9 @@ constexpr int MM_THREADS = MM_DQ_THREADS + 32;   // + the issuer warp (TMEM owne
 constexpr int MM_XS = 4;                   // X tile ring slots
 constexpr uint32_t MM_TOKENS = MM_BM * MM_MB;
 constexpr uint32_t MM_X_BYTES = MM_BM * MM_BK * 2;          // one bf16 X tile (hi or lo), 16 KB
+constexpr int MM_BN = 128;                 // weight rows per CTA (UMMA N); TMEM: MM_MB x 128 = all 512 columns
 constexpr uint32_t mm_w_bytes(int bn) { return (uint32_t)bn * MM_BK * 2; }
-constexpr uint32_t mm_smem(int bn) { return 2 * 2 * mm_w_bytes(bn) + MM_XS * 2 * MM_X_BYTES; }
+constexpr uint32_t mm_smem(int bn) { return 2 * 2 * mm_w_bytes(bn) + MM_XS * 2 * MM_X_BYTES; }   // 192 KB
 // instruction descriptor: D f32, A/B bf16, both K-major, N = bn, M = 128
 constexpr uint32_t mm_idesc(int bn) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(MM_BM >> 4) << 24);
@@ -233,8 +234,8 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_x_split(const float* __restri
 template <int DT, int BN>
 __global__ void __launch_bounds__(MM_THREADS, 1)
     k_mm_tc(const uint8_t* __restrict__ w, uint32_t n_rows, uint32_t k_cols, const uint8_t* __restrict__ xh,
-            const uint8_t* __restrict__ xl, uint32_t m, uint32_t kpad, float* y, uint32_t ldy, const float* resid,
-            int* errf) {
+            const uint8_t* __restrict__ xl, uint32_t m, uint32_t kpad, uint32_t kb_per, float* y, uint32_t ldy,
+            const float* resid, int* errf) {
     constexpr int BS = block_size_of(DT), BB = block_bytes_of(DT);
     constexpr uint32_t WB = mm_w_bytes(BN), TCOLS = MM_MB * BN, IDESC = mm_idesc(BN);
     extern __shared__ __align__(128) uint8_t smem[];   // no-swizzle descriptors need 16-byte alignment
@@ -245,7 +246,11 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t n0 = blockIdx.x * BN, gmb0 = blockIdx.y * MM_MB;
     const uint32_t mpad = (m + MM_BM - 1) / MM_BM * MM_BM, nmb = min((uint32_t)MM_MB, mpad / MM_BM - gmb0);
-    const uint32_t nk = kpad / MM_BK;
+    // split K: this CTA's K steps [kb0, kb0 + nk) of the kpad / 64; its output
+    // (a partial sum when gridDim.z > 1) goes to slice blockIdx.z of y
+    const uint32_t nk_all = kpad / MM_BK, kb0 = blockIdx.z * kb_per;
+    const uint32_t nk = kb0 < nk_all ? min(kb_per, nk_all - kb0) : 0u;
+    y += (size_t)blockIdx.z * m * ldy;
     const uint64_t row_bytes = (uint64_t)(k_cols / BS) * BB;
 
     if (warp == 8) {
@@ -274,8 +279,9 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
             if (use > 0) mbar_wait(&wfree[slot], (use - 1) & 1, errf);
             uint8_t* wh = wsm + slot * 2 * WB;
             uint8_t* wl = wh + WB;
-            for (uint32_t it = tid; it < (uint32_t)BN * 8; it += MM_DQ_THREADS) {
-                const uint32_t r = it % BN, kc = it / BN, n = n0 + r, k0 = kb * MM_BK + kc * 8;
+#pragma unroll
+            for (uint32_t it = tid; it < (uint32_t)BN * 8; it += MM_DQ_THREADS) {   // BN / 32 independent items
+                const uint32_t r = it % BN, kc = it / BN, n = n0 + r, k0 = (kb0 + kb) * MM_BK + kc * 8;
                 float v[8];
                 if (BS >= 8 && n < n_rows && k0 + 8 <= k_cols) {   // the 8 elements share one block
                     deq8<DT>(w + (uint64_t)n * row_bytes + (uint64_t)(k0 / BS) * BB, (int)(k0 % BS), v);
@@ -303,7 +309,7 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
             const uint32_t q = seq % MM_XS, kb = seq / nmb, mb = seq % nmb;
             if (seq >= (uint32_t)MM_XS) mbar_wait(&xfree[q], ((seq / MM_XS) - 1) & 1, errf);
             mbar_arrive_expect_tx(&xfull[q], 2 * MM_X_BYTES);
-            const size_t src = ((size_t)(gmb0 + mb) * nk + kb) * MM_X_BYTES;
+            const size_t src = ((size_t)(gmb0 + mb) * nk_all + kb0 + kb) * MM_X_BYTES;
             bulk_g2s(xsm + q * 2 * MM_X_BYTES, xh + src, MM_X_BYTES, &xfull[q]);
             bulk_g2s(xsm + q * 2 * MM_X_BYTES + MM_X_BYTES, xl + src, MM_X_BYTES, &xfull[q]);
         };
@@ -311,9 +317,11 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
         // prefetch per row (16-byte aligned, clipped to the matrix)
         {
             const uintptr_t wend = ((uintptr_t)w + (uint64_t)n_rows * row_bytes) & ~(uintptr_t)15;
+            const uint64_t c0 = (uint64_t)(kb0 * MM_BK) / BS * BB;
+            const uint64_t c1 = min((uint64_t)((kb0 + nk) * MM_BK + BS - 1) / BS * BB, row_bytes);
             for (uint32_t r = 0; r < (uint32_t)BN && n0 + r < n_rows; ++r) {
-                const uintptr_t a = ((uintptr_t)w + (uint64_t)(n0 + r) * row_bytes) & ~(uintptr_t)15;
-                uintptr_t e = ((uintptr_t)w + (uint64_t)(n0 + r + 1) * row_bytes + 15) & ~(uintptr_t)15;
+                const uintptr_t a = ((uintptr_t)w + (uint64_t)(n0 + r) * row_bytes + c0) & ~(uintptr_t)15;
+                uintptr_t e = ((uintptr_t)w + (uint64_t)(n0 + r) * row_bytes + c1 + 15) & ~(uintptr_t)15;
                 e = e < wend ? e : wend;
                 if (e > a)
                     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"((uint32_t)(e - a)) : "memory");
@@ -379,6 +387,22 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
         __syncwarp();   // .sync.aligned: the whole warp, converged
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS) : "memory");
+    }
+}
+
+// y[r][c] = (resid[r][c] +) sum over s of part[s][r][c], s in order: the split-K
+// partial products of k_mm_tc summed deterministically
+__global__ void __launch_bounds__(256) k_mm_reduce(const float* __restrict__ part, uint32_t ks, uint32_t m, uint32_t n,
+                                                   float* y, uint32_t ldy, const float* resid) {
+    pdl_trigger();
+    pdl_wait();
+    const uint64_t total = (uint64_t)m * n, slice = (uint64_t)m * n;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t r = i / n, c = i - r * n;
+        float v = part[i];
+        for (uint32_t s = 1; s < ks; ++s) v = __fadd_rn(v, part[s * slice + i]);
+        const size_t idx = (size_t)r * ldy + c;
+        y[idx] = resid ? __fadd_rn(resid[idx], v) : v;
     }
 }
 
