@@ -233,6 +233,17 @@ class LlamaModel:
         # cache rows hold this rank's kv heads under tensor parallelism
         self.kv_dim = hp["n_kv_heads"] // self.ctx.world * (hp["embed_dim"] // hp["n_heads"])
 
+    @classmethod
+    def from_gguf(cls, path, max_ctx: int = 2048, kv_f16: bool = False, ctx: Context | None = None):
+        """LlamaModel::new over a .gguf file (gguf_cuda.loader: header, HParams,
+        tensor names, the physical-span dtype re-inference)."""
+        from . import loader
+        f = loader.GgufFile.open(path)
+        hp, tensors = loader.model_tensors(f)
+        m = cls(hp, tensors, max_ctx=max_ctx, kv_f16=kv_f16, ctx=ctx)
+        m.gguf = f
+        return m
+
     def forward(self, tokens, positions, logits=None, want_logits=True):
         """LlamaModel::forward: logits (vocab f32) of the last token; appends K/V."""
         t = np.ascontiguousarray(tokens, dtype=np.uint32) if not hasattr(tokens, "data_ptr") else tokens
