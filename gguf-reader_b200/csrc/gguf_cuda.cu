@@ -4,6 +4,7 @@
 // tensors and the LlamaModel forward / Engine greedy loop.  Kernels live in the
 // included .cuh files.  Built with -fmad=false so that the dequantisers' f32
 // arithmetic is never contracted into FMAs (bit-exact with the reference).
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdarg>
@@ -27,6 +28,8 @@
 #include "attention.cuh"
 #include "noalloc.cuh"
 #include "prefill.cuh"
+#include "sample.cuh"
+#include "ops.cuh"
 
 using namespace ggc;
 
@@ -121,9 +124,10 @@ struct ggc_ctx {
     uint64_t launches = 0;
     // owner + one per live model / tensor: the context outlives everything made on it
     std::atomic<int> refs{1};
-    // staging buffers for host arguments (0-2), matmul operands (3-4) and split-K partials (5)
-    void* stage[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
-    size_t stage_cap[6] = {0, 0, 0, 0, 0, 0};
+    // staging buffers for host arguments (0-2), matmul operands (3-4), split-K
+    // partials (5), sampling scratch (6) and the sampler's seen ids + result (7)
+    void* stage[8] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+    size_t stage_cap[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     int* errf = nullptr;   // device error flags of the context's own launches
 };
 
@@ -294,7 +298,7 @@ void ctx_release(ggc_ctx* ctx) {
     {
         DeviceGuard g(ctx->device);
         cudaStreamSynchronize(ctx->stream);
-        for (int i = 0; i < 6; ++i)
+        for (int i = 0; i < 8; ++i)
             if (ctx->stage[i]) cudaFree(ctx->stage[i]);
         if (ctx->errf) cudaFree(ctx->errf);
         if (ctx->comm) nccl().CommDestroy(ctx->comm);
@@ -881,6 +885,167 @@ extern "C" int ggc_tensor_matmul(ggc_ctx* ctx, const ggc_tensor* t, const float*
         return set_error(GGC_ERR_TIMEOUT, "a bounded device wait expired");
     }
     return GGC_OK;
+}
+
+// ===========================================================================
+// ops.rs standalone functions (ops.cuh)
+// ===========================================================================
+namespace {
+
+// a caller's in/out vector: device pointers pass through, host data is staged
+// in buffer `i` and copied back by done()
+struct InOut {
+    ggc_ctx* ctx;
+    void* user;
+    void* dev = nullptr;
+    size_t bytes = 0;
+    bool staged = false;
+    int open(ggc_ctx* c, int i, void* p, size_t n) {
+        ctx = c;
+        user = p;
+        bytes = n;
+        staged = !is_device_ptr(p);
+        if (!staged || n == 0) { dev = p; return GGC_OK; }
+        GGC_TRY(ensure_stage(c, i, n));
+        dev = c->stage[i];
+        GGC_CUDA_TRY(cudaMemcpyAsync(dev, p, n, cudaMemcpyHostToDevice, c->stream));
+        return GGC_OK;
+    }
+    int done() {
+        if (staged && bytes) GGC_CUDA_TRY(cudaMemcpyAsync(user, dev, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+        GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+        return GGC_OK;
+    }
+};
+
+// the three matvec layouts share one kernel and the reference's checks
+int ops_matvec(ggc_ctx* ctx, const float* a, uint64_t a_len, uint64_t rows, uint64_t cols, uint64_t rs, uint64_t cs,
+               const float* x, uint64_t x_len, float* y, uint64_t y_len, const float* b) {
+    if (!ctx || (!a && a_len) || (!x && x_len) || (!y && y_len)) return set_error(GGC_ERR_INVALID_ARG, "null argument");
+    if (a_len < rows * cols) return set_dequant_error(GGC_F32, rows * cols, a_len, "matvec a");
+    if (x_len != cols) return set_dequant_error(GGC_F32, cols, x_len, "matvec x");
+    if (y_len != rows) return set_dequant_error(GGC_F32, rows, y_len, "matvec y");
+    if (rows == 0) return GGC_OK;
+    DeviceGuard g(ctx->device);
+    const void *da, *dx, *db = nullptr;
+    GGC_TRY(dev_in(ctx, 0, a, rows * cols * sizeof(float), &da));
+    GGC_TRY(dev_in(ctx, 1, x, cols * sizeof(float), &dx));
+    if (b) GGC_TRY(dev_in(ctx, 3, b, rows * sizeof(float), &db));
+    InOut yo;
+    GGC_TRY(yo.open(ctx, 2, y, rows * sizeof(float)));
+    GGC_CUDA_TRY(launch(ctx, k_ops_matvec, dim3((unsigned)cdiv<uint64_t>(rows, 128)), dim3(128), 0, (const float*)da, rows,
+                        cols, rs, cs, (const float*)dx, (const float*)db, (float*)yo.dev));
+    return yo.done();
+}
+
+}  // namespace
+
+// ops::matvec (ops.rs:14-72): y = A x (+ b), A row-major rows x cols
+extern "C" int ggc_ops_matvec(ggc_ctx* ctx, const float* a, uint64_t a_len, uint64_t rows, uint64_t cols,
+                              const float* x, uint64_t x_len, float* y, uint64_t y_len, const float* b) {
+    return ops_matvec(ctx, a, a_len, rows, cols, cols, 1, x, x_len, y, y_len, b);
+}
+// ops::matvec_colmajor (ops.rs:121-170): y[i] = sum_j a[j * rows + i] x[j] (+ b)
+extern "C" int ggc_ops_matvec_colmajor(ggc_ctx* ctx, const float* a, uint64_t a_len, uint64_t rows, uint64_t cols,
+                                       const float* x, uint64_t x_len, float* y, uint64_t y_len, const float* b) {
+    return ops_matvec(ctx, a, a_len, rows, cols, 1, rows, x, x_len, y, y_len, b);
+}
+// ops::matvec_colmajor_trans (ops.rs:172-227): y[i] = sum_j a[i * dim0 + j] x[j] (+ b), i < dim1
+extern "C" int ggc_ops_matvec_colmajor_trans(ggc_ctx* ctx, const float* a, uint64_t a_len, uint64_t dim0, uint64_t dim1,
+                                             const float* x, uint64_t x_len, float* y, uint64_t y_len, const float* b) {
+    if (a_len < dim0 * dim1) return set_dequant_error(GGC_F32, dim0 * dim1, a_len, "matvec a");
+    return ops_matvec(ctx, a, a_len, dim1, dim0, dim0, 1, x, x_len, y, y_len, b);
+}
+// ops::matmul (ops.rs:74-113): C = A B, row-major
+extern "C" int ggc_ops_matmul(ggc_ctx* ctx, const float* a, uint64_t a_len, uint64_t ra, uint64_t ca, const float* b,
+                              uint64_t b_len, uint64_t cb, float* c, uint64_t c_len) {
+    if (!ctx || (!a && a_len) || (!b && b_len) || (!c && c_len)) return set_error(GGC_ERR_INVALID_ARG, "null argument");
+    if (a_len < ra * ca) return set_dequant_error(GGC_F32, ra * ca, a_len, "matmul a");
+    if (b_len < ca * cb) return set_dequant_error(GGC_F32, ca * cb, b_len, "matmul b");
+    if (c_len < ra * cb) return set_dequant_error(GGC_F32, ra * cb, c_len, "matmul c");
+    if (ra == 0 || cb == 0) return GGC_OK;
+    if (ra > 65535) return set_error(GGC_ERR_INVALID_ARG, "matmul: at most 65535 rows");
+    DeviceGuard g(ctx->device);
+    const void *da, *db;
+    GGC_TRY(dev_in(ctx, 0, a, ra * ca * sizeof(float), &da));
+    GGC_TRY(dev_in(ctx, 1, b, ca * cb * sizeof(float), &db));
+    InOut co;
+    GGC_TRY(co.open(ctx, 2, c, ra * cb * sizeof(float)));
+    GGC_CUDA_TRY(launch(ctx, k_ops_matmul, dim3((unsigned)cdiv<uint64_t>(cb, 256), (unsigned)ra), dim3(256), 0,
+                        (const float*)da, (const float*)db, ra, ca, cb, (float*)co.dev));
+    return co.done();
+}
+
+namespace {
+int ops_act(ggc_ctx* ctx, float* x, uint64_t n, int gelu) {
+    if (!ctx || (!x && n)) return set_error(GGC_ERR_INVALID_ARG, "null argument");
+    if (n == 0) return GGC_OK;
+    DeviceGuard g(ctx->device);
+    InOut xo;
+    GGC_TRY(xo.open(ctx, 0, x, n * sizeof(float)));
+    const unsigned grid = (unsigned)std::min<uint64_t>(cdiv<uint64_t>(n, 256), (uint64_t)ctx->num_sms * 8);
+    GGC_CUDA_TRY(launch(ctx, k_ops_act, dim3(grid), dim3(256), 0, (float*)xo.dev, n, gelu));
+    return xo.done();
+}
+int ops_norm(ggc_ctx* ctx, float* x, uint64_t n, const float* w, const float* b, float eps, int layer) {
+    DeviceGuard g(ctx->device);
+    InOut xo;
+    GGC_TRY(xo.open(ctx, 0, x, n * sizeof(float)));
+    const void *dw, *db = nullptr;
+    GGC_TRY(dev_in(ctx, 1, w, n * sizeof(float), &dw));
+    if (layer) GGC_TRY(dev_in(ctx, 3, b, n * sizeof(float), &db));
+    GGC_CUDA_TRY(launch(ctx, k_ops_norm, dim3(1), dim3(256), 0, (float*)xo.dev, n, (const float*)dw, (const float*)db,
+                        eps, layer));
+    return xo.done();
+}
+}  // namespace
+
+// ops::silu / ops::gelu (ops.rs:237-256), in place
+extern "C" int ggc_ops_silu(ggc_ctx* ctx, float* x, uint64_t n) { return ops_act(ctx, x, n, 0); }
+extern "C" int ggc_ops_gelu(ggc_ctx* ctx, float* x, uint64_t n) { return ops_act(ctx, x, n, 1); }
+
+// ops::rmsnorm (ops.rs:262-274), in place; a length mismatch leaves x as is (as the reference)
+extern "C" int ggc_ops_rmsnorm(ggc_ctx* ctx, float* x, uint64_t n, const float* w, uint64_t w_len, float eps) {
+    if (!ctx || (!x && n) || (!w && w_len)) return set_error(GGC_ERR_INVALID_ARG, "null argument");
+    if (n != w_len || n == 0) return GGC_OK;
+    return ops_norm(ctx, x, n, w, nullptr, eps, 0);
+}
+// ops::layernorm (ops.rs:279-291), in place; empty or mismatched lengths leave x as is
+extern "C" int ggc_ops_layernorm(ggc_ctx* ctx, float* x, uint64_t n, const float* w, uint64_t w_len, const float* b,
+                                 uint64_t b_len, float eps) {
+    if (!ctx || (!x && n) || (!w && w_len) || (!b && b_len)) return set_error(GGC_ERR_INVALID_ARG, "null argument");
+    if (n == 0 || n != w_len || n != b_len) return GGC_OK;
+    return ops_norm(ctx, x, n, w, b, eps, 1);
+}
+// ops::softmax (ops.rs:295-308), in place
+extern "C" int ggc_ops_softmax(ggc_ctx* ctx, float* x, uint64_t n) {
+    if (!ctx || (!x && n)) return set_error(GGC_ERR_INVALID_ARG, "null argument");
+    if (n == 0) return GGC_OK;
+    DeviceGuard g(ctx->device);
+    InOut xo;
+    GGC_TRY(xo.open(ctx, 0, x, n * sizeof(float)));
+    GGC_CUDA_TRY(launch(ctx, k_ops_softmax, dim3(1), dim3(256), 0, (float*)xo.dev, n));
+    return xo.done();
+}
+// ops::rope (ops.rs:318-337), in place: x holds n_x / head_dim tokens, head_dim = 2 * n_freqs
+extern "C" int ggc_ops_rope(ggc_ctx* ctx, float* x, uint64_t n_x, const int64_t* positions, uint64_t n_pos,
+                            const float* freqs, uint64_t n_freqs) {
+    if (!ctx || (!x && n_x) || (!positions && n_pos) || (!freqs && n_freqs))
+        return set_error(GGC_ERR_INVALID_ARG, "null argument");
+    if (n_x == 0 || n_pos == 0 || n_freqs == 0) return GGC_OK;
+    if (n_freqs > 0xFFFFFFFFull) return set_error(GGC_ERR_INVALID_ARG, "rope: too many frequencies");
+    const uint64_t n_tok = n_x / (2 * n_freqs);
+    if (n_tok == 0) return GGC_OK;
+    DeviceGuard g(ctx->device);
+    InOut xo;
+    GGC_TRY(xo.open(ctx, 0, x, n_x * sizeof(float)));
+    const void *dp, *df;
+    GGC_TRY(dev_in(ctx, 1, positions, n_pos * sizeof(int64_t), &dp));
+    GGC_TRY(dev_in(ctx, 3, freqs, n_freqs * sizeof(float), &df));
+    const unsigned grid = (unsigned)std::min<uint64_t>(cdiv<uint64_t>(n_tok * n_freqs, 256), (uint64_t)ctx->num_sms * 8);
+    GGC_CUDA_TRY(launch(ctx, k_ops_rope, dim3(grid), dim3(256), 0, (float*)xo.dev, n_tok, (const int64_t*)dp, n_pos,
+                        (const float*)df, (uint32_t)n_freqs));
+    return xo.done();
 }
 
 // ===========================================================================
@@ -2028,6 +2193,51 @@ extern "C" int ggc_model_wait(ggc_model* m, uint32_t* out_ids, uint64_t* n_out) 
 }
 
 extern "C" uint64_t ggc_model_cache_len(const ggc_model* m) { return m ? m->cache_len : 0; }
+
+// Sampler::sample (sampler.rs:86-186) on the device (k_sample, sample.cuh)
+extern "C" int ggc_sample(ggc_ctx* ctx, const float* logits, uint64_t vocab, const ggc_sampler_config* cfg,
+                          const uint32_t* seen, uint64_t n_seen, float u, uint32_t* out_id) {
+    if (!ctx || !logits || !cfg || !out_id || (n_seen && !seen)) return set_error(GGC_ERR_INVALID_ARG, "null argument");
+    if (vocab == 0) return set_error(GGC_ERR_INFERENCE, "logits empty");
+    if (vocab > 0xFFFFFFFFull) return set_error(GGC_ERR_INVALID_ARG, "vocabulary too large");
+    if (!(u >= 0.0f && u < 1.0f)) return set_error(GGC_ERR_INVALID_ARG, "u must lie in [0, 1)");
+    if (cfg->temperature > 1e-6f) {
+        const bool use_k = cfg->top_k > 0 && cfg->top_k < vocab;
+        if ((use_k ? (uint64_t)cfg->top_k : vocab) > (uint64_t)SAMPLE_MAX_K)
+            return set_error(GGC_ERR_INVALID_ARG, "device sampling keeps at most %d candidates: set top_k in [1, %d]",
+                             SAMPLE_MAX_K, SAMPLE_MAX_K);
+    }
+    DeviceGuard g(ctx->device);
+    std::vector<uint32_t> ids(seen, seen + n_seen);   // the reference's seen map: distinct keys
+    std::sort(ids.begin(), ids.end());
+    ids.erase(std::unique(ids.begin(), ids.end()), ids.end());
+    const void* dl;
+    GGC_TRY(dev_in(ctx, 0, logits, vocab * sizeof(float), &dl));
+    GGC_TRY(ensure_stage(ctx, 6, vocab * sizeof(float)));
+    GGC_TRY(ensure_stage(ctx, 7, (ids.size() + 2) * sizeof(uint32_t)));
+    uint32_t* io = (uint32_t*)ctx->stage[7];   // [0] id, [1] error flag, [2..] seen ids
+    GGC_CUDA_TRY(cudaMemsetAsync(io, 0, 2 * sizeof(uint32_t), ctx->stream));
+    if (!ids.empty())
+        GGC_CUDA_TRY(cudaMemcpyAsync(io + 2, ids.data(), ids.size() * sizeof(uint32_t), cudaMemcpyHostToDevice,
+                                     ctx->stream));
+    const SampleCfg c{cfg->temperature, cfg->top_k, cfg->top_p, cfg->min_p, cfg->repeat_penalty};
+    GGC_CUDA_TRY(launch(ctx, k_sample, dim3(1), dim3(SAMPLE_THREADS), 0, (const float*)dl, (uint32_t)vocab,
+                        (const uint32_t*)(io + 2), (uint32_t)ids.size(), c, u, (float*)ctx->stage[6], io,
+                        (int*)(io + 1)));
+    uint32_t res[2] = {0, 0};
+    GGC_CUDA_TRY(cudaMemcpyAsync(res, io, sizeof(res), cudaMemcpyDeviceToHost, ctx->stream));
+    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    if (res[1]) return set_error(GGC_ERR_INFERENCE, "NaN in logits");
+    *out_id = res[0];
+    return GGC_OK;
+}
+
+// the same over the logits of the model's last forward / decode step (device)
+extern "C" int ggc_model_sample(ggc_model* m, const ggc_sampler_config* cfg, const uint32_t* seen, uint64_t n_seen,
+                                float u, uint32_t* out_id) {
+    if (!m) return set_error(GGC_ERR_INVALID_ARG, "null model");
+    return ggc_sample(m->ctx, m->logits, m->hp.vocab_size, cfg, seen, n_seen, u, out_id);
+}
 
 extern "C" int ggc_model_allreduce_kind(const ggc_model* m) {
     if (!m || m->ctx->world < 2) return 0;

@@ -44,6 +44,11 @@ class TpShard(C.Structure):
                 ("ffn0", C.c_uint64), ("ffn_len", C.c_uint64)]
 
 
+class SamplerConfig(C.Structure):
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_uint32), ("top_p", C.c_float), ("min_p", C.c_float),
+                ("repeat_penalty", C.c_float)]
+
+
 class TensorDesc(C.Structure):
     _fields_ = [("data", C.c_void_p), ("nbytes", C.c_uint64), ("dtype", C.c_int), ("n_elements", C.c_uint64)]
 
@@ -145,6 +150,18 @@ SIGNATURES = {
     "ggc_model_forward": (_i32, [_vp, _vp, _vp, _u64, _vp, _vp]),
     "ggc_model_cache_len": (_u64, [_vp]),
     "ggc_model_allreduce_kind": (_i32, [_vp]),
+    "ggc_model_sample": (_i32, [_vp, C.POINTER(SamplerConfig), _vp, _u64, C.c_float, C.POINTER(_u32)]),
+    "ggc_ops_matvec": (_i32, [_vp, _vp, _u64, _u64, _u64, _vp, _u64, _vp, _u64, _vp]),
+    "ggc_ops_matvec_colmajor": (_i32, [_vp, _vp, _u64, _u64, _u64, _vp, _u64, _vp, _u64, _vp]),
+    "ggc_ops_matvec_colmajor_trans": (_i32, [_vp, _vp, _u64, _u64, _u64, _vp, _u64, _vp, _u64, _vp]),
+    "ggc_ops_matmul": (_i32, [_vp, _vp, _u64, _u64, _u64, _vp, _u64, _u64, _vp, _u64]),
+    "ggc_ops_silu": (_i32, [_vp, _vp, _u64]),
+    "ggc_ops_gelu": (_i32, [_vp, _vp, _u64]),
+    "ggc_ops_rmsnorm": (_i32, [_vp, _vp, _u64, _vp, _u64, C.c_float]),
+    "ggc_ops_layernorm": (_i32, [_vp, _vp, _u64, _vp, _u64, _vp, _u64, C.c_float]),
+    "ggc_ops_softmax": (_i32, [_vp, _vp, _u64]),
+    "ggc_ops_rope": (_i32, [_vp, _vp, _u64, _vp, _u64, _vp, _u64]),
+    "ggc_sample": (_i32, [_vp, _vp, _u64, C.POINTER(SamplerConfig), _vp, _u64, C.c_float, C.POINTER(_u32)]),
     "ggc_model_reset_cache": (_i32, [_vp]),
     "ggc_model_truncate": (_i32, [_vp, _u64]),
     "ggc_model_cache_append": (_i32, [_vp, _u32, _vp, _vp, _u64]),

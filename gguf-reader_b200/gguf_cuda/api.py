@@ -209,6 +209,30 @@ def tp_plan(hp: dict, attn_output_dtype: int, ffn_down_dtype: int, rank: int, wo
             "ffn": (out.ffn0, out.ffn_len)}
 
 
+# ---- sampler.rs ----------------------------------------------------------------
+def _sampler_args(cfg, seen):
+    cfg = cfg or {}
+    c = L.SamplerConfig(cfg.get("temperature", 1.0), cfg.get("top_k", 40), cfg.get("top_p", 0.95),
+                        cfg.get("min_p", 0.0), cfg.get("repeat_penalty", 1.1))
+    return c, np.ascontiguousarray(list(seen), dtype=np.uint32)
+
+
+def sample(logits, cfg: dict | None = None, seen=(), u: float = 0.5, ctx: Context | None = None) -> int:
+    """Sampler::sample (sampler.rs:86-186) on the device (ggc_sample): `u` is the
+    caller's uniform draw in [0, 1) (the reference's rng.gen_range(0.0..1.0));
+    cfg keys as SamplerConfig, reference defaults temperature 1.0, top_k 40,
+    top_p 0.95, min_p 0.0, repeat_penalty 1.1; seen: ids with a repeat count."""
+    ctx = ctx or default_context()
+    if isinstance(logits, np.ndarray):
+        logits = np.ascontiguousarray(logits, dtype=np.float32)
+    n = logits.size if isinstance(logits, np.ndarray) else logits.numel()
+    c, ids = _sampler_args(cfg, seen)
+    out = C.c_uint32(0)
+    check(lib().ggc_sample(ctx.h, _ptr(logits)[0], n, C.byref(c), ids.ctypes.data if ids.size else None, ids.size,
+                           float(u), C.byref(out)))
+    return int(out.value)
+
+
 # ---- model/llama.rs ------------------------------------------------------------
 class LlamaModel:
     """LlamaModel over tensors given in role order (see synth.TENSOR_ROLES)."""
@@ -264,6 +288,14 @@ class LlamaModel:
 
     def reset_cache(self):
         check(lib().ggc_model_reset_cache(self.h))
+
+    def sample(self, cfg: dict | None = None, seen=(), u: float = 0.5) -> int:
+        """Sampler::sample on the device over the last forward's logits (ggc_model_sample)."""
+        c, ids = _sampler_args(cfg, seen)
+        out = C.c_uint32(0)
+        check(lib().ggc_model_sample(self.h, C.byref(c), ids.ctypes.data if ids.size else None, ids.size, float(u),
+                                     C.byref(out)))
+        return int(out.value)
 
     @property
     def allreduce(self) -> str:

@@ -142,6 +142,28 @@ int ggc_tensor_matmul(ggc_ctx* ctx, const ggc_tensor* t, const float* x, uint64_
  * -1 = None. */
 int ggc_infer_k_quant_dtype(uint64_t span, uint64_t n, int marked);
 
+/* ---- ops.rs standalone functions (API surface; the model fuses its own) ----
+ * Host or device pointers; lengths as the reference's slices; size errors are
+ * DequantError { F32, expected, actual } as in ops.rs.  Products and sums keep
+ * the reference's serial order per output (its bits); silu / gelu / softmax /
+ * rope use CUDA's expf / tanhf / sincosf (within a few ulp of libm). */
+int ggc_ops_matvec(ggc_ctx* ctx, const float* a, uint64_t a_len, uint64_t rows, uint64_t cols, const float* x,
+                   uint64_t x_len, float* y, uint64_t y_len, const float* b);            /* ops.rs:14, b: rows or NULL */
+int ggc_ops_matvec_colmajor(ggc_ctx* ctx, const float* a, uint64_t a_len, uint64_t rows, uint64_t cols,
+                            const float* x, uint64_t x_len, float* y, uint64_t y_len, const float* b);   /* ops.rs:121 */
+int ggc_ops_matvec_colmajor_trans(ggc_ctx* ctx, const float* a, uint64_t a_len, uint64_t dim0, uint64_t dim1,
+                                  const float* x, uint64_t x_len, float* y, uint64_t y_len, const float* b); /* :172 */
+int ggc_ops_matmul(ggc_ctx* ctx, const float* a, uint64_t a_len, uint64_t ra, uint64_t ca, const float* b,
+                   uint64_t b_len, uint64_t cb, float* c, uint64_t c_len);                   /* ops.rs:74 */
+int ggc_ops_silu(ggc_ctx* ctx, float* x, uint64_t n);                                        /* ops.rs:237 */
+int ggc_ops_gelu(ggc_ctx* ctx, float* x, uint64_t n);                                        /* ops.rs:250 */
+int ggc_ops_rmsnorm(ggc_ctx* ctx, float* x, uint64_t n, const float* w, uint64_t w_len, float eps);   /* :262 */
+int ggc_ops_layernorm(ggc_ctx* ctx, float* x, uint64_t n, const float* w, uint64_t w_len, const float* b,
+                      uint64_t b_len, float eps);                                             /* ops.rs:279 */
+int ggc_ops_softmax(ggc_ctx* ctx, float* x, uint64_t n);                                     /* ops.rs:295 */
+int ggc_ops_rope(ggc_ctx* ctx, float* x, uint64_t n_x, const int64_t* positions, uint64_t n_pos, const float* freqs,
+                 uint64_t n_freqs);                                                           /* ops.rs:318 */
+
 /* ---- model/llama.rs ------------------------------------------------------ */
 typedef struct ggc_model ggc_model;
 
@@ -224,6 +246,30 @@ int ggc_model_generate_greedy(ggc_model* m, const uint32_t* prompt, uint64_t n_p
  * array of `steps`, may be NULL). */
 int ggc_model_decode(ggc_model* m, uint64_t steps, int64_t eos, int sync, uint32_t* out_ids, uint64_t* n_out);
 int ggc_model_wait(ggc_model* m, uint32_t* out_ids, uint64_t* n_out);
+
+/* Sampler::sample (src/infer/sampler.rs:86-186) on the device over `vocab`
+ * logits (host or device pointer; ggc_model_sample: the logits of the model's last
+ * forward / decode step, already on the device): repeat penalty on `seen` (host array of
+ * token ids; duplicates count once, as the reference's HashMap keys), temperature
+ * (<= 1e-6: greedy, the last maximum), softmax, top-k, top-p, min-p, and the pick
+ * with `u` in [0, 1) standing for the reference's rng.gen_range(0.0..1.0) draw --
+ * the caller keeps the RNG, so a host holding the reference's StdRng gets its
+ * stream.  Only the token id comes back (no logits copy).  Limit: at most 1024
+ * candidates after top-k (top_k in 1..1024, or a vocabulary of <= 1024), else
+ * InvalidArg.  The softmax sum is a parallel reduction, so a pick can differ from
+ * the reference's only when u*total lands within a few ulp of a cumulative
+ * boundary.  NaN logits: InferenceError (the reference panics). */
+typedef struct ggc_sampler_config {
+    float temperature;
+    uint32_t top_k;          /* 0 = off */
+    float top_p;             /* 1.0 = off */
+    float min_p;             /* 0.0 = off */
+    float repeat_penalty;    /* 1.0 = off */
+} ggc_sampler_config;
+int ggc_sample(ggc_ctx* ctx, const float* logits, uint64_t vocab, const ggc_sampler_config* cfg, const uint32_t* seen,
+               uint64_t n_seen, float u, uint32_t* out_id);
+int ggc_model_sample(ggc_model* m, const ggc_sampler_config* cfg, const uint32_t* seen, uint64_t n_seen, float u,
+                     uint32_t* out_id);
 
 /* How a tensor-parallel model sums its row-parallel partials: 0 = single GPU
  * (none), 1 = NCCL all-reduce, 2 = fused into the GEMVs over peer memory. */

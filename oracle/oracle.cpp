@@ -17,6 +17,7 @@
 // reduced serially, so results do not depend on the thread count.
 #include "oracle.h"
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <cstdio>
@@ -456,6 +457,20 @@ int orc_matmul(const float* a, uint64_t a_len, uint64_t ra, uint64_t ca, const f
 }
 
 // ops.rs:172-227
+// ops.rs:121-170: y[i] = sum_j a[j * rows + i] x[j] (+ b[i])
+int orc_matvec_colmajor(const float* a, uint64_t a_len, uint64_t rows, uint64_t cols, const float* x, uint64_t x_len,
+                        float* y, uint64_t y_len, const float* b) {
+    if (a_len < rows * cols) return set_err(ORC_ERR_DEQUANT, rows * cols, a_len, "F32");
+    if (x_len != cols) return set_err(ORC_ERR_DEQUANT, cols, x_len, "F32");
+    if (y_len != rows) return set_err(ORC_ERR_DEQUANT, rows, y_len, "F32");
+    for (uint64_t i = 0; i < rows; ++i) {
+        float acc = 0.0f;
+        for (uint64_t j = 0; j < cols; ++j) acc += a[j * rows + i] * x[j];
+        y[i] = acc + (b ? b[i] : 0.0f);
+    }
+    return ORC_OK;
+}
+
 int orc_matvec_colmajor_trans(const float* a, uint64_t a_len, uint64_t dim0, uint64_t dim1,
                               const float* x, uint64_t x_len, float* y, uint64_t y_len,
                               const float* b) {
@@ -587,6 +602,75 @@ uint32_t orc_greedy(const float* logits, uint64_t n) {
     for (uint64_t i = 1; i < n; ++i)
         if (!(logits[i] < logits[best])) best = i;
     return (uint32_t)best;
+}
+
+// sampler.rs:86-186, step by step in the reference's f32 order
+int orc_sample(const float* logits, uint64_t vocab, const orc_sampler_cfg* cfg, const uint32_t* seen, uint64_t n_seen,
+               float u, uint32_t* out) {
+    if (vocab == 0) return set_err(ORC_ERR_INFERENCE, 0, 0, "logits empty");
+    std::vector<float> v(logits, logits + vocab);
+    for (uint64_t i = 0; i < vocab; ++i)
+        if (std::isnan(v[i])) return set_err(ORC_ERR_INFERENCE, 0, 0, "NaN logit");
+    // step 1: repeat penalty (sampler.rs:95-110)
+    if (cfg->repeat_penalty != 1.0f)
+        for (uint64_t k = 0; k < n_seen; ++k) {
+            const uint64_t idx = seen[k];
+            if (idx < vocab) v[idx] = v[idx] > 0.0f ? v[idx] / cfg->repeat_penalty : v[idx] * cfg->repeat_penalty;
+        }
+    // step 2: temperature, or greedy (:112-124; max_by keeps the last maximum)
+    const float temp = cfg->temperature;
+    if (!(temp > 1e-6f)) { *out = orc_greedy(v.data(), vocab); return ORC_OK; }
+    for (auto& x : v) x = x / temp;
+    // step 3: softmax (:127-130)
+    float max_v = -std::numeric_limits<float>::max();
+    for (float x : v) max_v = std::fmax(max_v, x);
+    std::vector<float> pr(vocab);
+    float sum = 0.0f;
+    for (uint64_t i = 0; i < vocab; ++i) { pr[i] = expf(v[i] - max_v); sum += pr[i]; }
+    for (auto& p : pr) p = p / sum;
+    // step 4: top-k (:133-139), stable sort by probability, descending
+    std::vector<std::pair<uint32_t, float>> c(vocab);
+    for (uint64_t i = 0; i < vocab; ++i) c[i] = {(uint32_t)i, pr[i]};
+    auto desc = [](const std::pair<uint32_t, float>& a, const std::pair<uint32_t, float>& b) { return a.second > b.second; };
+    if (cfg->top_k > 0 && cfg->top_k < c.size()) {
+        std::stable_sort(c.begin(), c.end(), desc);
+        c.resize(cfg->top_k);
+    }
+    // step 5: top-p (:142-156)
+    if (cfg->top_p < 1.0f) {
+        std::stable_sort(c.begin(), c.end(), desc);
+        float total = 0.0f;
+        for (auto& e : c) total += e.second;
+        const float threshold = total * cfg->top_p;
+        float cum = 0.0f;
+        size_t cut = c.size();
+        for (size_t i = 0; i < c.size(); ++i) {
+            cum += c[i].second;
+            if (cum >= threshold) { cut = i + 1; break; }
+        }
+        c.resize(cut);
+    }
+    // step 6: min-p (:159-163)
+    if (cfg->min_p > 0.0f) {
+        float mp = 0.0f;
+        for (auto& e : c) mp = std::fmax(mp, e.second);
+        const float thr = mp * cfg->min_p;
+        std::vector<std::pair<uint32_t, float>> kept;
+        for (auto& e : c)
+            if (e.second >= thr) kept.push_back(e);
+        c.swap(kept);
+    }
+    // step 7: renormalise and pick (:166-184)
+    if (c.empty()) { *out = orc_greedy(v.data(), vocab); return ORC_OK; }
+    float total = 0.0f;
+    for (auto& e : c) total += e.second;
+    float r = u * total;
+    for (auto& e : c) {
+        r -= e.second;
+        if (r <= 0.0f) { *out = e.first; return ORC_OK; }
+    }
+    *out = c.back().first;
+    return ORC_OK;
 }
 
 }  // extern "C"

@@ -61,6 +61,8 @@ int orc_matvec(const float* a, uint64_t a_len, uint64_t rows, uint64_t cols, con
                uint64_t x_len, float* y, uint64_t y_len, const float* b);
 int orc_matmul(const float* a, uint64_t a_len, uint64_t rows_a, uint64_t cols_a, const float* b,
                uint64_t b_len, uint64_t cols_b, float* c, uint64_t c_len);
+int orc_matvec_colmajor(const float* a, uint64_t a_len, uint64_t rows, uint64_t cols, const float* x, uint64_t x_len,
+                        float* y, uint64_t y_len, const float* b);
 int orc_matvec_colmajor_trans(const float* a, uint64_t a_len, uint64_t dim0, uint64_t dim1,
                               const float* x, uint64_t x_len, float* y, uint64_t y_len,
                               const float* b);
@@ -112,6 +114,18 @@ int orc_model_cache_read(const orc_model* m, uint32_t layer, float* k, float* v)
 int orc_generate_greedy(orc_model* m, const uint32_t* prompt, uint64_t n_prompt, int64_t start_pos,
                         uint64_t max_tokens, int64_t eos, uint32_t* out_ids, uint64_t* n_out);
 uint32_t orc_greedy(const float* logits, uint64_t n);
+/* Sampler::sample (sampler.rs:86-186) with `u` standing for the one
+ * rng.gen_range(0.0..1.0) draw it makes; seen: the distinct token ids with a
+ * positive repeat count.  Returns ORC status (NaN logits: the reference panics). */
+typedef struct {
+    float temperature;
+    uint32_t top_k;
+    float top_p;
+    float min_p;
+    float repeat_penalty;
+} orc_sampler_cfg;
+int orc_sample(const float* logits, uint64_t vocab, const orc_sampler_cfg* cfg, const uint32_t* seen, uint64_t n_seen,
+               float u, uint32_t* out);
 
 #ifdef __cplusplus
 }

@@ -79,6 +79,7 @@ def lib():
         L.orc_matvec.argtypes = [vp, u64, u64, u64, vp, u64, vp, u64, vp]
         L.orc_matmul.argtypes = [vp, u64, u64, u64, vp, u64, u64, vp, u64]
         L.orc_matvec_colmajor_trans.argtypes = [vp, u64, u64, u64, vp, u64, vp, u64, vp]
+        L.orc_matvec_colmajor.argtypes = [vp, u64, u64, u64, vp, u64, vp, u64, vp]
         L.orc_silu.argtypes = [vp, u64]
         L.orc_gelu.argtypes = [vp, u64]
         L.orc_rmsnorm.argtypes = [vp, u64, vp, u64, C.c_float]
@@ -100,6 +101,7 @@ def lib():
         L.orc_generate_greedy.argtypes = [vp, vp, u64, i64, u64, i64, vp, C.POINTER(u64)]
         L.orc_greedy.restype = C.c_uint32
         L.orc_greedy.argtypes = [vp, u64]
+        L.orc_sample.argtypes = [vp, u64, C.POINTER(SamplerCfg), vp, u64, C.c_float, C.POINTER(C.c_uint32)]
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_last_error.argtypes = [C.POINTER(_Err)]
         _lib = L
@@ -172,6 +174,16 @@ def matvec_colmajor_trans(a, dim0, dim1, x, b=None):
     y = np.zeros(dim1, dtype=np.float32)
     bb = None if b is None else np.ascontiguousarray(b, dtype=np.float32)
     _check(lib().orc_matvec_colmajor_trans(_ptr(a), a.size, dim0, dim1, _ptr(x), x.size, _ptr(y), y.size, _ptr(bb)))
+    return y
+
+
+def matvec_colmajor(a, rows, cols, x, b=None):
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.zeros(rows, dtype=np.float32)
+    bb = None if b is None else np.ascontiguousarray(b, dtype=np.float32)
+    _check(lib().orc_matvec_colmajor(_ptr(a), a.size, rows, cols, _ptr(x), x.size, _ptr(y), y.size,
+                                     None if bb is None else _ptr(bb)))
     return y
 
 
@@ -248,6 +260,23 @@ def rope_freqs(dim, base, max_seq_len):
 def infer_k_quant_dtype(span, n, marked):
     v = lib().orc_infer_k_quant_dtype(span, n, marked)
     return None if v < 0 else v
+
+
+class SamplerCfg(C.Structure):
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_uint32), ("top_p", C.c_float), ("min_p", C.c_float),
+                ("repeat_penalty", C.c_float)]
+
+
+def sample(logits, cfg: dict, seen=(), u: float = 0.5) -> int:
+    """Sampler::sample (sampler.rs:86-186) with `u` as its uniform draw."""
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    sd = np.ascontiguousarray(sorted(set(int(s) for s in seen)), dtype=np.uint32)
+    c = SamplerCfg(cfg.get("temperature", 1.0), cfg.get("top_k", 40), cfg.get("top_p", 0.95), cfg.get("min_p", 0.0),
+                   cfg.get("repeat_penalty", 1.1))
+    out = C.c_uint32(0)
+    _check(lib().orc_sample(_ptr(lg), lg.size, C.byref(c), _ptr(sd) if sd.size else None, sd.size, float(u),
+                            C.byref(out)))
+    return int(out.value)
 
 
 def greedy(logits) -> int:

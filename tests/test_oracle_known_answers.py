@@ -393,3 +393,23 @@ def test_infer_k_quant_dtype(orc):
     assert orc.infer_k_quant_dtype(n // 256 * 210, n, orc.Q5_1) is None
     assert orc.infer_k_quant_dtype(123, n, orc.F32) is None
     assert orc.infer_k_quant_dtype(n // 32 * 20, n, orc.Q4_1) is None   # 160 B / 256 not in the table
+
+
+# ---- sampler.rs:86-186 restatement (orc_sample), checked on CPU --------------
+def test_oracle_sampler_basics(orc):
+    import numpy as np
+    lg = np.array([1.0, 3.0, 2.0, 3.0, -1.0], np.float32)
+    assert orc.sample(lg, dict(temperature=0.0, repeat_penalty=1.0)) == 3          # greedy: the last maximum
+    assert orc.sample(lg, dict(temperature=1.0, top_k=1, repeat_penalty=1.0), u=0.99) == 1   # stable sort: index 1 first
+    # the penalty divides a positive logit: 3 / 2 < 2, so index 2 leads
+    assert orc.sample(lg, dict(temperature=0.0, repeat_penalty=2.0), seen=[1, 3]) == 2
+    # u walks the sorted candidates: small u -> the most probable, u near 1 -> the last kept
+    cfg = dict(temperature=1.0, top_k=3, top_p=1.0, repeat_penalty=1.0)
+    assert orc.sample(lg, cfg, u=0.0) == 1 and orc.sample(lg, cfg, u=0.999) == 2
+    ids = [orc.sample(lg, cfg, u=u) for u in np.linspace(0, 0.999, 200)]
+    assert ids == sorted(ids, key=[1, 3, 2].index)                                 # monotone in u
+    # top-p 0.5 keeps the top two (equal mass 0.42 each): never index 2
+    assert all(orc.sample(lg, dict(top_k=0, top_p=0.5, repeat_penalty=1.0), u=u) in (1, 3) for u in np.linspace(0, 0.99, 50))
+    # min-p 0.9 keeps only probabilities within 90 % of the top: indices 1 and 3
+    assert all(orc.sample(lg, dict(top_k=0, top_p=1.0, min_p=0.9, repeat_penalty=1.0), u=u) in (1, 3)
+               for u in np.linspace(0, 0.99, 50))
