@@ -6,6 +6,6 @@ from ._lib import (ALL_DTYPES, BF16, BLOCK, DTYPE_NAMES, F16, F32, Q2_K, Q3_K_L,
                    UnsupportedArchitecture, lib)
 from .api import (Context, LlamaModel, Tensor, block_bytes, block_size, default_context, dequantize,
                   infer_k_quant_dtype, quant_matvec, sample, tp_plan)
-from . import loader, ops
+from . import engine, loader, ops
 
 __all__ = [n for n in dir() if not n.startswith("_")]
