@@ -784,41 +784,94 @@ extern "C" int ggc_tensor_dequantize(ggc_ctx* ctx, const ggc_tensor* t, float* o
 
 namespace {
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link)
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return (EncodeTiledFn)p;
+    }();
+    return fn;
+}
+
+// The raw rows of a block matrix as a 2-D byte tensor (x = byte in the row,
+// y = row) with a box of one block x `box_rows` rows; false when the layout does
+// not allow it (base or row pitch not 16-byte aligned, no driver entry point).
+bool raw_row_map(CUtensorMap* map, const uint8_t* w, uint32_t rows, uint64_t row_bytes, uint32_t block_bytes,
+                 uint32_t box_rows) {
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc || ((uintptr_t)w & 15) || (row_bytes & 15) || (block_bytes & 15) || block_bytes > 256 || box_rows > 256)
+        return false;
+    const cuuint64_t dims[2] = {row_bytes, rows}, strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {block_bytes, box_rows}, estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)w, dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // 128 weight rows x 512 tokens per CTA; K split over enough CTAs to fill the
-// SMs (partials summed in split order by k_mm_reduce)
+// SMs (partials summed in split order by k_mm_reduce).  Q4_K / Q5_K stage their
+// raw blocks by TMA (split ranges of whole 256-element blocks) when the tensor
+// map can be made, else they read the blocks from global memory as the rest do.
 template <int DT>
 struct RunMM {
-    static void run(ggc_ctx* ctx, const uint8_t* w, uint32_t n, uint32_t k, const uint8_t* xh, const uint8_t* xl,
-                    uint32_t m, uint32_t kpad, float* y, uint32_t ldy, const float* resid, int* errf,
-                    cudaError_t* err) {
+    template <bool STAGE>
+    static cudaError_t set_attr() {
         static std::once_flag once;
         static cudaError_t attr = cudaSuccess;
         std::call_once(once, [] {
-            attr = cudaFuncSetAttribute(k_mm_tc<DT, MM_BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)mm_smem(MM_BN));
+            attr = cudaFuncSetAttribute(k_mm_tc<DT, MM_BN, STAGE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)mm_smem(MM_BN, STAGE, block_bytes_of(DT)));
         });
-        if (attr != cudaSuccess) { *err = attr; return; }
+        return attr;
+    }
+    template <bool STAGE>
+    static void go(ggc_ctx* ctx, const uint8_t* w, uint32_t n, uint32_t k, const uint8_t* xh, const uint8_t* xl,
+                   uint32_t m, uint32_t kpad, float* y, uint32_t ldy, const float* resid, int* errf,
+                   const CUtensorMap& map, cudaError_t* err) {
+        *err = set_attr<STAGE>();
+        if (*err != cudaSuccess) return;
+        const uint32_t smem = mm_smem(MM_BN, STAGE, block_bytes_of(DT));
         const uint32_t gx = cdiv<uint32_t>(n, MM_BN), gy = cdiv<uint32_t>(cdiv<uint32_t>(m, MM_BM), MM_MB);
-        const uint32_t nk = kpad / MM_BK;
+        const uint32_t nk = kpad / MM_BK, step = STAGE ? (uint32_t)(block_size_of(DT) / MM_BK) : 1u;
         uint32_t ks = cdiv<uint32_t>((uint32_t)ctx->num_sms, gx * gy);
-        ks = ks < 1 ? 1 : (ks > nk ? nk : ks);
-        const uint32_t kb_per = cdiv<uint32_t>(nk, ks);
+        ks = ks < 1 ? 1 : (ks > nk / step ? nk / step : ks);
+        const uint32_t kb_per = cdiv<uint32_t>(cdiv<uint32_t>(nk, ks), step) * step;   // whole staged blocks
         ks = cdiv<uint32_t>(nk, kb_per);   // no empty split
         if (ks == 1) {
-            *err = launch(ctx, k_mm_tc<DT, MM_BN>, dim3(gx, gy, 1), dim3(MM_THREADS), mm_smem(MM_BN), w, n, k, xh, xl,
-                          m, kpad, kb_per, y, ldy, resid, errf);
+            *err = launch(ctx, k_mm_tc<DT, MM_BN, STAGE>, dim3(gx, gy, 1), dim3(MM_THREADS), smem, w, n, k, xh, xl,
+                          m, kpad, kb_per, y, ldy, resid, errf, map);
             return;
         }
         const size_t pbytes = (size_t)ks * m * n * sizeof(float);
         int st = ensure_stage(ctx, 5, pbytes);
         if (st != GGC_OK) { *err = cudaErrorMemoryAllocation; return; }
         float* part = (float*)ctx->stage[5];
-        *err = launch(ctx, k_mm_tc<DT, MM_BN>, dim3(gx, gy, ks), dim3(MM_THREADS), mm_smem(MM_BN), w, n, k, xh, xl, m,
-                      kpad, kb_per, part, n, (const float*)nullptr, errf);
+        *err = launch(ctx, k_mm_tc<DT, MM_BN, STAGE>, dim3(gx, gy, ks), dim3(MM_THREADS), smem, w, n, k, xh, xl, m,
+                      kpad, kb_per, part, n, (const float*)nullptr, errf, map);
         if (*err != cudaSuccess) return;
         const uint64_t total = (uint64_t)m * n;
         const unsigned grid = (unsigned)std::min<uint64_t>(cdiv<uint64_t>(total, 256), (uint64_t)ctx->num_sms * 8);
         *err = launch(ctx, k_mm_reduce, dim3(grid), dim3(256), 0, (const float*)part, ks, m, n, y, ldy, resid);
+    }
+    static void run(ggc_ctx* ctx, const uint8_t* w, uint32_t n, uint32_t k, const uint8_t* xh, const uint8_t* xl,
+                    uint32_t m, uint32_t kpad, float* y, uint32_t ldy, const float* resid, int* errf,
+                    cudaError_t* err) {
+        CUtensorMap map;
+        std::memset(&map, 0, sizeof(map));
+        if constexpr (mm_staged(DT)) {
+            const uint64_t row_bytes = (uint64_t)(k / block_size_of(DT)) * block_bytes_of(DT);
+            if (k % block_size_of(DT) == 0 && kpad == k &&
+                raw_row_map(&map, w, n, row_bytes, (uint32_t)block_bytes_of(DT), MM_BN))
+                return go<true>(ctx, w, n, k, xh, xl, m, kpad, y, ldy, resid, errf, map, err);
+        }
+        go<false>(ctx, w, n, k, xh, xl, m, kpad, y, ldy, resid, errf, map, err);
     }
 };
 

@@ -19,6 +19,7 @@
 //   * Epilogue: tcgen05.ld of the TMEM rows (tokens), Y (+ residual) stores.
 //     TMEM is freed on every path; every wait is bounded.
 #pragma once
+#include <cuda.h>   // CUtensorMap (the tensor-map type only)
 #include <cuda_bf16.h>
 #include "common.cuh"
 #include "dequant.cuh"
@@ -37,7 +38,15 @@ constexpr uint32_t MM_TOKENS = MM_BM * MM_MB;
 constexpr uint32_t MM_X_BYTES = MM_BM * MM_BK * 2;          // one bf16 X tile (hi or lo), 16 KB
 constexpr int MM_BN = 128;                 // weight rows per CTA (UMMA N); TMEM: MM_MB x 128 = all 512 columns
 constexpr uint32_t mm_w_bytes(int bn) { return (uint32_t)bn * MM_BK * 2; }
-constexpr uint32_t mm_smem(int bn) { return 2 * 2 * mm_w_bytes(bn) + MM_XS * 2 * MM_X_BYTES; }   // 192 KB
+// formats whose raw blocks the product stages in shared memory by TMA (256-element
+// blocks of a 16-byte multiple: every block of a raw row starts 16-byte aligned)
+constexpr bool mm_staged(int dt) { return dt == GGC_Q4_K || dt == GGC_Q5_K; }
+constexpr int mm_xs(bool staged) { return staged ? 3 : MM_XS; }   // X ring slots (smem for the raw ring)
+// dynamic shared memory: W ring [2][hi, lo], X ring [XS][hi, lo], staged: raw ring [2][bn rows][bb]
+// at the next 128-byte boundary (the TMA destination alignment)
+constexpr uint32_t mm_smem(int bn, bool staged = false, int bb = 0) {
+    return 2 * 2 * mm_w_bytes(bn) + mm_xs(staged) * 2 * MM_X_BYTES + (staged ? 2u * bn * (uint32_t)bb + 128u : 0u);
+}
 // instruction descriptor: D f32, A/B bf16, both K-major, N = bn, M = 128
 constexpr uint32_t mm_idesc(int bn) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(MM_BM >> 4) << 24);
@@ -231,18 +240,30 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_x_split(const float* __restri
 //   epilogue: the 8 warps read TMEM (warp w: lanes 32 (w % 4).., M-blocks of
 //     half w / 4) and write Y (+ the residual).
 // Every wait is bounded (ERRF_TIMEOUT); no thread leaves early, warp 8 frees TMEM.
-template <int DT, int BN>
+//
+// STAGE (the mm_staged formats Q4_K, Q5_K): the issuer also loads the CTA's raw
+// blocks of each 256-element K range (BN rows x one block, rows past the matrix
+// zero-filled) with one 2-D TMA copy (tensor map over the raw rows as bytes,
+// no multicast) into a 2-slot ring (rfull / rfree), so the dequantising warps
+// read shared memory only; the split-K ranges are whole blocks.
+template <int DT, int BN, bool STAGE>
 __global__ void __launch_bounds__(MM_THREADS, 1)
     k_mm_tc(const uint8_t* __restrict__ w, uint32_t n_rows, uint32_t k_cols, const uint8_t* __restrict__ xh,
             const uint8_t* __restrict__ xl, uint32_t m, uint32_t kpad, uint32_t kb_per, float* y, uint32_t ldy,
-            const float* resid, int* errf) {
+            const float* resid, int* errf, const __grid_constant__ CUtensorMap wmap) {
     constexpr int BS = block_size_of(DT), BB = block_bytes_of(DT);
-    constexpr uint32_t WB = mm_w_bytes(BN), TCOLS = MM_MB * BN, IDESC = mm_idesc(BN);
+    static_assert(!STAGE || (mm_staged(DT) && BS == 4 * MM_BK && BB % 16 == 0 && (BN * BB) % 128 == 0),
+                  "staged: 256-element blocks of a 16-byte multiple");
+    constexpr int XS = mm_xs(STAGE);
+    constexpr uint32_t WB = mm_w_bytes(BN), TCOLS = MM_MB * BN, IDESC = mm_idesc(BN), RB = (uint32_t)BN * BB;
+    constexpr uint32_t KSTEPS_PER_BLOCK = STAGE ? BS / MM_BK : 1;   // K steps per staged raw block (4)
     extern __shared__ __align__(128) uint8_t smem[];   // no-swizzle descriptors need 16-byte alignment
-    __shared__ uint64_t wfull[2], wfree[2], xfull[MM_XS], xfree[MM_XS], done;
+    __shared__ uint64_t wfull[2], wfree[2], xfull[MM_XS], xfree[MM_XS], rfull[2], rfree[2], done;
     __shared__ uint32_t s_tmem;
     uint8_t* wsm = smem;                  // [2 slots][hi, lo][WB]
-    uint8_t* xsm = smem + 4 * WB;         // [MM_XS slots][hi, lo][MM_X_BYTES]
+    uint8_t* xsm = smem + 4 * WB;         // [XS slots][hi, lo][MM_X_BYTES]
+    uint8_t* rsm = xsm + XS * 2 * MM_X_BYTES;   // staged: [2 slots][BN rows][BB] raw blocks
+    rsm += (128u - (smem_addr(rsm) & 127u)) & 127u;   // RB is a multiple of 128: both slots aligned
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t n0 = blockIdx.x * BN, gmb0 = blockIdx.y * MM_MB;
     const uint32_t mpad = (m + MM_BM - 1) / MM_BM * MM_BM, nmb = min((uint32_t)MM_MB, mpad / MM_BM - gmb0);
@@ -261,7 +282,8 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
     }
     if (tid == 0) {
         for (int i = 0; i < 2; ++i) { mbar_init(&wfull[i], MM_DQ_THREADS); mbar_init(&wfree[i], 1); }
-        for (int i = 0; i < MM_XS; ++i) { mbar_init(&xfull[i], 1); mbar_init(&xfree[i], 1); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&rfull[i], 1); mbar_init(&rfree[i], MM_DQ_THREADS); }
+        for (int i = 0; i < XS; ++i) { mbar_init(&xfull[i], 1); mbar_init(&xfree[i], 1); }
         mbar_init(&done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -279,11 +301,21 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
             if (use > 0) mbar_wait(&wfree[slot], (use - 1) & 1, errf);
             uint8_t* wh = wsm + slot * 2 * WB;
             uint8_t* wl = wh + WB;
+            const uint32_t lb = kb / KSTEPS_PER_BLOCK;   // staged: the raw block step of this K step
+            if (STAGE && kb % KSTEPS_PER_BLOCK == 0) mbar_wait(&rfull[lb & 1], (lb >> 1) & 1, errf);
+            const uint8_t* rblk = rsm + (lb & 1) * RB;
 #pragma unroll
             for (uint32_t it = tid; it < (uint32_t)BN * 8; it += MM_DQ_THREADS) {   // BN / 32 independent items
                 const uint32_t r = it % BN, kc = it / BN, n = n0 + r, k0 = (kb0 + kb) * MM_BK + kc * 8;
                 float v[8];
-                if (BS >= 8 && n < n_rows && k0 + 8 <= k_cols) {   // the 8 elements share one block
+                if (STAGE) {
+                    if (n < n_rows) {
+                        deq8<DT>(rblk + r * BB, (int)(k0 % BS), v);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) v[j] = 0.f;
+                    }
+                } else if (BS >= 8 && n < n_rows && k0 + 8 <= k_cols) {   // the 8 elements share one block
                     deq8<DT>(w + (uint64_t)n * row_bytes + (uint64_t)(k0 / BS) * BB, (int)(k0 % BS), v);
                 } else {
 #pragma unroll
@@ -299,6 +331,8 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
                 *reinterpret_cast<uint4*>(wh + kc * (BN * 16) + r * 16) = h;
                 *reinterpret_cast<uint4*>(wl + kc * (BN * 16) + r * 16) = l;
             }
+            if (STAGE && (kb % KSTEPS_PER_BLOCK == KSTEPS_PER_BLOCK - 1 || kb + 1 == nk))
+                mbar_arrive(&rfree[lb & 1]);   // this raw slot is read
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic stores -> tensor-core reads
             mbar_arrive(&wfull[slot]);
         }
@@ -306,16 +340,31 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
         // ---------------- issuer ----------------
         const uint32_t total = nk * nmb;   // X tiles, K-step-major
         auto load_x = [&](uint32_t seq) {
-            const uint32_t q = seq % MM_XS, kb = seq / nmb, mb = seq % nmb;
-            if (seq >= (uint32_t)MM_XS) mbar_wait(&xfree[q], ((seq / MM_XS) - 1) & 1, errf);
+            const uint32_t q = seq % XS, kb = seq / nmb, mb = seq % nmb;
+            if (seq >= (uint32_t)XS) mbar_wait(&xfree[q], ((seq / XS) - 1) & 1, errf);
             mbar_arrive_expect_tx(&xfull[q], 2 * MM_X_BYTES);
             const size_t src = ((size_t)(gmb0 + mb) * nk_all + kb0 + kb) * MM_X_BYTES;
             bulk_g2s(xsm + q * 2 * MM_X_BYTES, xh + src, MM_X_BYTES, &xfull[q]);
             bulk_g2s(xsm + q * 2 * MM_X_BYTES + MM_X_BYTES, xl + src, MM_X_BYTES, &xfull[q]);
         };
+        // staged: raw blocks of block step lb (x = byte offset of the block in a row, y = first row)
+        const uint32_t nblk = STAGE ? nk / KSTEPS_PER_BLOCK : 0u;
+        auto load_raw = [&](uint32_t lb) {
+            const uint32_t q = lb & 1;
+            if (lb >= 2) mbar_wait(&rfree[q], ((lb >> 1) - 1) & 1, errf);
+            mbar_arrive_expect_tx(&rfull[q], RB);
+            const int x = (int)((kb0 / KSTEPS_PER_BLOCK + lb) * BB), yrow = (int)n0;
+            asm volatile(
+                "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+                "[%4];" ::"r"(smem_addr(rsm + q * RB)),
+                "l"(reinterpret_cast<uint64_t>(&wmap)), "r"(x), "r"(yrow), "r"(smem_addr(&rfull[q]))
+                : "memory");
+        };
+        if constexpr (STAGE)
+            for (uint32_t lb = 0; lb < 2 && lb < nblk; ++lb) load_raw(lb);
         // the CTA's weight rows into L2 ahead of the dequantising warps: one bulk
         // prefetch per row (16-byte aligned, clipped to the matrix)
-        {
+        if (!STAGE) {
             const uintptr_t wend = ((uintptr_t)w + (uint64_t)n_rows * row_bytes) & ~(uintptr_t)15;
             const uint64_t c0 = (uint64_t)(kb0 * MM_BK) / BS * BB;
             const uint64_t c1 = min((uint64_t)((kb0 + nk) * MM_BK + BS - 1) / BS * BB, row_bytes);
@@ -327,16 +376,18 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
                     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"((uint32_t)(e - a)) : "memory");
             }
         }
-        for (uint32_t seq = 0; seq + 1 < (uint32_t)MM_XS && seq < total; ++seq) load_x(seq);
+        for (uint32_t seq = 0; seq + 1 < (uint32_t)XS && seq < total; ++seq) load_x(seq);
         const uint32_t w0 = smem_addr(wsm), x0 = smem_addr(xsm);
         for (uint32_t kb = 0; kb < nk; ++kb) {
             const uint32_t slot = kb & 1;
             mbar_wait(&wfull[slot], (kb >> 1) & 1, errf);
             tc_fence_after();
+            if (STAGE && kb % KSTEPS_PER_BLOCK == KSTEPS_PER_BLOCK - 1 && kb / KSTEPS_PER_BLOCK + 2 < nblk)
+                load_raw(kb / KSTEPS_PER_BLOCK + 2);   // its slot's block was dequantised (before wfull)
             const uint32_t bh = w0 + slot * 2 * WB, bl = bh + WB;
             for (uint32_t mb = 0; mb < nmb; ++mb) {
-                const uint32_t seq = kb * nmb + mb, q = seq % MM_XS;
-                mbar_wait(&xfull[q], (seq / MM_XS) & 1, errf);
+                const uint32_t seq = kb * nmb + mb, q = seq % XS;
+                mbar_wait(&xfull[q], (seq / XS) & 1, errf);
                 tc_fence_after();
                 const uint32_t ah = x0 + q * 2 * MM_X_BYTES, al = ah + MM_X_BYTES;
                 const uint32_t d = tmem + mb * BN;
@@ -351,7 +402,7 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
                     tc_mma(d, dal, dbh, IDESC, 1u);
                 }
                 tc_commit(&xfree[q]);
-                if (seq + MM_XS - 1 < total) load_x(seq + MM_XS - 1);   // into the slot of tile seq - 1
+                if (seq + XS - 1 < total) load_x(seq + XS - 1);   // into the slot of tile seq - 1
             }
             tc_commit(&wfree[slot]);
         }

@@ -56,6 +56,21 @@ def test_matmul_shapes(ggc, orc, ctx, rows, cols, m):
         assert rel_l2(got[r], t.matvec(x[r])) <= REL_L2
 
 
+@pytest.mark.parametrize("dtname", ["Q4_K", "Q5_K"])
+@pytest.mark.parametrize("rows,cols,m", [(200, 256 * 37, 70), (130, 256, 513), (64, 256 * 5, 1)],
+                         ids=["split-k-37-blocks", "one-block-two-passes", "m1"])
+def test_matmul_staged_raw_blocks(ggc, orc, ctx, dtname, rows, cols, m):
+    """Q4_K / Q5_K stage their raw blocks in shared memory by TMA: ragged rows
+    (zero-filled past the matrix), K split in whole blocks, one-block rows."""
+    dt = getattr(ggc, dtname)
+    w, x, want = case(orc, dt, rows, cols, m, 34)
+    t = ggc.Tensor(w, dt, (cols, rows), repack=False, ctx=ctx)
+    got = t.matmul(x)
+    assert got.shape == (m, rows) and np.all(np.isfinite(got))
+    assert rel_l2(got, want) <= REL_L2, rel_l2(got, want)
+    assert np.array_equal(got, t.matmul(x))          # deterministic
+
+
 def test_matmul_device_buffers_and_repeat(ggc, orc, ctx):
     import torch
     dt, rows, cols, m = ggc.Q6_K, 256, 1024, 300
