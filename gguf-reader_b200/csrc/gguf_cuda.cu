@@ -815,6 +815,26 @@ bool raw_row_map(CUtensorMap* map, const uint8_t* w, uint32_t rows, uint64_t row
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// K split of the product: ks ranges of kb_per K steps (kb_per a multiple of
+// `step`, no empty range) minimising the estimated time in K steps of one CTA:
+// waves of `tiles` x ks CTAs over the SMs times kb_per, plus the partial slices'
+// write + read (m x n x 8 bytes a split, about 12 MB per K step's time).
+void mm_split(uint32_t nk, uint32_t step, uint32_t tiles, uint32_t sms, uint32_t m, uint32_t n, uint32_t* ks_out,
+              uint32_t* kb_per_out) {
+    const double part = (double)m * n * 8.0 / 12e6;
+    double best = 1e300;
+    for (uint32_t c = 1; c <= std::max(nk / step, 1u); ++c) {
+        const uint32_t kb_per = cdiv<uint32_t>(cdiv<uint32_t>(nk, c), step) * step, ks = cdiv<uint32_t>(nk, kb_per);
+        if (ks != c) continue;
+        const double cost = (double)cdiv<uint32_t>(tiles * ks, sms) * kb_per + (ks > 1 ? ks * part : 0.0);
+        if (cost < best) {
+            best = cost;
+            *ks_out = ks;
+            *kb_per_out = kb_per;
+        }
+    }
+}
+
 // 128 weight rows x 512 tokens per CTA; K split over enough CTAs to fill the
 // SMs (partials summed in split order by k_mm_reduce).  Q4_K / Q5_K stage their
 // raw blocks by TMA (split ranges of whole 256-element blocks) when the tensor
@@ -840,10 +860,8 @@ struct RunMM {
         const uint32_t smem = mm_smem(MM_BN, STAGE, block_bytes_of(DT));
         const uint32_t gx = cdiv<uint32_t>(n, MM_BN), gy = cdiv<uint32_t>(cdiv<uint32_t>(m, MM_BM), MM_MB);
         const uint32_t nk = kpad / MM_BK, step = STAGE ? (uint32_t)(block_size_of(DT) / MM_BK) : 1u;
-        uint32_t ks = cdiv<uint32_t>((uint32_t)ctx->num_sms, gx * gy);
-        ks = ks < 1 ? 1 : (ks > nk / step ? nk / step : ks);
-        const uint32_t kb_per = cdiv<uint32_t>(cdiv<uint32_t>(nk, ks), step) * step;   // whole staged blocks
-        ks = cdiv<uint32_t>(nk, kb_per);   // no empty split
+        uint32_t ks = 1, kb_per = nk;
+        mm_split(nk, step, gx * gy, (uint32_t)ctx->num_sms, m, n, &ks, &kb_per);
         if (ks == 1) {
             *err = launch(ctx, k_mm_tc<DT, MM_BN, STAGE>, dim3(gx, gy, 1), dim3(MM_THREADS), smem, w, n, k, xh, xl,
                           m, kpad, kb_per, y, ldy, resid, errf, map);

@@ -32,20 +32,21 @@ constexpr int MM_BM = 128;                 // tokens per M-block (UMMA M, TMEM l
 constexpr int MM_MB = 4;                   // M-blocks per CTA (512 tokens: W dequantised once)
 constexpr int MM_BK = 64;                  // K per stage
 constexpr int MM_DQ_THREADS = 256;         // 8 dequantising / epilogue warps
-constexpr int MM_THREADS = MM_DQ_THREADS + 32;   // + the issuer warp (TMEM owner, X copies, MMAs)
-constexpr int MM_XS = 4;                   // X tile ring slots
+constexpr int MM_THREADS = MM_DQ_THREADS + 64;   // + the MMA issuer warp (TMEM owner) + the copy warp
+constexpr int MM_XS = 8;                   // X half-tile ring slots
 constexpr uint32_t MM_TOKENS = MM_BM * MM_MB;
-constexpr uint32_t MM_X_BYTES = MM_BM * MM_BK * 2;          // one bf16 X tile (hi or lo), 16 KB
+constexpr uint32_t MM_X_BYTES = MM_BM * MM_BK * 2;          // one bf16 X tile (hi or lo) of a K step, 16 KB
+constexpr uint32_t MM_XH_BYTES = MM_X_BYTES / 2;            // its K half (32 columns), 8 KB
 constexpr int MM_BN = 128;                 // weight rows per CTA (UMMA N); TMEM: MM_MB x 128 = all 512 columns
 constexpr uint32_t mm_w_bytes(int bn) { return (uint32_t)bn * MM_BK * 2; }
 // formats whose raw blocks the product stages in shared memory by TMA (256-element
 // blocks of a 16-byte multiple: every block of a raw row starts 16-byte aligned)
 constexpr bool mm_staged(int dt) { return dt == GGC_Q4_K || dt == GGC_Q5_K; }
-constexpr int mm_xs(bool staged) { return staged ? 3 : MM_XS; }   // X ring slots (smem for the raw ring)
-// dynamic shared memory: W ring [2][hi, lo], X ring [XS][hi, lo], staged: raw ring [2][bn rows][bb]
-// at the next 128-byte boundary (the TMA destination alignment)
+constexpr int mm_xs(bool staged) { return staged ? 6 : MM_XS; }   // X ring slots (smem for the raw ring)
+// dynamic shared memory: W ring [2][hi, lo], X ring [XS][hi, lo] half tiles, staged: raw ring
+// [2][bn rows][bb] at the next 128-byte boundary (the TMA destination alignment)
 constexpr uint32_t mm_smem(int bn, bool staged = false, int bb = 0) {
-    return 2 * 2 * mm_w_bytes(bn) + mm_xs(staged) * 2 * MM_X_BYTES + (staged ? 2u * bn * (uint32_t)bb + 128u : 0u);
+    return 2 * 2 * mm_w_bytes(bn) + mm_xs(staged) * 2 * MM_XH_BYTES + (staged ? 2u * bn * (uint32_t)bb + 128u : 0u);
 }
 // instruction descriptor: D f32, A/B bf16, both K-major, N = bn, M = 128
 constexpr uint32_t mm_idesc(int bn) {
@@ -231,17 +232,20 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_x_split(const float* __restri
 // Y[m][n] (+)= X . W^T.  Block = 8 dequantising warps + 1 issuer warp.
 //   dequant warps: W tile of K step kb (BN rows x 64) -> bf16 hi / lo into W
 //     slot kb % 2 (after the MMAs of kb - 2 freed it: wfree), arrive on wfull;
-//   issuer (warp 8, one lane): keeps MM_XS X tiles (one M-block x K step, hi +
-//     lo) in flight by bulk copy (xfull; a slot is refilled after the MMAs that
-//     read it completed: xfree), and for each K step waits for the W slot, then
-//     per M-block for its X tile, issues 4 x 3 MMAs into the M-block's TMEM
-//     columns and commits them to xfree; the step's commit frees the W slot, the
-//     last one signals `done`;
+//   copy warp (warp 9, one lane): keeps the X ring full by bulk copy -- one slot
+//     = one M-block x half a K step (32 columns), hi + lo, 16 KB (xfull; a slot
+//     is refilled after the MMAs that read it completed: xfree) -- and, for the
+//     staged formats, the raw ring;
+//   MMA issuer (warp 8, one lane, TMEM owner): for each K step waits for the W
+//     slot, then per M-block and K half for its X slot, issues 2 x 3 MMAs into
+//     the M-block's TMEM columns and commits them to xfree; the step's commit
+//     frees the W slot, the last one signals `done`.  It never waits on a free
+//     slot, so the tensor pipe's queue stays full while copies are in flight;
 //   epilogue: the 8 warps read TMEM (warp w: lanes 32 (w % 4).., M-blocks of
 //     half w / 4) and write Y (+ the residual).
 // Every wait is bounded (ERRF_TIMEOUT); no thread leaves early, warp 8 frees TMEM.
 //
-// STAGE (the mm_staged formats Q4_K, Q5_K): the issuer also loads the CTA's raw
+// STAGE (the mm_staged formats Q4_K, Q5_K): the copy warp also loads the CTA's raw
 // blocks of each 256-element K range (BN rows x one block, rows past the matrix
 // zero-filled) with one 2-D TMA copy (tensor map over the raw rows as bytes,
 // no multicast) into a 2-slot ring (rfull / rfree), so the dequantising warps
@@ -261,8 +265,8 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
     __shared__ uint64_t wfull[2], wfree[2], xfull[MM_XS], xfree[MM_XS], rfull[2], rfree[2], done;
     __shared__ uint32_t s_tmem;
     uint8_t* wsm = smem;                  // [2 slots][hi, lo][WB]
-    uint8_t* xsm = smem + 4 * WB;         // [XS slots][hi, lo][MM_X_BYTES]
-    uint8_t* rsm = xsm + XS * 2 * MM_X_BYTES;   // staged: [2 slots][BN rows][BB] raw blocks
+    uint8_t* xsm = smem + 4 * WB;         // [XS slots][hi, lo][MM_XH_BYTES]
+    uint8_t* rsm = xsm + XS * 2 * MM_XH_BYTES;   // staged: [2 slots][BN rows][BB] raw blocks
     rsm += (128u - (smem_addr(rsm) & 127u)) & 127u;   // RB is a multiple of 128: both slots aligned
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t n0 = blockIdx.x * BN, gmb0 = blockIdx.y * MM_MB;
@@ -336,16 +340,17 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic stores -> tensor-core reads
             mbar_arrive(&wfull[slot]);
         }
-    } else if (lane == 0) {
-        // ---------------- issuer ----------------
-        const uint32_t total = nk * nmb;   // X tiles, K-step-major
+    } else if (warp == 9 && lane == 0) {
+        // ---------------- copy warp ----------------
+        // X slot seq = (K step, M-block, K half), K-step-major; its source is half h of
+        // the pre-tiled X tile (M-block, K step)
         auto load_x = [&](uint32_t seq) {
-            const uint32_t q = seq % XS, kb = seq / nmb, mb = seq % nmb;
+            const uint32_t q = seq % XS, h = seq & 1, mb = (seq >> 1) % nmb, kb = (seq >> 1) / nmb;
             if (seq >= (uint32_t)XS) mbar_wait(&xfree[q], ((seq / XS) - 1) & 1, errf);
-            mbar_arrive_expect_tx(&xfull[q], 2 * MM_X_BYTES);
-            const size_t src = ((size_t)(gmb0 + mb) * nk_all + kb0 + kb) * MM_X_BYTES;
-            bulk_g2s(xsm + q * 2 * MM_X_BYTES, xh + src, MM_X_BYTES, &xfull[q]);
-            bulk_g2s(xsm + q * 2 * MM_X_BYTES + MM_X_BYTES, xl + src, MM_X_BYTES, &xfull[q]);
+            mbar_arrive_expect_tx(&xfull[q], 2 * MM_XH_BYTES);
+            const size_t src = ((size_t)(gmb0 + mb) * nk_all + kb0 + kb) * MM_X_BYTES + h * MM_XH_BYTES;
+            bulk_g2s(xsm + q * 2 * MM_XH_BYTES, xh + src, MM_XH_BYTES, &xfull[q]);
+            bulk_g2s(xsm + q * 2 * MM_XH_BYTES + MM_XH_BYTES, xl + src, MM_XH_BYTES, &xfull[q]);
         };
         // staged: raw blocks of block step lb (x = byte offset of the block in a row, y = first row)
         const uint32_t nblk = STAGE ? nk / KSTEPS_PER_BLOCK : 0u;
@@ -360,11 +365,11 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
                 "l"(reinterpret_cast<uint64_t>(&wmap)), "r"(x), "r"(yrow), "r"(smem_addr(&rfull[q]))
                 : "memory");
         };
-        if constexpr (STAGE)
+        if constexpr (STAGE) {
             for (uint32_t lb = 0; lb < 2 && lb < nblk; ++lb) load_raw(lb);
-        // the CTA's weight rows into L2 ahead of the dequantising warps: one bulk
-        // prefetch per row (16-byte aligned, clipped to the matrix)
-        if (!STAGE) {
+        } else {
+            // the CTA's weight rows into L2 ahead of the dequantising warps: one bulk
+            // prefetch per row (16-byte aligned, clipped to the matrix)
             const uintptr_t wend = ((uintptr_t)w + (uint64_t)n_rows * row_bytes) & ~(uintptr_t)15;
             const uint64_t c0 = (uint64_t)(kb0 * MM_BK) / BS * BB;
             const uint64_t c1 = min((uint64_t)((kb0 + nk) * MM_BK + BS - 1) / BS * BB, row_bytes);
@@ -376,33 +381,39 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
                     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"((uint32_t)(e - a)) : "memory");
             }
         }
-        for (uint32_t seq = 0; seq + 1 < (uint32_t)XS && seq < total; ++seq) load_x(seq);
+        for (uint32_t kb = 0; kb < nk; ++kb) {
+            // raw block lb + 1 when K step 4 lb is next: its slot held block lb - 1,
+            // which the dequantising warps finished before the MMAs of K step 4 lb - 1
+            if (STAGE && kb % KSTEPS_PER_BLOCK == 0 && kb >= KSTEPS_PER_BLOCK && kb / KSTEPS_PER_BLOCK + 1 < nblk)
+                load_raw(kb / KSTEPS_PER_BLOCK + 1);
+            for (uint32_t i = 0; i < 2 * nmb; ++i) load_x(kb * 2 * nmb + i);
+        }
+    } else if (warp == 8 && lane == 0) {
+        // ---------------- MMA issuer ----------------
         const uint32_t w0 = smem_addr(wsm), x0 = smem_addr(xsm);
         for (uint32_t kb = 0; kb < nk; ++kb) {
             const uint32_t slot = kb & 1;
             mbar_wait(&wfull[slot], (kb >> 1) & 1, errf);
             tc_fence_after();
-            if (STAGE && kb % KSTEPS_PER_BLOCK == KSTEPS_PER_BLOCK - 1 && kb / KSTEPS_PER_BLOCK + 2 < nblk)
-                load_raw(kb / KSTEPS_PER_BLOCK + 2);   // its slot's block was dequantised (before wfull)
             const uint32_t bh = w0 + slot * 2 * WB, bl = bh + WB;
-            for (uint32_t mb = 0; mb < nmb; ++mb) {
-                const uint32_t seq = kb * nmb + mb, q = seq % XS;
+            for (uint32_t i = 0; i < 2 * nmb; ++i) {
+                const uint32_t seq = kb * 2 * nmb + i, q = seq % XS, h = i & 1, mb = i >> 1;
                 mbar_wait(&xfull[q], (seq / XS) & 1, errf);
                 tc_fence_after();
-                const uint32_t ah = x0 + q * 2 * MM_X_BYTES, al = ah + MM_X_BYTES;
+                const uint32_t ah = x0 + q * 2 * MM_XH_BYTES, al = ah + MM_XH_BYTES;
                 const uint32_t d = tmem + mb * BN;
 #pragma unroll
-                for (uint32_t j = 0; j < MM_BK / 16; ++j) {
+                for (uint32_t j = 0; j < 2; ++j) {   // the two 16-column steps of this K half
+                    const uint32_t kk = 2 * h + j;   // 16-column step within the K step
                     const uint64_t dah = mm_desc(ah + 2 * j * (MM_BM * 16), MM_BM * 16, 128);
                     const uint64_t dal = mm_desc(al + 2 * j * (MM_BM * 16), MM_BM * 16, 128);
-                    const uint64_t dbh = mm_desc(bh + 2 * j * (BN * 16), BN * 16, 128);
-                    const uint64_t dbl = mm_desc(bl + 2 * j * (BN * 16), BN * 16, 128);
-                    tc_mma(d, dah, dbh, IDESC, (kb > 0 || j > 0) ? 1u : 0u);
+                    const uint64_t dbh = mm_desc(bh + 2 * kk * (BN * 16), BN * 16, 128);
+                    const uint64_t dbl = mm_desc(bl + 2 * kk * (BN * 16), BN * 16, 128);
+                    tc_mma(d, dah, dbh, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
                     tc_mma(d, dah, dbl, IDESC, 1u);
                     tc_mma(d, dal, dbh, IDESC, 1u);
                 }
                 tc_commit(&xfree[q]);
-                if (seq + XS - 1 < total) load_x(seq + XS - 1);   // into the slot of tile seq - 1
             }
             tc_commit(&wfree[slot]);
         }
