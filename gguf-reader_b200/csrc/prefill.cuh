@@ -75,17 +75,20 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void tc_ld16(uint32_t taddr, float* v) {
-    uint32_t r[16];
+// 32 consecutive TMEM columns of this thread's lane (32x32b shape, 32 repeats)
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, float* v) {
+    uint32_t r[32];
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
-        "[%16];"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // hi + lo bf16 split of 8 floats, packed as two 16-byte rows
@@ -420,26 +423,35 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
         tc_commit(&done);
     }
     // ---------------- epilogue ----------------
+    // per warp: TMEM lanes 32 (w % 4).. (tokens) of the M-blocks of half w / 4, in
+    // 32-column chunks; each chunk goes through a padded 32 x 33 staging tile in
+    // the W ring (free: every MMA has completed) so that a store instruction
+    // writes 32 consecutive floats of one token row (one 128-byte line)
     if (warp < 8) {
         mbar_wait(&done, 0, errf);
         tc_fence_after();
         const uint32_t quarter = warp & 3, half = warp >> 2;
+        float* stg = reinterpret_cast<float*>(smem) + warp * (32 * 33);
         for (uint32_t mb = half * 2; mb < half * 2 + 2 && mb < nmb; ++mb) {
-            const uint32_t row = (gmb0 + mb) * MM_BM + quarter * 32 + lane;
+            const uint32_t row0 = (gmb0 + mb) * MM_BM + quarter * 32;
 #pragma unroll 1
-            for (uint32_t c0 = 0; c0 < (uint32_t)BN; c0 += 16) {
-                float v[16];
-                tc_ld16(tmem + ((quarter * 32) << 16) + mb * BN + c0, v);
-                if (row < m) {
+            for (uint32_t c0 = 0; c0 < (uint32_t)BN; c0 += 32) {
+                float v[32];
+                tc_ld32(tmem + ((quarter * 32) << 16) + mb * BN + c0, v);
 #pragma unroll
-                    for (int c = 0; c < 16; ++c) {
-                        const uint32_t n = n0 + c0 + c;
-                        if (n < n_rows) {
-                            const size_t idx = (size_t)row * ldy + n;
-                            y[idx] = resid ? __fadd_rn(resid[idx], v[c]) : v[c];
-                        }
+                for (int c = 0; c < 32; ++c) stg[lane * 33 + c] = v[c];
+                __syncwarp();
+                const uint32_t n = n0 + c0 + lane;
+#pragma unroll 4
+                for (uint32_t r = 0; r < 32; ++r) {
+                    const uint32_t row = row0 + r;
+                    if (row < m && n < n_rows) {
+                        const size_t idx = (size_t)row * ldy + n;
+                        const float t = stg[r * 33 + lane];
+                        y[idx] = resid ? __fadd_rn(resid[idx], t) : t;
                     }
                 }
+                __syncwarp();
             }
         }
     }
