@@ -858,7 +858,7 @@ struct RunMM {
         *err = set_attr<STAGE>();
         if (*err != cudaSuccess) return;
         const uint32_t smem = mm_smem(MM_BN, STAGE, block_bytes_of(DT));
-        const uint32_t gx = cdiv<uint32_t>(n, MM_BN), gy = cdiv<uint32_t>(cdiv<uint32_t>(m, MM_BM), MM_MB);
+        const uint32_t gx = cdiv<uint32_t>(n, MM_BN), gy = cdiv<uint32_t>(cdiv<uint32_t>(m, MM_TG), MM_NTG);
         const uint32_t nk = kpad / MM_BK, step = STAGE ? (uint32_t)(block_size_of(DT) / MM_BK) : 1u;
         uint32_t ks = 1, kb_per = nk;
         mm_split(nk, step, gx * gy, (uint32_t)ctx->num_sms, m, n, &ks, &kb_per);
@@ -907,7 +907,7 @@ int ctx_errf(ggc_ctx* ctx, int** out) {
 int split_rows(ggc_ctx* ctx, const float* x, const float* x2, uint32_t m, uint32_t k, uint32_t ldx, int pro,
                uint8_t** xh, uint8_t** xl, uint32_t* kpad) {
     *kpad = (k + MM_BK - 1) / MM_BK * MM_BK;
-    const uint32_t mpad = (m + MM_BM - 1) / MM_BM * MM_BM;
+    const uint32_t mpad = (m + MM_TG - 1) / MM_TG * MM_TG;
     const size_t bytes = (size_t)mpad * *kpad * 2;
     GGC_TRY(ensure_stage(ctx, 3, bytes));
     GGC_TRY(ensure_stage(ctx, 4, bytes));

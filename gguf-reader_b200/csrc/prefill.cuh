@@ -1,22 +1,23 @@
 // prefill.cuh -- the batched (prompt / prefill) path: a quantized-weight matrix
 // product on the 5th-generation tensor cores, and the per-token kernels around it.
 //
-// k_mm_tc<DT, BN>: Y[m][n] (+)= X[m][k] . W[n][k]^T with W in raw GGUF blocks.
-//   * CTA = BN (64, or 32 for narrow W) weight rows x up to 512 tokens (MM_MB
-//     M-blocks of 128): the f32 accumulators of all its tokens live in tensor
-//     memory (4 x BN columns of 128 lanes), so each W tile is read from HBM and
-//     dequantised (bit-exact, dequant.cuh) once per CTA and X tiles come from L2.
+// k_mm_tc<DT, BN, STAGE>: Y[m][n] (+)= X[m][k] . W[n][k]^T with W in raw GGUF blocks.
+//   * CTA = 128 weight rows x up to 512 tokens: D = W . X^T with the weight rows
+//     as the UMMA M side (TMEM lanes) and two 256-token groups as N (2 x 256 f32
+//     columns = all of TMEM), so each W tile is read from HBM and dequantised
+//     (bit-exact, dequant.cuh) once per CTA and X tiles come from L2.
 //   * Precision: W and X are each split into bf16 hi + lo (v = hi + lo to ~16
-//     mantissa bits) and D accumulates hi.hi + hi.lo + lo.hi in f32
+//     mantissa bits) and D accumulates Wh.Xh + Wl.Xh + Wh.Xl in f32
 //     (tcgen05.mma kind::f16, bf16 operands): ~1e-5 relative per product, within
 //     the 1e-4 relative-L2 parity bar that plain bf16 (~1e-3) misses.
 //   * Shared-memory operands use the canonical K-major layout without swizzle
 //     (8-row x 16-byte core matrices: byte (row, kchunk) = kchunk*rows*16 +
 //     row*16, so LBO = rows*16 between K chunks, SBO = 128 between 8-row
 //     groups); X arrives in that layout by bulk copy (k_x_split writes it so),
-//     W is dequantised into it by 8 warps while one issuer thread keeps the X
-//     copies and the MMAs going (mbarrier rings, see the kernel).
-//   * Epilogue: tcgen05.ld of the TMEM rows (tokens), Y (+ residual) stores.
+//     W is dequantised into it by 8 warps while a copy warp keeps the X (and raw
+//     W) rings full and one issuer thread the MMAs (mbarrier rings, see the kernel).
+//   * Epilogue: tcgen05.ld of the TMEM lanes (weight rows): for each token a
+//     warp stores 32 consecutive floats of a Y row (+ residual).
 //     TMEM is freed on every path; every wait is bounded.
 #pragma once
 #include <cuda.h>   // CUtensorMap (the tensor-map type only)
@@ -28,29 +29,29 @@
 
 namespace ggc {
 
-constexpr int MM_BM = 128;                 // tokens per M-block (UMMA M, TMEM lanes)
-constexpr int MM_MB = 4;                   // M-blocks per CTA (512 tokens: W dequantised once)
+constexpr int MM_TG = 256;                 // tokens per token group (UMMA N: TMEM columns of one accumulator)
+constexpr int MM_NTG = 2;                  // token groups per CTA (512 tokens: W dequantised once)
 constexpr int MM_BK = 64;                  // K per stage
 constexpr int MM_DQ_THREADS = 256;         // 8 dequantising / epilogue warps
 constexpr int MM_THREADS = MM_DQ_THREADS + 64;   // + the MMA issuer warp (TMEM owner) + the copy warp
-constexpr int MM_XS = 8;                   // X half-tile ring slots
-constexpr uint32_t MM_TOKENS = MM_BM * MM_MB;
-constexpr uint32_t MM_X_BYTES = MM_BM * MM_BK * 2;          // one bf16 X tile (hi or lo) of a K step, 16 KB
-constexpr uint32_t MM_XH_BYTES = MM_X_BYTES / 2;            // its K half (32 columns), 8 KB
-constexpr int MM_BN = 128;                 // weight rows per CTA (UMMA N); TMEM: MM_MB x 128 = all 512 columns
+constexpr int MM_XS = 8;                   // X quarter-tile ring slots
+constexpr uint32_t MM_TOKENS = MM_TG * MM_NTG;
+constexpr uint32_t MM_X_BYTES = MM_TG * MM_BK * 2;          // one bf16 X tile (hi or lo): token group x K step, 32 KB
+constexpr uint32_t MM_XQ_BYTES = MM_X_BYTES / 4;            // its K quarter (16 columns), 8 KB
+constexpr int MM_BN = 128;                 // weight rows per CTA (UMMA M = TMEM lanes); TMEM: 2 x 256 = all 512 columns
 constexpr uint32_t mm_w_bytes(int bn) { return (uint32_t)bn * MM_BK * 2; }
 // formats whose raw blocks the product stages in shared memory by TMA (256-element
 // blocks of a 16-byte multiple: every block of a raw row starts 16-byte aligned)
 constexpr bool mm_staged(int dt) { return dt == GGC_Q4_K || dt == GGC_Q5_K; }
 constexpr int mm_xs(bool staged) { return staged ? 6 : MM_XS; }   // X ring slots (smem for the raw ring)
-// dynamic shared memory: W ring [2][hi, lo], X ring [XS][hi, lo] half tiles, staged: raw ring
+// dynamic shared memory: W ring [2][hi, lo], X ring [XS][hi, lo] quarter tiles, staged: raw ring
 // [2][bn rows][bb] at the next 128-byte boundary (the TMA destination alignment)
 constexpr uint32_t mm_smem(int bn, bool staged = false, int bb = 0) {
-    return 2 * 2 * mm_w_bytes(bn) + mm_xs(staged) * 2 * MM_XH_BYTES + (staged ? 2u * bn * (uint32_t)bb + 128u : 0u);
+    return 2 * 2 * mm_w_bytes(bn) + mm_xs(staged) * 2 * MM_XQ_BYTES + (staged ? 2u * bn * (uint32_t)bb + 128u : 0u);
 }
-// instruction descriptor: D f32, A/B bf16, both K-major, N = bn, M = 128
+// instruction descriptor: D f32, A/B bf16, both K-major, M = bn weight rows, N = MM_TG tokens
 constexpr uint32_t mm_idesc(int bn) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(MM_BM >> 4) << 24);
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(MM_TG >> 3) << 17) | ((uint32_t)(bn >> 4) << 24);
 }
 
 // shared-memory matrix descriptor: K-major, no swizzle, version 1
@@ -210,7 +211,7 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_x_split(const float* __restri
         __syncthreads();
         scale = s_scale;
     }
-    const size_t tile0 = (size_t)(row / MM_BM) * nk * MM_X_BYTES + (row % MM_BM) * 16;
+    const size_t tile0 = (size_t)(row / MM_TG) * nk * MM_X_BYTES + (row % MM_TG) * 16;
     for (uint32_t c = threadIdx.x; c < kpad / 8; c += SPLIT_THREADS) {
         float v[8];
 #pragma unroll
@@ -226,7 +227,7 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_x_split(const float* __restri
         }
         uint4 h, l;
         split8(v, h, l);
-        const size_t off = tile0 + (size_t)(c / 8) * MM_X_BYTES + (c % 8) * (MM_BM * 16);
+        const size_t off = tile0 + (size_t)(c / 8) * MM_X_BYTES + (c % 8) * (MM_TG * 16);
         *reinterpret_cast<uint4*>(xh + off) = h;
         *reinterpret_cast<uint4*>(xl + off) = l;
     }
@@ -262,18 +263,19 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
     static_assert(!STAGE || (mm_staged(DT) && BS == 4 * MM_BK && BB % 16 == 0 && (BN * BB) % 128 == 0),
                   "staged: 256-element blocks of a 16-byte multiple");
     constexpr int XS = mm_xs(STAGE);
-    constexpr uint32_t WB = mm_w_bytes(BN), TCOLS = MM_MB * BN, IDESC = mm_idesc(BN), RB = (uint32_t)BN * BB;
+    static_assert(BN == 128, "UMMA M = 128 weight rows (all TMEM lanes)");
+    constexpr uint32_t WB = mm_w_bytes(BN), TCOLS = MM_NTG * MM_TG, IDESC = mm_idesc(BN), RB = (uint32_t)BN * BB;
     constexpr uint32_t KSTEPS_PER_BLOCK = STAGE ? BS / MM_BK : 1;   // K steps per staged raw block (4)
     extern __shared__ __align__(128) uint8_t smem[];   // no-swizzle descriptors need 16-byte alignment
     __shared__ uint64_t wfull[2], wfree[2], xfull[MM_XS], xfree[MM_XS], rfull[2], rfree[2], done;
     __shared__ uint32_t s_tmem;
     uint8_t* wsm = smem;                  // [2 slots][hi, lo][WB]
-    uint8_t* xsm = smem + 4 * WB;         // [XS slots][hi, lo][MM_XH_BYTES]
-    uint8_t* rsm = xsm + XS * 2 * MM_XH_BYTES;   // staged: [2 slots][BN rows][BB] raw blocks
+    uint8_t* xsm = smem + 4 * WB;         // [XS slots][hi, lo][MM_XQ_BYTES]
+    uint8_t* rsm = xsm + XS * 2 * MM_XQ_BYTES;   // staged: [2 slots][BN rows][BB] raw blocks
     rsm += (128u - (smem_addr(rsm) & 127u)) & 127u;   // RB is a multiple of 128: both slots aligned
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t n0 = blockIdx.x * BN, gmb0 = blockIdx.y * MM_MB;
-    const uint32_t mpad = (m + MM_BM - 1) / MM_BM * MM_BM, nmb = min((uint32_t)MM_MB, mpad / MM_BM - gmb0);
+    const uint32_t n0 = blockIdx.x * BN, gtg0 = blockIdx.y * MM_NTG;
+    const uint32_t mpad = (m + MM_TG - 1) / MM_TG * MM_TG, ntg = min((uint32_t)MM_NTG, mpad / MM_TG - gtg0);
     // split K: this CTA's K steps [kb0, kb0 + nk) of the kpad / 64; its output
     // (a partial sum when gridDim.z > 1) goes to slice blockIdx.z of y
     const uint32_t nk_all = kpad / MM_BK, kb0 = blockIdx.z * kb_per;
@@ -345,15 +347,15 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
         }
     } else if (warp == 9 && lane == 0) {
         // ---------------- copy warp ----------------
-        // X slot seq = (K step, M-block, K half), K-step-major; its source is half h of
-        // the pre-tiled X tile (M-block, K step)
+        // X slot seq = (K step, token group, K quarter), K-step-major; its source is
+        // quarter kq of the pre-tiled X tile (token group, K step)
         auto load_x = [&](uint32_t seq) {
-            const uint32_t q = seq % XS, h = seq & 1, mb = (seq >> 1) % nmb, kb = (seq >> 1) / nmb;
+            const uint32_t q = seq % XS, kq = seq & 3, tg = (seq >> 2) % ntg, kb = (seq >> 2) / ntg;
             if (seq >= (uint32_t)XS) mbar_wait(&xfree[q], ((seq / XS) - 1) & 1, errf);
-            mbar_arrive_expect_tx(&xfull[q], 2 * MM_XH_BYTES);
-            const size_t src = ((size_t)(gmb0 + mb) * nk_all + kb0 + kb) * MM_X_BYTES + h * MM_XH_BYTES;
-            bulk_g2s(xsm + q * 2 * MM_XH_BYTES, xh + src, MM_XH_BYTES, &xfull[q]);
-            bulk_g2s(xsm + q * 2 * MM_XH_BYTES + MM_XH_BYTES, xl + src, MM_XH_BYTES, &xfull[q]);
+            mbar_arrive_expect_tx(&xfull[q], 2 * MM_XQ_BYTES);
+            const size_t src = ((size_t)(gtg0 + tg) * nk_all + kb0 + kb) * MM_X_BYTES + kq * MM_XQ_BYTES;
+            bulk_g2s(xsm + q * 2 * MM_XQ_BYTES, xh + src, MM_XQ_BYTES, &xfull[q]);
+            bulk_g2s(xsm + q * 2 * MM_XQ_BYTES + MM_XQ_BYTES, xl + src, MM_XQ_BYTES, &xfull[q]);
         };
         // staged: raw blocks of block step lb (x = byte offset of the block in a row, y = first row)
         const uint32_t nblk = STAGE ? nk / KSTEPS_PER_BLOCK : 0u;
@@ -389,7 +391,7 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
             // which the dequantising warps finished before the MMAs of K step 4 lb - 1
             if (STAGE && kb % KSTEPS_PER_BLOCK == 0 && kb >= KSTEPS_PER_BLOCK && kb / KSTEPS_PER_BLOCK + 1 < nblk)
                 load_raw(kb / KSTEPS_PER_BLOCK + 1);
-            for (uint32_t i = 0; i < 2 * nmb; ++i) load_x(kb * 2 * nmb + i);
+            for (uint32_t i = 0; i < 4 * ntg; ++i) load_x(kb * 4 * ntg + i);
         }
     } else if (warp == 8 && lane == 0) {
         // ---------------- MMA issuer ----------------
@@ -398,24 +400,21 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
             const uint32_t slot = kb & 1;
             mbar_wait(&wfull[slot], (kb >> 1) & 1, errf);
             tc_fence_after();
-            const uint32_t bh = w0 + slot * 2 * WB, bl = bh + WB;
-            for (uint32_t i = 0; i < 2 * nmb; ++i) {
-                const uint32_t seq = kb * 2 * nmb + i, q = seq % XS, h = i & 1, mb = i >> 1;
+            const uint32_t wh = w0 + slot * 2 * WB, wl = wh + WB;
+            for (uint32_t i = 0; i < 4 * ntg; ++i) {
+                const uint32_t seq = kb * 4 * ntg + i, q = seq % XS, kk = i & 3, tg = i >> 2;
                 mbar_wait(&xfull[q], (seq / XS) & 1, errf);
                 tc_fence_after();
-                const uint32_t ah = x0 + q * 2 * MM_XH_BYTES, al = ah + MM_XH_BYTES;
-                const uint32_t d = tmem + mb * BN;
-#pragma unroll
-                for (uint32_t j = 0; j < 2; ++j) {   // the two 16-column steps of this K half
-                    const uint32_t kk = 2 * h + j;   // 16-column step within the K step
-                    const uint64_t dah = mm_desc(ah + 2 * j * (MM_BM * 16), MM_BM * 16, 128);
-                    const uint64_t dal = mm_desc(al + 2 * j * (MM_BM * 16), MM_BM * 16, 128);
-                    const uint64_t dbh = mm_desc(bh + 2 * kk * (BN * 16), BN * 16, 128);
-                    const uint64_t dbl = mm_desc(bl + 2 * kk * (BN * 16), BN * 16, 128);
-                    tc_mma(d, dah, dbh, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
-                    tc_mma(d, dah, dbl, IDESC, 1u);
-                    tc_mma(d, dal, dbh, IDESC, 1u);
-                }
+                // A = W rows (16-column step kk of the W slot), B = X tokens (this quarter slot)
+                const uint32_t xh_s = x0 + q * 2 * MM_XQ_BYTES, xl_s = xh_s + MM_XQ_BYTES;
+                const uint64_t dwh = mm_desc(wh + 2 * kk * (BN * 16), BN * 16, 128);
+                const uint64_t dwl = mm_desc(wl + 2 * kk * (BN * 16), BN * 16, 128);
+                const uint64_t dxh = mm_desc(xh_s, MM_TG * 16, 128);
+                const uint64_t dxl = mm_desc(xl_s, MM_TG * 16, 128);
+                const uint32_t d = tmem + tg * MM_TG;
+                tc_mma(d, dwh, dxh, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+                tc_mma(d, dwl, dxh, IDESC, 1u);
+                tc_mma(d, dwh, dxl, IDESC, 1u);
                 tc_commit(&xfree[q]);
             }
             tc_commit(&wfree[slot]);
@@ -423,35 +422,28 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
         tc_commit(&done);
     }
     // ---------------- epilogue ----------------
-    // per warp: TMEM lanes 32 (w % 4).. (tokens) of the M-blocks of half w / 4, in
-    // 32-column chunks; each chunk goes through a padded 32 x 33 staging tile in
-    // the W ring (free: every MMA has completed) so that a store instruction
-    // writes 32 consecutive floats of one token row (one 128-byte line)
+    // warp w reads TMEM lanes 32 (w % 4).. (weight rows n0 + 32 (w % 4) + lane) of
+    // token group w / 4 in 32-column chunks (tokens); for each token the warp's 32
+    // lanes store 32 consecutive floats of its y row (one 128-byte line)
     if (warp < 8) {
         mbar_wait(&done, 0, errf);
         tc_fence_after();
-        const uint32_t quarter = warp & 3, half = warp >> 2;
-        float* stg = reinterpret_cast<float*>(smem) + warp * (32 * 33);
-        for (uint32_t mb = half * 2; mb < half * 2 + 2 && mb < nmb; ++mb) {
-            const uint32_t row0 = (gmb0 + mb) * MM_BM + quarter * 32;
+        const uint32_t quarter = warp & 3, tg = warp >> 2;
+        const uint32_t n = n0 + quarter * 32 + lane;
+        if (tg < ntg) {
 #pragma unroll 1
-            for (uint32_t c0 = 0; c0 < (uint32_t)BN; c0 += 32) {
+            for (uint32_t c0 = 0; c0 < (uint32_t)MM_TG; c0 += 32) {
                 float v[32];
-                tc_ld32(tmem + ((quarter * 32) << 16) + mb * BN + c0, v);
+                tc_ld32(tmem + ((quarter * 32) << 16) + tg * MM_TG + c0, v);
+                const uint32_t tok0 = (gtg0 + tg) * MM_TG + c0;
 #pragma unroll
-                for (int c = 0; c < 32; ++c) stg[lane * 33 + c] = v[c];
-                __syncwarp();
-                const uint32_t n = n0 + c0 + lane;
-#pragma unroll 4
-                for (uint32_t r = 0; r < 32; ++r) {
-                    const uint32_t row = row0 + r;
-                    if (row < m && n < n_rows) {
-                        const size_t idx = (size_t)row * ldy + n;
-                        const float t = stg[r * 33 + lane];
-                        y[idx] = resid ? __fadd_rn(resid[idx], t) : t;
+                for (uint32_t j = 0; j < 32; ++j) {
+                    const uint32_t tok = tok0 + j;
+                    if (tok < m && n < n_rows) {
+                        const size_t idx = (size_t)tok * ldy + n;
+                        y[idx] = resid ? __fadd_rn(resid[idx], v[j]) : v[j];
                     }
                 }
-                __syncwarp();
             }
         }
     }
