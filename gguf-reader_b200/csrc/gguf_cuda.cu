@@ -616,6 +616,11 @@ int init_kernel_attrs() {
                            GGC_Q2_K, GGC_Q3_K_S, GGC_Q3_K_M, GGC_Q3_K_L, GGC_Q4_K, GGC_Q5_K, GGC_Q6_K, GGC_Q8_K};
         for (int dt : dts) dispatch_dtype<SetGemvSmem>(dt, &ok);
         if (cudaFuncSetAttribute(k_attn_av, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024) != cudaSuccess) ok = 0;
+        if (cudaFuncSetAttribute(k_attn_prefill<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pa_smem<64>()) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(k_attn_prefill<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pa_smem<128>()) !=
+                cudaSuccess)
+            ok = 0;
         for_each_attn_decode([](auto kernel, size_t smem) {
             if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) ok = 0;
         });
@@ -2034,18 +2039,33 @@ int ensure_prefill_buffers(ggc_model* m) {
 }
 
 // y[:, 0:rows] (ldy) (+)= rmsnorm / swiglu / plain(x) . W^T for a raw weight
-int mm_raw(ggc_model* m, const RawMat& w, const float* x, const float* x2, uint32_t n, uint32_t ldx, int pro, float* y,
-           uint32_t ldy, const float* resid) {
-    ggc_ctx* ctx = m->ctx;
-    uint8_t *xh, *xl;
+// X of a batch split into the product's bf16 hi / lo tiles once, for every
+// weight that multiplies the same input (q, k, v; up, gate)
+struct SplitX {
+    uint8_t* xh = nullptr;
+    uint8_t* xl = nullptr;
     uint32_t kpad = 0;
-    GGC_TRY(split_rows(ctx, x, x2, n, w.cols, ldx, pro, &xh, &xl, &kpad));
+    uint32_t cols = 0;
+};
+int mm_split_x(ggc_model* m, const float* x, const float* x2, uint32_t n, uint32_t cols, uint32_t ldx, int pro,
+               SplitX* sx) {
+    sx->cols = cols;
+    return split_rows(m->ctx, x, x2, n, cols, ldx, pro, &sx->xh, &sx->xl, &sx->kpad);
+}
+int mm_split_w(ggc_model* m, const RawMat& w, const SplitX& sx, uint32_t n, float* y, uint32_t ldy, const float* resid) {
+    if (w.cols != sx.cols) return set_error(GGC_ERR_INVALID_ARG, "prefill product: %u columns, split input %u", w.cols, sx.cols);
     cudaError_t err = cudaSuccess;
-    if (!dispatch_dtype<RunMM>(w.dtype, ctx, (const uint8_t*)w.p, w.rows, w.cols, (const uint8_t*)xh,
-                               (const uint8_t*)xl, n, kpad, y, ldy, resid, m->errf, &err))
+    if (!dispatch_dtype<RunMM>(w.dtype, m->ctx, (const uint8_t*)w.p, w.rows, w.cols, (const uint8_t*)sx.xh,
+                               (const uint8_t*)sx.xl, n, sx.kpad, y, ldy, resid, m->errf, &err))
         return set_dequant_error(w.dtype, 0, 0, "prefill dtype");
     GGC_CUDA_TRY(err);
     return GGC_OK;
+}
+int mm_raw(ggc_model* m, const RawMat& w, const float* x, const float* x2, uint32_t n, uint32_t ldx, int pro, float* y,
+           uint32_t ldy, const float* resid) {
+    SplitX sx;
+    GGC_TRY(mm_split_x(m, x, x2, n, w.cols, ldx, pro, &sx));
+    return mm_split_w(m, w, sx, n, y, ldy, resid);
 }
 
 // K/V of `count` prompt tokens at cache slots [cache_len, cache_len + count)
@@ -2105,9 +2125,11 @@ int prefill_batch(ggc_model* m, const uint32_t* tokens, const int64_t* positions
             float* yk = m->pf_y + m->qdim;
             float* yv = yk + m->kvdim;
             const uint32_t ldy = m->qdim + 2 * m->kvdim;
-            if (!last) GGC_TRY(mm_raw(m, L.rq, m->pf_h, L.attn_norm, n, d, MMP_RMSNORM, yq, ldy, nullptr));
-            GGC_TRY(mm_raw(m, L.rk, m->pf_h, L.attn_norm, n, d, MMP_RMSNORM, yk, ldy, nullptr));
-            GGC_TRY(mm_raw(m, L.rv, m->pf_h, L.attn_norm, n, d, MMP_RMSNORM, yv, ldy, nullptr));
+            SplitX sx;   // RMSNorm(h) split once for q, k, v
+            GGC_TRY(mm_split_x(m, m->pf_h, L.attn_norm, n, d, d, MMP_RMSNORM, &sx));
+            if (!last) GGC_TRY(mm_split_w(m, L.rq, sx, n, yq, ldy, nullptr));
+            GGC_TRY(mm_split_w(m, L.rk, sx, n, yk, ldy, nullptr));
+            GGC_TRY(mm_split_w(m, L.rv, sx, n, yv, ldy, nullptr));
             GGC_CUDA_TRY(launch(ctx, k_qkv_post, dim3(n), dim3(256), 0, (const float*)m->pf_y, ldy, m->qdim, m->kvdim, hd,
                                 (const float*)L.bq, (const float*)L.bk, (const float*)L.bv, (const int64_t*)m->pf_pos,
                                 (const float2*)m->rope, slot0, last ? (float*)nullptr : m->pf_q, kc, vc, hp.max_ctx,
@@ -2115,11 +2137,11 @@ int prefill_batch(ggc_model* m, const uint32_t* tokens, const int64_t* positions
             if (last) break;
             const dim3 ag(m->heads_l, cdiv<uint32_t>(n, PA_Q));
             if (hd == 64)
-                GGC_CUDA_TRY(launch(ctx, k_attn_prefill<64>, ag, dim3(PA_WARPS * 32), 0, (const float*)m->pf_q,
+                GGC_CUDA_TRY(launch(ctx, k_attn_prefill<64>, ag, dim3(PA_WARPS * 32), pa_smem<64>(), (const float*)m->pf_q,
                                     (const void*)kc, (const void*)vc, (const int64_t*)m->pf_pos, slot0, n, m->heads_l,
                                     m->kv_heads_l, hp.max_ctx, hp.kv_f16 ? 1 : 0, inv, m->pf_o));
             else
-                GGC_CUDA_TRY(launch(ctx, k_attn_prefill<128>, ag, dim3(PA_WARPS * 32), 0, (const float*)m->pf_q,
+                GGC_CUDA_TRY(launch(ctx, k_attn_prefill<128>, ag, dim3(PA_WARPS * 32), pa_smem<128>(), (const float*)m->pf_q,
                                     (const void*)kc, (const void*)vc, (const int64_t*)m->pf_pos, slot0, n, m->heads_l,
                                     m->kv_heads_l, hp.max_ctx, hp.kv_f16 ? 1 : 0, inv, m->pf_o));
             // attn_output + residual (rank 0 alone under tensor parallelism), all-reduce, NaN guard
@@ -2128,8 +2150,9 @@ int prefill_batch(ggc_model* m, const uint32_t* tokens, const int64_t* positions
             GGC_TRY(nan_scan(n, ERRF_NAN_ATTN, (int)l + 1));
             // ffn: up | gate side by side in pf_y, then down (+ residual)
             const uint32_t fl = L.f_l, ldu = 2 * fl;
-            GGC_TRY(mm_raw(m, L.rup, m->pf_h, L.ffn_norm, n, d, MMP_RMSNORM, m->pf_y, ldu, nullptr));
-            GGC_TRY(mm_raw(m, L.rgate, m->pf_h, L.ffn_norm, n, d, MMP_RMSNORM, m->pf_y + fl, ldu, nullptr));
+            GGC_TRY(mm_split_x(m, m->pf_h, L.ffn_norm, n, d, d, MMP_RMSNORM, &sx));   // once for up and gate
+            GGC_TRY(mm_split_w(m, L.rup, sx, n, m->pf_y, ldu, nullptr));
+            GGC_TRY(mm_split_w(m, L.rgate, sx, n, m->pf_y + fl, ldu, nullptr));
             GGC_TRY(mm_raw(m, L.rdown, m->pf_y + fl, m->pf_y, n, ldu, MMP_SWIGLU, m->pf_h, d, lead ? m->pf_h : nullptr));
             GGC_TRY(allreduce_h(n));
             GGC_TRY(nan_scan(n, ERRF_NAN_FFN, (int)l + 1));

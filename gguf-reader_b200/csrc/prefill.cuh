@@ -549,36 +549,50 @@ __global__ void __launch_bounds__(256) k_qkv_post(const float* __restrict__ y, u
 }
 
 // Causal attention of the batch (llama.rs:499-545) on the CUDA cores: CTA = one
-// q head x PA_Q tokens (4 warps x 4 tokens), K/V tiles of 32 cache rows in
-// shared memory (K rows padded by one float: lane j reads row j without bank
-// conflicts).  Token t (cache slot base + t, position pos[t]) sees the rows
-// s < min(pos[t] + 1, base + t + 1), as the decode kernels do; the softmax runs
-// online (running max / sum, o rescaled per tile) and o is divided by the sum
-// at the end.  Output o[t][head * hd + i].
-constexpr int PA_WARPS = 4, PA_QW = 4, PA_Q = PA_WARPS * PA_QW, PA_KT = 32;
-
+// q head x PA_Q tokens (8 warps x 8 tokens), K/V tiles of PA_KT cache rows in
+// shared memory.  Token t (cache slot base + t, position pos[t]) sees the rows
+// s < min(pos[t] + 1, base + t + 1), as the decode kernels do.
+//   scores: lane l holds keys l and l + 32 of the tile for the warp's 8 tokens;
+//     each dot product runs over the head dimension in order (fmaf chain), from
+//     float4 loads of K rows (padded by 4 floats: conflict-free) and broadcast q;
+//   softmax: online per token (running max / sum, o rescaled per tile), the
+//     tile's probabilities through a per-warp shared row;
+//   o: lane l owns dimensions [l NI, l NI + NI) of the 8 tokens and adds
+//     p . V over the tile's keys in order; o is divided by the sum at the end.
+// Token tiles run heaviest (latest) first.  Output o[t][head * hd + i].
+constexpr int PA_WARPS = 8, PA_QW = 8, PA_Q = PA_WARPS * PA_QW, PA_KT = 64;
 template <int HD>
-__global__ void __launch_bounds__(PA_WARPS * 32) k_attn_prefill(const float* __restrict__ q, const void* kc,
+constexpr size_t pa_smem() {
+    return sizeof(float) * ((size_t)PA_Q * HD + (size_t)PA_KT * (HD + 4) + (size_t)PA_KT * HD + (size_t)PA_WARPS * PA_QW * PA_KT);
+}
+template <int HD>
+__global__ void __launch_bounds__(PA_WARPS * 32, 1) k_attn_prefill(const float* __restrict__ q, const void* kc,
                                                                  const void* vc, const int64_t* __restrict__ pos,
                                                                  uint32_t base, uint32_t m, uint32_t n_heads,
                                                                  uint32_t kvh, uint32_t kv_ctx, int kv_f16, float inv,
                                                                  float* __restrict__ o) {
-    constexpr int NI = HD / 32;
-    __shared__ float sk[PA_KT][HD + 1];
-    __shared__ float sv[PA_KT][HD];
-    __shared__ float sq[PA_Q][HD];
+    constexpr int NI = HD / 32, KP = HD + 4;
+    static_assert(NI == 2 || NI == 4, "head dim 64 or 128");
+    extern __shared__ __align__(16) float pa_sm[];
+    float* sq = pa_sm;                       // [PA_Q][HD]
+    float* sk = sq + PA_Q * HD;              // [PA_KT][KP]
+    float* sv = sk + PA_KT * KP;             // [PA_KT][HD]
+    float* sp = sv + PA_KT * HD;             // [warp][PA_QW][PA_KT]
     pdl_trigger();
     pdl_wait();
-    const uint32_t head = blockIdx.x, t0 = blockIdx.y * PA_Q, kvhead = head / (n_heads / kvh);
+    const uint32_t head = blockIdx.x, t0 = (gridDim.y - 1 - blockIdx.y) * PA_Q, kvhead = head / (n_heads / kvh);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t qdim = n_heads * HD;
-    for (uint32_t i = tid; i < PA_Q * HD; i += blockDim.x) {
-        const uint32_t r = i / HD, t = t0 + r;
-        sq[r][i % HD] = t < m ? q[(size_t)t * qdim + head * HD + i % HD] : 0.f;
+    for (uint32_t i = tid; i < PA_Q * HD / 4; i += blockDim.x) {
+        const uint32_t r = i / (HD / 4), c = (i % (HD / 4)) * 4, t = t0 + r;
+        const float4 v = t < m ? *reinterpret_cast<const float4*>(q + (size_t)t * qdim + head * HD + c)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(sq + r * HD + c) = v;
     }
     // visible rows per token of this warp, and of the whole CTA
     uint32_t vis[PA_QW];
-    uint32_t vmax = 0;
+    uint32_t vmax = 0, vwarp = 0;
+#pragma unroll
     for (int k = 0; k < PA_QW; ++k) {
         const uint32_t t = t0 + warp * PA_QW + k;
         uint32_t v = 0;
@@ -588,6 +602,7 @@ __global__ void __launch_bounds__(PA_WARPS * 32) k_attn_prefill(const float* __r
             v = (p + 1 < (int64_t)seq) ? (uint32_t)(p + 1) : seq;
         }
         vis[k] = v;
+        vwarp = v > vwarp ? v : vwarp;
     }
     for (uint32_t r = 0; r < PA_Q; ++r) {
         const uint32_t t = t0 + r;
@@ -606,56 +621,116 @@ __global__ void __launch_bounds__(PA_WARPS * 32) k_attn_prefill(const float* __r
         for (int c = 0; c < NI; ++c) acc[k][c] = 0.f;
     }
     const uint64_t hb = (uint64_t)kvhead * kv_ctx * HD;
+    const float* sqw = sq + warp * PA_QW * HD;
+    float* spw = sp + warp * PA_QW * PA_KT;
     for (uint32_t s0 = 0; s0 < vmax; s0 += PA_KT) {
         __syncthreads();   // previous tile consumed (and sq written, first time)
-        for (uint32_t i = tid; i < PA_KT * HD; i += blockDim.x) {
-            const uint32_t r = i / HD, c = i % HD, s = s0 + r;
-            float kv = 0.f, vv = 0.f;
+        for (uint32_t i = tid; i < PA_KT * HD / 4; i += blockDim.x) {
+            const uint32_t r = i / (HD / 4), c = (i % (HD / 4)) * 4, s = s0 + r;
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
             if (s < vmax) {
                 const uint64_t idx = hb + (uint64_t)s * HD + c;
-                kv = kv_f16 ? __half2float(reinterpret_cast<const __half*>(kc)[idx]) : reinterpret_cast<const float*>(kc)[idx];
-                vv = kv_f16 ? __half2float(reinterpret_cast<const __half*>(vc)[idx]) : reinterpret_cast<const float*>(vc)[idx];
+                if (kv_f16) {
+                    const __half* kh = reinterpret_cast<const __half*>(kc) + idx;
+                    const __half* vh = reinterpret_cast<const __half*>(vc) + idx;
+                    kv = make_float4(__half2float(kh[0]), __half2float(kh[1]), __half2float(kh[2]), __half2float(kh[3]));
+                    vv = make_float4(__half2float(vh[0]), __half2float(vh[1]), __half2float(vh[2]), __half2float(vh[3]));
+                } else {
+                    kv = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(kc) + idx);
+                    vv = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(vc) + idx);
+                }
             }
-            sk[r][c] = kv;
-            sv[r][c] = vv;
+            *reinterpret_cast<float4*>(sk + r * KP + c) = kv;
+            *reinterpret_cast<float4*>(sv + r * HD + c) = vv;
         }
         __syncthreads();
-        const uint32_t s = s0 + lane;   // this lane's key
+        if (s0 >= vwarp) continue;   // no key of this tile is visible to the warp's tokens
+        // scores of keys s0 + lane and s0 + lane + 32
+        float sc[PA_QW][2];
+#pragma unroll
+        for (int k = 0; k < PA_QW; ++k) sc[k][0] = sc[k][1] = 0.f;
+        const float* ka = sk + lane * KP;
+        const float* kb = sk + (lane + 32) * KP;
+#pragma unroll 2
+        for (int d = 0; d < HD; d += 4) {
+            const float4 a = *reinterpret_cast<const float4*>(ka + d);
+            const float4 b = *reinterpret_cast<const float4*>(kb + d);
+#pragma unroll
+            for (int k = 0; k < PA_QW; ++k) {
+                const float4 qv = *reinterpret_cast<const float4*>(sqw + k * HD + d);
+                sc[k][0] = fmaf(qv.x, a.x, sc[k][0]);
+                sc[k][0] = fmaf(qv.y, a.y, sc[k][0]);
+                sc[k][0] = fmaf(qv.z, a.z, sc[k][0]);
+                sc[k][0] = fmaf(qv.w, a.w, sc[k][0]);
+                sc[k][1] = fmaf(qv.x, b.x, sc[k][1]);
+                sc[k][1] = fmaf(qv.y, b.y, sc[k][1]);
+                sc[k][1] = fmaf(qv.z, b.z, sc[k][1]);
+                sc[k][1] = fmaf(qv.w, b.w, sc[k][1]);
+            }
+        }
+        // online softmax per token; probabilities into this warp's shared rows
 #pragma unroll
         for (int k = 0; k < PA_QW; ++k) {
-            if (s0 >= vis[k]) continue;   // warp-uniform
-            const float* qr = sq[warp * PA_QW + k];
-            float dot = 0.f;
-#pragma unroll 8
-            for (int i = 0; i < HD; ++i) dot = fmaf(qr[i], sk[lane][i], dot);
-            const float sc = s < vis[k] ? __fmul_rn(dot, inv) : -INFINITY;
-            float tmax = sc;
+            const uint32_t sa = s0 + lane, sb = s0 + lane + 32;
+            if (s0 >= vis[k]) {   // warp-uniform: no visible key in this tile
+                spw[k * PA_KT + lane] = 0.f;
+                spw[k * PA_KT + lane + 32] = 0.f;
+                continue;
+            }
+            const float xa = sa < vis[k] ? __fmul_rn(sc[k][0], inv) : -INFINITY;
+            const float xb = sb < vis[k] ? __fmul_rn(sc[k][1], inv) : -INFINITY;
+            float tmax = fmaxf(xa, xb);
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
             const float mnew = fmaxf(mx[k], tmax);
-            const float scale = expf(mx[k] - mnew);   // 0 on the first tile (mx = -inf)
-            const float pj = s < vis[k] ? expf(sc - mnew) : 0.f;
-            float ps = pj;
+            const float scale = expf(mx[k] - mnew);   // 0 on the first visible tile (mx = -inf)
+            const float pa = sa < vis[k] ? expf(xa - mnew) : 0.f;
+            const float pb = sb < vis[k] ? expf(xb - mnew) : 0.f;
+            float ps = pa + pb;
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
             sum[k] = sum[k] * scale + ps;
             mx[k] = mnew;
 #pragma unroll
             for (int c = 0; c < NI; ++c) acc[k][c] *= scale;
-            for (int j = 0; j < PA_KT; ++j) {
-                const float pb = __shfl_sync(0xffffffffu, pj, j);
+            spw[k * PA_KT + lane] = pa;
+            spw[k * PA_KT + lane + 32] = pb;
+        }
+        __syncwarp();
+        // o += p . V over the tile's keys in order
+        const uint32_t kend = min((uint32_t)PA_KT, vmax - s0);
+        for (uint32_t j = 0; j < kend; j += 4) {
+            float4 p4[PA_QW];
 #pragma unroll
-                for (int c = 0; c < NI; ++c) acc[k][c] = fmaf(pb, sv[j][lane + 32 * c], acc[k][c]);
+            for (int k = 0; k < PA_QW; ++k) p4[k] = *reinterpret_cast<const float4*>(spw + k * PA_KT + j);
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                float vr[NI];
+                if constexpr (NI == 4) {
+                    const float4 t4 = *reinterpret_cast<const float4*>(sv + (j + jj) * HD + lane * 4);
+                    vr[0] = t4.x; vr[1] = t4.y; vr[2] = t4.z; vr[3] = t4.w;
+                } else {
+                    const float2 t2 = *reinterpret_cast<const float2*>(sv + (j + jj) * HD + lane * 2);
+                    vr[0] = t2.x; vr[1] = t2.y;
+                }
+#pragma unroll
+                for (int k = 0; k < PA_QW; ++k) {
+                    const float pk = jj == 0 ? p4[k].x : jj == 1 ? p4[k].y : jj == 2 ? p4[k].z : p4[k].w;
+#pragma unroll
+                    for (int c = 0; c < NI; ++c) acc[k][c] = fmaf(pk, vr[c], acc[k][c]);
+                }
             }
         }
+        __syncwarp();
     }
 #pragma unroll
     for (int k = 0; k < PA_QW; ++k) {
         const uint32_t t = t0 + warp * PA_QW + k;
         if (t >= m) continue;
         const float rs = vis[k] ? 1.0f / sum[k] : 0.f;
+        float* dst = o + (size_t)t * qdim + head * HD + lane * NI;
 #pragma unroll
-        for (int c = 0; c < NI; ++c) o[(size_t)t * qdim + head * HD + lane + 32 * c] = acc[k][c] * rs;
+        for (int c = 0; c < NI; ++c) dst[c] = acc[k][c] * rs;
     }
 }
 
