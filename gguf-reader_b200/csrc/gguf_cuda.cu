@@ -879,9 +879,13 @@ struct RunMM {
         *err = launch(ctx, k_mm_tc<DT, MM_BN, STAGE>, dim3(gx, gy, ks), dim3(MM_THREADS), smem, w, n, k, xh, xl, m,
                       kpad, kb_per, part, n, (const float*)nullptr, errf, map);
         if (*err != cudaSuccess) return;
-        const uint64_t total = (uint64_t)m * n;
+        const bool vec4 = n % 4 == 0 && ldy % 4 == 0 && (uintptr_t)y % 16 == 0 && (uintptr_t)resid % 16 == 0;
+        const uint64_t total = (uint64_t)m * (vec4 ? n / 4 : n);
         const unsigned grid = (unsigned)std::min<uint64_t>(cdiv<uint64_t>(total, 256), (uint64_t)ctx->num_sms * 8);
-        *err = launch(ctx, k_mm_reduce, dim3(grid), dim3(256), 0, (const float*)part, ks, m, n, y, ldy, resid);
+        if (vec4)
+            *err = launch(ctx, k_mm_reduce4, dim3(grid), dim3(256), 0, (const float4*)part, ks, m, n / 4, y, ldy, resid);
+        else
+            *err = launch(ctx, k_mm_reduce, dim3(grid), dim3(256), 0, (const float*)part, ks, m, n, y, ldy, resid);
     }
     static void run(ggc_ctx* ctx, const uint8_t* w, uint32_t n, uint32_t k, const uint8_t* xh, const uint8_t* xl,
                     uint32_t m, uint32_t kpad, float* y, uint32_t ldy, const float* resid, int* errf,
@@ -918,7 +922,8 @@ int split_rows(ggc_ctx* ctx, const float* x, const float* x2, uint32_t m, uint32
     GGC_TRY(ensure_stage(ctx, 4, bytes));
     *xh = (uint8_t*)ctx->stage[3];
     *xl = (uint8_t*)ctx->stage[4];
-    GGC_CUDA_TRY(launch(ctx, k_x_split, dim3(mpad), dim3(SPLIT_THREADS), 0, x, x2, m, k, ldx, *kpad, pro, *xh, *xl));
+    const int vec = ((uintptr_t)x % 16 == 0) && (!x2 || (uintptr_t)x2 % 16 == 0) && ldx % 4 == 0;
+    GGC_CUDA_TRY(launch(ctx, k_x_split, dim3(mpad), dim3(SPLIT_THREADS), 0, x, x2, m, k, ldx, *kpad, pro, vec, *xh, *xl));
     return GGC_OK;
 }
 

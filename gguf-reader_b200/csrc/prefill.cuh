@@ -188,7 +188,7 @@ constexpr int SPLIT_THREADS = 256;
 
 __global__ void __launch_bounds__(SPLIT_THREADS) k_x_split(const float* __restrict__ x, const float* __restrict__ x2,
                                                            uint32_t m, uint32_t k, uint32_t ldx, uint32_t kpad, int pro,
-                                                           uint8_t* __restrict__ xh, uint8_t* __restrict__ xl) {
+                                                           int vec, uint8_t* __restrict__ xh, uint8_t* __restrict__ xl) {
     pdl_trigger();
     pdl_wait();
     const uint32_t row = blockIdx.x, nk = kpad / MM_BK;
@@ -212,18 +212,35 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_x_split(const float* __restri
         scale = s_scale;
     }
     const size_t tile0 = (size_t)(row / MM_TG) * nk * MM_X_BYTES + (row % MM_TG) * 16;
+    // whole 8-element chunks by float4 loads when the rows allow it (vec: x, x2
+    // 16-byte aligned, ldx a multiple of 4); the same arithmetic per element
+    const float* x2r = pro == MMP_SWIGLU ? x2 + (size_t)row * ldx : x2;
     for (uint32_t c = threadIdx.x; c < kpad / 8; c += SPLIT_THREADS) {
         float v[8];
+        if (vec && row < m && c * 8 + 8 <= k) {
+            const float4 a0 = *reinterpret_cast<const float4*>(xr + c * 8);
+            const float4 a1 = *reinterpret_cast<const float4*>(xr + c * 8 + 4);
+            v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w; v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
+            if (pro != MMP_PLAIN) {
+                const float4 b0 = *reinterpret_cast<const float4*>(x2r + c * 8);
+                const float4 b1 = *reinterpret_cast<const float4*>(x2r + c * 8 + 4);
+                const float w[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const uint32_t e = c * 8 + j;
-            float t = 0.f;
-            if (row < m && e < k) {
-                t = xr[e];
-                if (pro == MMP_RMSNORM) t = __fmul_rn(__fmul_rn(t, scale), x2[e]);
-                else if (pro == MMP_SWIGLU) t = ffn_silu_mul(t, x2[(size_t)row * ldx + e]);
+                for (int j = 0; j < 8; ++j)
+                    v[j] = pro == MMP_RMSNORM ? __fmul_rn(__fmul_rn(v[j], scale), w[j]) : ffn_silu_mul(v[j], w[j]);
             }
-            v[j] = t;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t e = c * 8 + j;
+                float t = 0.f;
+                if (row < m && e < k) {
+                    t = xr[e];
+                    if (pro == MMP_RMSNORM) t = __fmul_rn(__fmul_rn(t, scale), x2[e]);
+                    else if (pro == MMP_SWIGLU) t = ffn_silu_mul(t, x2[(size_t)row * ldx + e]);
+                }
+                v[j] = t;
+            }
         }
         uint4 h, l;
         split8(v, h, l);
@@ -469,6 +486,34 @@ __global__ void __launch_bounds__(256) k_mm_reduce(const float* __restrict__ par
         for (uint32_t s = 1; s < ks; ++s) v = __fadd_rn(v, part[s * slice + i]);
         const size_t idx = (size_t)r * ldy + c;
         y[idx] = resid ? __fadd_rn(resid[idx], v) : v;
+    }
+}
+
+// k_mm_reduce over float4 columns (n, ldy multiples of 4, every pointer 16-byte
+// aligned): the same additions in the same order, four columns per thread, the
+// ks loads of a thread independent of one another
+__global__ void __launch_bounds__(256) k_mm_reduce4(const float4* __restrict__ part, uint32_t ks, uint32_t m,
+                                                    uint32_t n4, float* y, uint32_t ldy, const float* resid) {
+    pdl_trigger();
+    pdl_wait();
+    const uint64_t total = (uint64_t)m * n4, slice = total;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t r = i / n4, c = (i - r * n4) * 4;
+        float4 v = __ldcs(part + i);
+#pragma unroll 4
+        for (uint32_t s = 1; s < ks; ++s) {
+            const float4 t = __ldcs(part + s * slice + i);
+            v.x = __fadd_rn(v.x, t.x);
+            v.y = __fadd_rn(v.y, t.y);
+            v.z = __fadd_rn(v.z, t.z);
+            v.w = __fadd_rn(v.w, t.w);
+        }
+        const size_t idx = (size_t)r * ldy + c;
+        if (resid) {
+            const float4 q = *reinterpret_cast<const float4*>(resid + idx);
+            v = make_float4(__fadd_rn(q.x, v.x), __fadd_rn(q.y, v.y), __fadd_rn(q.z, v.z), __fadd_rn(q.w, v.w));
+        }
+        *reinterpret_cast<float4*>(y + idx) = v;
     }
 }
 
