@@ -305,13 +305,15 @@ __device__ __forceinline__ float span_xval(const SpanX a, uint32_t e, float scal
     return x;
 }
 
+// Returns (thread 0) whether the RMSNorm sum of squares is NaN; the caller reports it.
 template <int DT>
-__device__ void span_x_prologue(const SpanX a, uint32_t nct, uint32_t* xl, float* xfs, double* red, float* s_scale) {
+__device__ bool span_x_prologue(const SpanX a, uint32_t nct, uint32_t* xl, float* xfs, double* red, float* s_scale) {
     using F = SpanFmt<DT>;
     constexpr uint32_t CT = GS_WARPS * 32;
     auto cbar = [] { asm volatile("bar.sync 1, %0;" ::"r"(CT) : "memory"); };
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     float scale = 0.f;
+    bool x_nan = false;
     if (a.pro == PRO_RMSNORM) {
         double ss = 0.0;
         if ((a.xcols & 3) == 0) {
@@ -332,7 +334,7 @@ __device__ void span_x_prologue(const SpanX a, uint32_t nct, uint32_t* xl, float
             double t = 0.0;
             for (int w = 0; w < GS_WARPS; ++w) t += red[w];
             *s_scale = (float)sqrt(1.0 / (t / (double)a.xcols + (double)1e-6f));   // ops.rs:262-274
-            if (a.pro_err_val && isnan(t)) atomicCAS(&a.errf[a.pro_err_slot], 0, a.pro_err_val);   // NaN in x <=> NaN sum
+            x_nan = isnan(t);   // NaN in x <=> NaN sum
         }
         cbar();
         scale = *s_scale;
@@ -415,6 +417,7 @@ __device__ void span_x_prologue(const SpanX a, uint32_t nct, uint32_t* xl, float
         }
     }
     cbar();
+    return x_nan;
 }
 
 // ---- the kernel ------------------------------------------------------------
@@ -507,14 +510,19 @@ __global__ void __launch_bounds__(GS_THREADS, 1) k_gemv_span(const GemvArgs a, c
 
     // ---------------- consumer warps ----------------
     pdl_wait();
-    if (skip()) {   // drain the copies issued before the flag was seen
+    // the skip flags' loads are issued here and used after the x prologue, so
+    // their latency overlaps it (the prologue only reads x, and its NaN report
+    // waits for the flags)
+    const bool skipping = skip();
+    constexpr uint32_t CT = GS_WARPS * 32;
+    auto cbar = [] { asm volatile("bar.sync 1, %0;" ::"r"(CT) : "memory"); };
+    const bool x_nan = span_x_prologue<DT>(span_x_of(a), nct, xl, xfs, red, &s_scale);
+    if (skipping) {   // drain the copies issued before the flag was seen
         const uint32_t n = ntiles < cfg.stages ? ntiles : cfg.stages;
         for (uint32_t i = 0; i < n; ++i) mbar_wait(&full[i], 0, a.errf);
         return;
     }
-    constexpr uint32_t CT = GS_WARPS * 32;
-    auto cbar = [] { asm volatile("bar.sync 1, %0;" ::"r"(CT) : "memory"); };
-    span_x_prologue<DT>(span_x_of(a), nct, xl, xfs, red, &s_scale);
+    if (tid == 0 && x_nan && a.pro_err_val) atomicCAS(&a.errf[a.pro_err_slot], 0, a.pro_err_val);
     for (uint32_t i = tid; i < cfg.part_rows; i += CT) part[i] = 0.f;
     cbar();
 
