@@ -95,6 +95,26 @@ def test_prefill_equals_token_by_token(ggc, ctx, monkeypatch):
     assert a.generate_greedy([5], 16, start_pos=80) == b.generate_greedy([5], 16, start_pos=80)
 
 
+def test_prefill_f16_cache_equals_token_by_token(ggc, ctx, monkeypatch):
+    """The batched attention reading an f16 cache (a prompt on top of cached rows)
+    against the token-by-token path over its own f16 cache.  The two paths round
+    K/V to f16 from slightly different f32 products (tensor-core vs integer GEMV),
+    so a few cache entries differ by one f16 ulp (~1e-3 relative): 5e-3 bound."""
+    hp, ts = synth.make_model(MINI, seed=4)
+    a = ggc.LlamaModel(hp, ts, max_ctx=256, kv_f16=True, ctx=ctx)
+    monkeypatch.setenv("GGC_PREFILL", "0")
+    b = ggc.LlamaModel(hp, ts, max_ctx=256, kv_f16=True, ctx=ctx)
+    rng = np.random.default_rng(11)
+    head = rng.integers(0, hp["vocab_size"], size=5).astype(np.uint32)
+    body = rng.integers(0, hp["vocab_size"], size=90).astype(np.uint32)
+    for model in (a, b):
+        model.forward(head, np.arange(5, dtype=np.int64))
+    la = a.forward(body, np.arange(5, 95, dtype=np.int64))
+    lb = b.forward(body, np.arange(5, 95, dtype=np.int64))
+    assert rel_l2(la, lb) <= 5e-3, rel_l2(la, lb)
+    assert a.cache_len() == b.cache_len() == 95
+
+
 def test_prefill_errors(ggc, ctx):
     hp, ts = synth.make_model(dict(MINI, weights=0, qkv_bias=False), seed=4)
     m = ggc.LlamaModel(hp, ts, max_ctx=256, ctx=ctx)
