@@ -708,7 +708,7 @@ extern "C" int ggc_tensor_upload(ggc_ctx* ctx, const void* raw, uint64_t bytes, 
         GGC_TRY(upload_mat(ctx, raw, bytes, dtype, rows, cols, nullptr, t->mat));
         t->repacked = true;
     } else {
-        GGC_CUDA_TRY(cudaMalloc(&t->raw, need));
+        GGC_CUDA_TRY(cudaMalloc(&t->raw, need + 16));   // 16 bytes of slack: the product's aligned row windows
         GGC_CUDA_TRY(cudaMemcpy(t->raw, raw, need, cudaMemcpyHostToDevice));
         t->raw_bytes = need;
     }
@@ -846,29 +846,30 @@ void mm_split(uint32_t nk, uint32_t step, uint32_t tiles, uint32_t sms, uint32_t
 // map can be made, else they read the blocks from global memory as the rest do.
 template <int DT>
 struct RunMM {
-    template <bool STAGE>
+    template <int SM>
     static cudaError_t set_attr() {
         static std::once_flag once;
         static cudaError_t attr = cudaSuccess;
         std::call_once(once, [] {
-            attr = cudaFuncSetAttribute(k_mm_tc<DT, MM_BN, STAGE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)mm_smem(MM_BN, STAGE, block_bytes_of(DT)));
+            attr = cudaFuncSetAttribute(k_mm_tc<DT, MM_BN, SM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)mm_smem(MM_BN, SM, block_bytes_of(DT)));
         });
         return attr;
     }
-    template <bool STAGE>
+    template <int SM>
     static void go(ggc_ctx* ctx, const uint8_t* w, uint32_t n, uint32_t k, const uint8_t* xh, const uint8_t* xl,
                    uint32_t m, uint32_t kpad, float* y, uint32_t ldy, const float* resid, int* errf,
                    const CUtensorMap& map, cudaError_t* err) {
-        *err = set_attr<STAGE>();
+        constexpr bool STAGE = SM != MMS_NONE;
+        *err = set_attr<SM>();
         if (*err != cudaSuccess) return;
-        const uint32_t smem = mm_smem(MM_BN, STAGE, block_bytes_of(DT));
+        const uint32_t smem = mm_smem(MM_BN, SM, block_bytes_of(DT));
         const uint32_t gx = cdiv<uint32_t>(n, MM_BN), gy = cdiv<uint32_t>(cdiv<uint32_t>(m, MM_TG), MM_NTG);
         const uint32_t nk = kpad / MM_BK, step = STAGE ? (uint32_t)(block_size_of(DT) / MM_BK) : 1u;
         uint32_t ks = 1, kb_per = nk;
         mm_split(nk, step, gx * gy, (uint32_t)ctx->num_sms, m, n, &ks, &kb_per);
         if (ks == 1) {
-            *err = launch(ctx, k_mm_tc<DT, MM_BN, STAGE>, dim3(gx, gy, 1), dim3(MM_THREADS), smem, w, n, k, xh, xl,
+            *err = launch(ctx, k_mm_tc<DT, MM_BN, SM>, dim3(gx, gy, 1), dim3(MM_THREADS), smem, w, n, k, xh, xl,
                           m, kpad, kb_per, y, ldy, resid, errf, map);
             return;
         }
@@ -876,7 +877,7 @@ struct RunMM {
         int st = ensure_stage(ctx, 5, pbytes);
         if (st != GGC_OK) { *err = cudaErrorMemoryAllocation; return; }
         float* part = (float*)ctx->stage[5];
-        *err = launch(ctx, k_mm_tc<DT, MM_BN, STAGE>, dim3(gx, gy, ks), dim3(MM_THREADS), smem, w, n, k, xh, xl, m,
+        *err = launch(ctx, k_mm_tc<DT, MM_BN, SM>, dim3(gx, gy, ks), dim3(MM_THREADS), smem, w, n, k, xh, xl, m,
                       kpad, kb_per, part, n, (const float*)nullptr, errf, map);
         if (*err != cudaSuccess) return;
         const bool vec4 = n % 4 == 0 && ldy % 4 == 0 && (uintptr_t)y % 16 == 0 && (uintptr_t)resid % 16 == 0;
@@ -896,9 +897,13 @@ struct RunMM {
             const uint64_t row_bytes = (uint64_t)(k / block_size_of(DT)) * block_bytes_of(DT);
             if (k % block_size_of(DT) == 0 && kpad == k &&
                 raw_row_map(&map, w, n, row_bytes, (uint32_t)block_bytes_of(DT), MM_BN))
-                return go<true>(ctx, w, n, k, xh, xl, m, kpad, y, ldy, resid, errf, map, err);
+                return go<MMS_TMA>(ctx, w, n, k, xh, xl, m, kpad, y, ldy, resid, errf, map, err);
         }
-        go<false>(ctx, w, n, k, xh, xl, m, kpad, y, ldy, resid, errf, map, err);
+        if constexpr (DT == GGC_Q6_K) {   // raw weights carry 16 bytes of slack past their end
+            if (k % block_size_of(DT) == 0 && kpad == k && ((uintptr_t)w & 15) == 0)
+                return go<MMS_ROWS>(ctx, w, n, k, xh, xl, m, kpad, y, ldy, resid, errf, map, err);
+        }
+        go<MMS_NONE>(ctx, w, n, k, xh, xl, m, kpad, y, ldy, resid, errf, map, err);
     }
 };
 

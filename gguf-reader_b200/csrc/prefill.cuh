@@ -43,11 +43,18 @@ constexpr uint32_t mm_w_bytes(int bn) { return (uint32_t)bn * MM_BK * 2; }
 // formats whose raw blocks the product stages in shared memory by TMA (256-element
 // blocks of a 16-byte multiple: every block of a raw row starts 16-byte aligned)
 constexpr bool mm_staged(int dt) { return dt == GGC_Q4_K || dt == GGC_Q5_K; }
+// raw staging modes of the product: none; one 2-D TMA copy per block step (Q4_K /
+// Q5_K); one bulk copy per row of the 16-byte-aligned window around the row's
+// block (Q6_K: 210-byte blocks start at any even offset)
+enum MmStage : int { MMS_NONE = 0, MMS_TMA = 1, MMS_ROWS = 2 };
 constexpr int mm_xs(bool staged) { return staged ? 6 : MM_XS; }   // X ring slots (smem for the raw ring)
+// bytes a staged row takes in the raw ring: the block, or its aligned window
+constexpr uint32_t mm_raw_pitch(int sm, int bb) { return sm == MMS_ROWS ? ((uint32_t)bb + 14u + 15u) / 16u * 16u : (uint32_t)bb; }
 // dynamic shared memory: W ring [2][hi, lo], X ring [XS][hi, lo] quarter tiles, staged: raw ring
-// [2][bn rows][bb] at the next 128-byte boundary (the TMA destination alignment)
-constexpr uint32_t mm_smem(int bn, bool staged = false, int bb = 0) {
-    return 2 * 2 * mm_w_bytes(bn) + mm_xs(staged) * 2 * MM_XQ_BYTES + (staged ? 2u * bn * (uint32_t)bb + 128u : 0u);
+// [2][bn rows][raw pitch] at the next 128-byte boundary (the TMA destination alignment)
+constexpr uint32_t mm_smem(int bn, int sm = MMS_NONE, int bb = 0) {
+    return 2 * 2 * mm_w_bytes(bn) + mm_xs(sm != MMS_NONE) * 2 * MM_XQ_BYTES +
+           (sm != MMS_NONE ? 2u * bn * mm_raw_pitch(sm, bb) + 128u : 0u);
 }
 // instruction descriptor: D f32, A/B bf16, both K-major, M = bn weight rows, N = MM_TG tokens
 constexpr uint32_t mm_idesc(int bn) {
@@ -266,29 +273,35 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_x_split(const float* __restri
 //     half w / 4) and write Y (+ the residual).
 // Every wait is bounded (ERRF_TIMEOUT); no thread leaves early, warp 8 frees TMEM.
 //
-// STAGE (the mm_staged formats Q4_K, Q5_K): the copy warp also loads the CTA's raw
-// blocks of each 256-element K range (BN rows x one block, rows past the matrix
-// zero-filled) with one 2-D TMA copy (tensor map over the raw rows as bytes,
-// no multicast) into a 2-slot ring (rfull / rfree), so the dequantising warps
-// read shared memory only; the split-K ranges are whole blocks.
-template <int DT, int BN, bool STAGE>
+// SM = MMS_TMA (Q4_K, Q5_K): the copy warp also loads the CTA's raw blocks of
+// each 256-element K range (BN rows x one block, rows past the matrix
+// zero-filled) with one 2-D TMA copy (tensor map over the raw rows as bytes, no
+// multicast) into a 2-slot ring (rfull / rfree), so the dequantising warps read
+// shared memory only; SM = MMS_ROWS (Q6_K): the same ring, filled with one bulk
+// copy per row of the 16-byte-aligned window around the row's block (rows past
+// the matrix not loaded, their values zero).  Split-K ranges are whole blocks.
+template <int DT, int BN, int SM>
 __global__ void __launch_bounds__(MM_THREADS, 1)
     k_mm_tc(const uint8_t* __restrict__ w, uint32_t n_rows, uint32_t k_cols, const uint8_t* __restrict__ xh,
             const uint8_t* __restrict__ xl, uint32_t m, uint32_t kpad, uint32_t kb_per, float* y, uint32_t ldy,
             const float* resid, int* errf, const __grid_constant__ CUtensorMap wmap) {
     constexpr int BS = block_size_of(DT), BB = block_bytes_of(DT);
-    static_assert(!STAGE || (mm_staged(DT) && BS == 4 * MM_BK && BB % 16 == 0 && (BN * BB) % 128 == 0),
-                  "staged: 256-element blocks of a 16-byte multiple");
+    constexpr bool STAGE = SM != MMS_NONE;
+    static_assert(SM != MMS_TMA || (mm_staged(DT) && BS == 4 * MM_BK && BB % 16 == 0 && (BN * BB) % 128 == 0),
+                  "TMA staging: 256-element blocks of a 16-byte multiple");
+    static_assert(SM != MMS_ROWS || (DT == GGC_Q6_K && BS == 4 * MM_BK), "row-window staging: Q6_K");
     constexpr int XS = mm_xs(STAGE);
     static_assert(BN == 128, "UMMA M = 128 weight rows (all TMEM lanes)");
-    constexpr uint32_t WB = mm_w_bytes(BN), TCOLS = MM_NTG * MM_TG, IDESC = mm_idesc(BN), RB = (uint32_t)BN * BB;
+    constexpr uint32_t RP = mm_raw_pitch(SM, BB);   // bytes of a staged row
+    constexpr uint32_t WB = mm_w_bytes(BN), TCOLS = MM_NTG * MM_TG, IDESC = mm_idesc(BN), RB = (uint32_t)BN * RP;
+    static_assert(!STAGE || (RP % 16 == 0 && RB % 128 == 0), "raw ring slots 128-byte aligned, rows 16-byte aligned");
     constexpr uint32_t KSTEPS_PER_BLOCK = STAGE ? BS / MM_BK : 1;   // K steps per staged raw block (4)
     extern __shared__ __align__(128) uint8_t smem[];   // no-swizzle descriptors need 16-byte alignment
     __shared__ uint64_t wfull[2], wfree[2], xfull[MM_XS], xfree[MM_XS], rfull[2], rfree[2], done;
     __shared__ uint32_t s_tmem;
     uint8_t* wsm = smem;                  // [2 slots][hi, lo][WB]
     uint8_t* xsm = smem + 4 * WB;         // [XS slots][hi, lo][MM_XQ_BYTES]
-    uint8_t* rsm = xsm + XS * 2 * MM_XQ_BYTES;   // staged: [2 slots][BN rows][BB] raw blocks
+    uint8_t* rsm = xsm + XS * 2 * MM_XQ_BYTES;   // staged: [2 slots][BN rows][RP] raw blocks
     rsm += (128u - (smem_addr(rsm) & 127u)) & 127u;   // RB is a multiple of 128: both slots aligned
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t n0 = blockIdx.x * BN, gtg0 = blockIdx.y * MM_NTG;
@@ -336,7 +349,11 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
                 float v[8];
                 if (STAGE) {
                     if (n < n_rows) {
-                        deq8<DT>(rblk + r * BB, (int)(k0 % BS), v);
+                        // MMS_ROWS: the block sits at its global address's offset in the aligned window
+                        const uint32_t off = SM == MMS_ROWS
+                                                 ? (uint32_t)(((uint64_t)n * row_bytes + (uint64_t)(k0 / BS) * BB) & 15u)
+                                                 : 0u;
+                        deq8<DT>(rblk + r * RP + off, (int)(k0 % BS), v);
                     } else {
 #pragma unroll
                         for (int j = 0; j < 8; ++j) v[j] = 0.f;
@@ -379,13 +396,25 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
         auto load_raw = [&](uint32_t lb) {
             const uint32_t q = lb & 1;
             if (lb >= 2) mbar_wait(&rfree[q], ((lb >> 1) - 1) & 1, errf);
-            mbar_arrive_expect_tx(&rfull[q], RB);
-            const int x = (int)((kb0 / KSTEPS_PER_BLOCK + lb) * BB), yrow = (int)n0;
-            asm volatile(
-                "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
-                "[%4];" ::"r"(smem_addr(rsm + q * RB)),
-                "l"(reinterpret_cast<uint64_t>(&wmap)), "r"(x), "r"(yrow), "r"(smem_addr(&rfull[q]))
-                : "memory");
+            if constexpr (SM == MMS_TMA) {
+                mbar_arrive_expect_tx(&rfull[q], RB);
+                const int x = (int)((kb0 / KSTEPS_PER_BLOCK + lb) * BB), yrow = (int)n0;
+                asm volatile(
+                    "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+                    "%3}], [%4];" ::"r"(smem_addr(rsm + q * RB)),
+                    "l"(reinterpret_cast<uint64_t>(&wmap)), "r"(x), "r"(yrow), "r"(smem_addr(&rfull[q]))
+                    : "memory");
+            } else {
+                // one RP-byte copy per row from the 16-byte boundary at or below its block
+                // (the weight base is 16-byte aligned; the allocation has 16 bytes of slack)
+                const uint32_t rows = min((uint32_t)BN, n_rows - n0);
+                const uint64_t boff = (uint64_t)(kb0 / KSTEPS_PER_BLOCK + lb) * BB;
+                mbar_arrive_expect_tx(&rfull[q], rows * RP);
+                for (uint32_t r = 0; r < rows; ++r) {
+                    const uint64_t src = ((uint64_t)(n0 + r) * row_bytes + boff) & ~(uint64_t)15;
+                    bulk_g2s(rsm + q * RB + r * RP, w + src, RP, &rfull[q]);
+                }
+            }
         };
         if constexpr (STAGE) {
             for (uint32_t lb = 0; lb < 2 && lb < nblk; ++lb) load_raw(lb);
