@@ -185,11 +185,12 @@ template <> __device__ __forceinline__ void deq8<GGC_Q6_K>(const uint8_t* b, int
     }
 }
 
-// X rows -> bf16 hi / lo in the blocked tile layout the product loads with one
-// bulk copy per tile: tile (M-block g, K step kb) is 16 KB at ((g * nk + kb) *
-// 16 KB), inside it byte kchunk * 2048 + row * 16 (the no-swizzle core-matrix
-// layout).  Rows m .. mpad-1 and columns k .. kpad-1 are zero.  The row's
-// RMSNorm (ops.rs:262-274, f64 sum of squares) or silu(gate) * up comes first.
+// X rows -> bf16 hi / lo in the blocked tile layout the product loads with bulk
+// copies: tile (256-token group g, K step kb) is 32 KB at ((g * nk + kb) * 32 KB),
+// inside it byte kchunk * 4096 + row * 16 (the no-swizzle core-matrix layout;
+// the 16 columns of a copy slot are 8 KB contiguous).  Rows m .. mpad-1 and
+// columns k .. kpad-1 are zero.  The row's RMSNorm (ops.rs:262-274, f64 sum of
+// squares) or silu(gate) * up comes first.
 enum MmPro : int { MMP_PLAIN = 0, MMP_RMSNORM = 1, MMP_SWIGLU = 2 };
 constexpr int SPLIT_THREADS = 256;
 
@@ -257,20 +258,22 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_x_split(const float* __restri
     }
 }
 
-// Y[m][n] (+)= X . W^T.  Block = 8 dequantising warps + 1 issuer warp.
+// Y[m][n] (+)= X . W^T as D = W . X^T.  Block = 8 dequantising warps + the MMA
+// warp + the copy warp.
 //   dequant warps: W tile of K step kb (BN rows x 64) -> bf16 hi / lo into W
 //     slot kb % 2 (after the MMAs of kb - 2 freed it: wfree), arrive on wfull;
 //   copy warp (warp 9, one lane): keeps the X ring full by bulk copy -- one slot
-//     = one M-block x half a K step (32 columns), hi + lo, 16 KB (xfull; a slot
-//     is refilled after the MMAs that read it completed: xfree) -- and, for the
-//     staged formats, the raw ring;
-//   MMA issuer (warp 8, one lane, TMEM owner): for each K step waits for the W
-//     slot, then per M-block and K half for its X slot, issues 2 x 3 MMAs into
-//     the M-block's TMEM columns and commits them to xfree; the step's commit
-//     frees the W slot, the last one signals `done`.  It never waits on a free
-//     slot, so the tensor pipe's queue stays full while copies are in flight;
-//   epilogue: the 8 warps read TMEM (warp w: lanes 32 (w % 4).., M-blocks of
-//     half w / 4) and write Y (+ the residual).
+//     = one 256-token group x 16 columns of a K step, hi + lo, 16 KB (xfull; a
+//     slot is refilled after the MMAs that read it completed: xfree) -- and, for
+//     the staged formats, the raw ring;
+//   MMA warp (warp 8, one lane, TMEM owner): for each K step waits for the W
+//     slot, then per token group and 16 columns for its X slot, issues 3 MMAs
+//     (A = the W rows of the slot, B = the X slot) into the group's 256 TMEM
+//     columns and commits them to xfree; the step's commit frees the W slot, the
+//     last one signals `done`.  It never waits on a free slot, so the tensor
+//     pipe's queue stays full while copies are in flight;
+//   epilogue: the 8 warps read TMEM (warp w: lanes 32 (w % 4).. = weight rows,
+//     columns of token group w / 4) and write Y (+ the residual).
 // Every wait is bounded (ERRF_TIMEOUT); no thread leaves early, warp 8 frees TMEM.
 //
 // SM = MMS_TMA (Q4_K, Q5_K): the copy warp also loads the CTA's raw blocks of
