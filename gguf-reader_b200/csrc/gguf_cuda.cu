@@ -919,7 +919,7 @@ int ctx_errf(ggc_ctx* ctx, int** out) {
 // x [m][k] f32 (device) -> bf16 hi / lo tiles (k_x_split's blocked layout,
 // rows padded to 128, columns to 64) in staging buffers 3 / 4
 int split_rows(ggc_ctx* ctx, const float* x, const float* x2, uint32_t m, uint32_t k, uint32_t ldx, int pro,
-               uint8_t** xh, uint8_t** xl, uint32_t* kpad) {
+               uint8_t** xh, uint8_t** xl, uint32_t* kpad, int* errf = nullptr, int nan_slot = 0, int nan_val = 0) {
     *kpad = (k + MM_BK - 1) / MM_BK * MM_BK;
     const uint32_t mpad = (m + MM_TG - 1) / MM_TG * MM_TG;
     const size_t bytes = (size_t)mpad * *kpad * 2;
@@ -928,7 +928,8 @@ int split_rows(ggc_ctx* ctx, const float* x, const float* x2, uint32_t m, uint32
     *xh = (uint8_t*)ctx->stage[3];
     *xl = (uint8_t*)ctx->stage[4];
     const int vec = ((uintptr_t)x % 16 == 0) && (!x2 || (uintptr_t)x2 % 16 == 0) && ldx % 4 == 0;
-    GGC_CUDA_TRY(launch(ctx, k_x_split, dim3(mpad), dim3(SPLIT_THREADS), 0, x, x2, m, k, ldx, *kpad, pro, vec, *xh, *xl));
+    GGC_CUDA_TRY(launch(ctx, k_x_split, dim3(mpad), dim3(SPLIT_THREADS), 0, x, x2, m, k, ldx, *kpad, pro, vec, *xh, *xl,
+                        errf, nan_slot, errf ? nan_val : 0));
     return GGC_OK;
 }
 
@@ -2057,10 +2058,11 @@ struct SplitX {
     uint32_t kpad = 0;
     uint32_t cols = 0;
 };
+// nan_val != 0 (RMSNorm only): the split is the NaN guard of x as well
 int mm_split_x(ggc_model* m, const float* x, const float* x2, uint32_t n, uint32_t cols, uint32_t ldx, int pro,
-               SplitX* sx) {
+               SplitX* sx, int nan_slot = 0, int nan_val = 0) {
     sx->cols = cols;
-    return split_rows(m->ctx, x, x2, n, cols, ldx, pro, &sx->xh, &sx->xl, &sx->kpad);
+    return split_rows(m->ctx, x, x2, n, cols, ldx, pro, &sx->xh, &sx->xl, &sx->kpad, m->errf, nan_slot, nan_val);
 }
 int mm_split_w(ggc_model* m, const RawMat& w, const SplitX& sx, uint32_t n, float* y, uint32_t ldy, const float* resid) {
     if (w.cols != sx.cols) return set_error(GGC_ERR_INVALID_ARG, "prefill product: %u columns, split input %u", w.cols, sx.cols);
@@ -2110,11 +2112,6 @@ int prefill_batch(ggc_model* m, const uint32_t* tokens, const int64_t* positions
         const ncclResult_t r = nccl().AllReduce(m->pf_h, m->pf_h, (size_t)n * d, ncclFloat, ncclSum, ctx->comm, ctx->stream);
         return r == ncclSuccess ? GGC_OK : nccl_error("ncclAllReduce", r);
     };
-    auto nan_scan = [&](uint32_t n, int slot, int val) -> int {
-        GGC_CUDA_TRY(launch(ctx, k_nan_scan, dim3((unsigned)std::min<uint64_t>(cdiv<uint64_t>((uint64_t)n * d, 256), 1024)),
-                            dim3(256), 0, (const float*)m->pf_h, (uint64_t)n * d, m->errf, slot, val));
-        return GGC_OK;
-    };
     for (uint64_t done = 0; done < count; done += PF_CHUNK) {
         const uint32_t n = (uint32_t)std::min<uint64_t>(PF_CHUNK, count - done);
         const uint32_t slot0 = (uint32_t)(base + done);
@@ -2135,8 +2132,8 @@ int prefill_batch(ggc_model* m, const uint32_t* tokens, const int64_t* positions
             float* yk = m->pf_y + m->qdim;
             float* yv = yk + m->kvdim;
             const uint32_t ldy = m->qdim + 2 * m->kvdim;
-            SplitX sx;   // RMSNorm(h) split once for q, k, v
-            GGC_TRY(mm_split_x(m, m->pf_h, L.attn_norm, n, d, d, MMP_RMSNORM, &sx));
+            SplitX sx;   // RMSNorm(h) split once for q, k, v; the NaN guard after layer l - 1's ffn
+            GGC_TRY(mm_split_x(m, m->pf_h, L.attn_norm, n, d, d, MMP_RMSNORM, &sx, ERRF_NAN_FFN, (int)l));
             if (!last) GGC_TRY(mm_split_w(m, L.rq, sx, n, yq, ldy, nullptr));
             GGC_TRY(mm_split_w(m, L.rk, sx, n, yk, ldy, nullptr));
             GGC_TRY(mm_split_w(m, L.rv, sx, n, yv, ldy, nullptr));
@@ -2154,18 +2151,17 @@ int prefill_batch(ggc_model* m, const uint32_t* tokens, const int64_t* positions
                 GGC_CUDA_TRY(launch(ctx, k_attn_prefill<128>, ag, dim3(PA_WARPS * 32), pa_smem<128>(), (const float*)m->pf_q,
                                     (const void*)kc, (const void*)vc, (const int64_t*)m->pf_pos, slot0, n, m->heads_l,
                                     m->kv_heads_l, hp.max_ctx, hp.kv_f16 ? 1 : 0, inv, m->pf_o));
-            // attn_output + residual (rank 0 alone under tensor parallelism), all-reduce, NaN guard
+            // attn_output + residual (rank 0 alone under tensor parallelism), all-reduce
             GGC_TRY(mm_raw(m, L.ro, m->pf_o, nullptr, n, m->qdim, MMP_PLAIN, m->pf_h, d, lead ? m->pf_h : nullptr));
             GGC_TRY(allreduce_h(n));
-            GGC_TRY(nan_scan(n, ERRF_NAN_ATTN, (int)l + 1));
-            // ffn: up | gate side by side in pf_y, then down (+ residual)
+            // ffn: up | gate side by side in pf_y, then down (+ residual); the split
+            // (once for up and gate) is the NaN guard after this layer's attention
             const uint32_t fl = L.f_l, ldu = 2 * fl;
-            GGC_TRY(mm_split_x(m, m->pf_h, L.ffn_norm, n, d, d, MMP_RMSNORM, &sx));   // once for up and gate
+            GGC_TRY(mm_split_x(m, m->pf_h, L.ffn_norm, n, d, d, MMP_RMSNORM, &sx, ERRF_NAN_ATTN, (int)l + 1));
             GGC_TRY(mm_split_w(m, L.rup, sx, n, m->pf_y, ldu, nullptr));
             GGC_TRY(mm_split_w(m, L.rgate, sx, n, m->pf_y + fl, ldu, nullptr));
             GGC_TRY(mm_raw(m, L.rdown, m->pf_y + fl, m->pf_y, n, ldu, MMP_SWIGLU, m->pf_h, d, lead ? m->pf_h : nullptr));
-            GGC_TRY(allreduce_h(n));
-            GGC_TRY(nan_scan(n, ERRF_NAN_FFN, (int)l + 1));
+            GGC_TRY(allreduce_h(n));   // its NaN guard: the next layer's q/k/v split
         }
     }
     int hf[ERRF_COUNT];

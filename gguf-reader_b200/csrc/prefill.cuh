@@ -190,13 +190,17 @@ template <> __device__ __forceinline__ void deq8<GGC_Q6_K>(const uint8_t* b, int
 // inside it byte kchunk * 4096 + row * 16 (the no-swizzle core-matrix layout;
 // the 16 columns of a copy slot are 8 KB contiguous).  Rows m .. mpad-1 and
 // columns k .. kpad-1 are zero.  The row's RMSNorm (ops.rs:262-274, f64 sum of
-// squares) or silu(gate) * up comes first.
+// squares) or silu(gate) * up comes first.  With RMSNorm and nan_val != 0 the
+// split is also the NaN guard of its input (llama.rs:300-307): a row's sum of
+// squares is NaN exactly when the row holds a NaN -> errf[nan_slot] = nan_val
+// (first wins).
 enum MmPro : int { MMP_PLAIN = 0, MMP_RMSNORM = 1, MMP_SWIGLU = 2 };
 constexpr int SPLIT_THREADS = 256;
 
 __global__ void __launch_bounds__(SPLIT_THREADS) k_x_split(const float* __restrict__ x, const float* __restrict__ x2,
                                                            uint32_t m, uint32_t k, uint32_t ldx, uint32_t kpad, int pro,
-                                                           int vec, uint8_t* __restrict__ xh, uint8_t* __restrict__ xl) {
+                                                           int vec, uint8_t* __restrict__ xh, uint8_t* __restrict__ xl,
+                                                           int* errf, int nan_slot, int nan_val) {
     pdl_trigger();
     pdl_wait();
     const uint32_t row = blockIdx.x, nk = kpad / MM_BK;
@@ -215,6 +219,7 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_x_split(const float* __restri
             double t = 0.0;
             for (int w = 0; w < SPLIT_THREADS / 32; ++w) t += red[w];
             s_scale = (float)sqrt(1.0 / (t / (double)k + (double)1e-6f));
+            if (nan_val && isnan(t)) atomicCAS(&errf[nan_slot], 0, nan_val);
         }
         __syncthreads();
         scale = s_scale;
@@ -809,17 +814,6 @@ __global__ void __launch_bounds__(PA_WARPS * 32, 1) k_attn_prefill(const float* 
 #pragma unroll
         for (int c = 0; c < NI; ++c) dst[c] = acc[k][c] * rs;
     }
-}
-
-// NaN anywhere in x[0, n) -> errf[slot] = val (first wins); the NaN guards of
-// llama.rs:300-307 for the batch
-__global__ void __launch_bounds__(256) k_nan_scan(const float* __restrict__ x, uint64_t n, int* errf, int slot, int val) {
-    pdl_trigger();
-    pdl_wait();
-    bool nan = false;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
-        nan |= isnan(x[i]);
-    if (__any_sync(0xffffffffu, nan) && (threadIdx.x & 31) == 0) atomicCAS(&errf[slot], 0, val);
 }
 
 }  // namespace ggc
