@@ -608,10 +608,22 @@ AttnDecodeSel attn_decode_sel(uint32_t hd, bool f16, uint32_t G) {
     }
 }
 
+// Kernel attributes are per device: set once for every device a context runs on
+// (the caller's device guard makes it current).
+constexpr int GGC_MAX_DEVICES = 64;
+int current_device() {
+    int d = -1;
+    return cudaGetDevice(&d) == cudaSuccess && d >= 0 && d < GGC_MAX_DEVICES ? d : -1;
+}
+
 int init_kernel_attrs() {
-    static std::once_flag once;
-    static int ok = 1;
-    std::call_once(once, [] {
+    static std::once_flag once_dev[GGC_MAX_DEVICES];
+    static int ok_dev[GGC_MAX_DEVICES];
+    const int dev = current_device();
+    if (dev < 0) return set_error(GGC_ERR_CUDA, "no current device below %d", GGC_MAX_DEVICES);
+    int& ok = ok_dev[dev];
+    std::call_once(once_dev[dev], [&ok] {
+        ok = 1;
         const int dts[] = {GGC_F32, GGC_F16, GGC_BF16, GGC_Q4_0, GGC_Q4_1, GGC_Q5_0, GGC_Q5_1, GGC_Q8_0,
                            GGC_Q2_K, GGC_Q3_K_S, GGC_Q3_K_M, GGC_Q3_K_L, GGC_Q4_K, GGC_Q5_K, GGC_Q6_K, GGC_Q8_K};
         for (int dt : dts) dispatch_dtype<SetGemvSmem>(dt, &ok);
@@ -621,7 +633,7 @@ int init_kernel_attrs() {
             cudaFuncSetAttribute(k_attn_prefill<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pa_smem<128>()) !=
                 cudaSuccess)
             ok = 0;
-        for_each_attn_decode([](auto kernel, size_t smem) {
+        for_each_attn_decode([&ok](auto kernel, size_t smem) {
             if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) ok = 0;
         });
     });
@@ -848,9 +860,12 @@ template <int DT>
 struct RunMM {
     template <int SM>
     static cudaError_t set_attr() {
-        static std::once_flag once;
-        static cudaError_t attr = cudaSuccess;
-        std::call_once(once, [] {
+        static std::once_flag once_dev[GGC_MAX_DEVICES];
+        static cudaError_t attr_dev[GGC_MAX_DEVICES];
+        const int dev = current_device();
+        if (dev < 0) return cudaErrorInvalidDevice;
+        cudaError_t& attr = attr_dev[dev];
+        std::call_once(once_dev[dev], [&attr] {
             attr = cudaFuncSetAttribute(k_mm_tc<DT, MM_BN, SM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)mm_smem(MM_BN, SM, block_bytes_of(DT)));
         });
