@@ -91,7 +91,10 @@ class _Cursor:
         n = self.take("<Q")
         if self.pos + n > len(self.buf):
             raise GgufFormatError(f"string of {n} bytes at {self.pos} past the end")
-        s = bytes(self.buf[self.pos:self.pos + n]).decode("utf-8", errors="replace")
+        try:   # the reader rejects a string that is not UTF-8 (InvalidStringLength)
+            s = bytes(self.buf[self.pos:self.pos + n]).decode("utf-8")
+        except UnicodeDecodeError as e:
+            raise GgufFormatError(f"invalid UTF-8 in the string of {n} bytes at {self.pos}") from e
         self.pos += n
         return s
 
@@ -102,7 +105,13 @@ class _Cursor:
             return self.string()
         if ty == T_ARR:
             ety = self.take("<i")
+            if ety not in _SCALAR and ety != T_STR:   # nested arrays and unknown types (InvalidArrayElemType)
+                raise GgufFormatError(f"invalid array element type {ety}")
             n = self.take("<Q")
+            # every element takes at least its scalar size (a string its 8-byte length)
+            least = struct.calcsize(_SCALAR[ety]) if ety in _SCALAR else 8
+            if n * least > len(self.buf) - self.pos:
+                raise GgufFormatError(f"array of {n} elements at {self.pos} past the end ({len(self.buf)})")
             return [self.value(ety) for _ in range(n)]
         raise GgufFormatError(f"invalid metadata type {ty}")
 
@@ -139,6 +148,8 @@ class GgufFile:
             if n_dims > 8:
                 raise GgufFormatError(f"tensor {name}: {n_dims} dims")
             shape = [c.take("<q") for _ in range(n_dims)]
+            if any(d < 0 for d in shape):   # InvalidTensorDim
+                raise GgufFormatError(f"tensor {name}: negative dimension in {shape}")
             dtype = c.take("<i")
             offset = c.take("<Q")
             self.tensors.append(TensorInfo(name, shape, dtype, offset))

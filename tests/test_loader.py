@@ -62,6 +62,56 @@ def test_format_errors(tmp_path):
         loader.GgufFile(memoryview(bytes(raw[:20])))                 # header cut short
 
 
+def _header(n_tensors, n_kv):
+    return struct.pack("<IIqq", loader.GGUF_MAGIC, 3, n_tensors, n_kv)
+
+
+def _gstr(b):
+    return struct.pack("<Q", len(b)) + b
+
+
+def _open(raw):
+    return loader.GgufFile(memoryview(bytes(raw)))
+
+
+def test_reader_edge_cases():
+    """The reader cases of the reference's tests/parse_buffer.rs, on byte buffers."""
+    for raw in (b"", b"\x47"):                                           # empty, one byte
+        with pytest.raises(loader.GgufFormatError):
+            _open(raw)
+    f = _open(_header(0, 0))                                              # header only parses
+    assert f.kv == {} and f.tensors == []
+    with pytest.raises(loader.GgufFormatError, match="past the end"):      # 1 KV claimed, none there
+        _open(_header(0, 1))
+    big = _gstr(b"big") + struct.pack("<iiQ", T_ARR, T_U8, 1000) + bytes([1, 2, 3, 4])
+    with pytest.raises(loader.GgufFormatError, match="past the end"):      # array count past the data
+        _open(_header(0, 1) + big)
+    nested = _gstr(b"nested") + struct.pack("<iiQ", T_ARR, T_ARR, 0)
+    with pytest.raises(loader.GgufFormatError, match="element type 9"):    # arrays of arrays
+        _open(_header(0, 1) + nested)
+    bad = _gstr(b"bad") + struct.pack("<i", T_STR) + _gstr(bytes([0xFF, 0xFE, 0xFD]))
+    with pytest.raises(loader.GgufFormatError, match="UTF-8"):
+        _open(_header(0, 1) + bad)
+
+    def tensor(name, dims, dtype, offset=0):
+        return _gstr(name) + struct.pack("<I", len(dims)) + struct.pack(f"<{len(dims)}q", *dims) + \
+            struct.pack("<iQ", dtype, offset)
+
+    with pytest.raises(loader.GgufFormatError, match="negative"):
+        _open(_header(1, 0) + tensor(b"neg", [-5, 3], F32))
+    f = _open(_header(1, 0) + tensor(b"z", [2, 2], 99))                  # unknown dtype: parses ...
+    assert f.tensors[0].dtype == 99
+    with pytest.raises(loader.GgufFormatError, match="unknown dtype 99"):  # ... and fails when sized
+        f.tensors[0].data_size()
+    kvs = b"".join(_gstr(k) + struct.pack("<iI", T_U32, i) for i, k in enumerate([b"first", b"second", b"third"]))
+    assert list(_open(_header(0, 3) + kvs).kv) == ["first", "second", "third"]   # KV order kept
+    one = tensor(b"a", [10], F32)
+    assert _open(_header(1, 0) + one + bytes(64)).alignment == 32        # default alignment
+    al = _gstr(b"general.alignment") + struct.pack("<iI", T_U32, 16)
+    f = _open(_header(1, 1) + al + one + bytes(64))
+    assert f.alignment == 16 and f.data_offset % 16 == 0 and f.data_offset <= f.file_size
+
+
 def test_hparams_keys_and_defaults(tmp_path):
     p = tmp_path / "q.gguf"
     kv = [("general.architecture", T_STR, "qwen2"), ("qwen2.embedding_length", T_U32, 64),
