@@ -22,6 +22,7 @@ The file is memory-mapped; tensor bytes are views into the map.
 from __future__ import annotations
 
 import mmap
+import os
 import struct
 from pathlib import Path
 
@@ -164,6 +165,8 @@ class GgufFile:
     def open(cls, path) -> "GgufFile":
         f = open(Path(path), "rb")
         try:
+            if os.fstat(f.fileno()).st_size == 0:   # (mmap refuses an empty file)
+                raise GgufFormatError(f"{path}: empty file")
             mm = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
         finally:
             f.close()

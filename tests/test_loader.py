@@ -112,6 +112,23 @@ def test_reader_edge_cases():
     assert f.alignment == 16 and f.data_offset % 16 == 0 and f.data_offset <= f.file_size
 
 
+def test_open_errors_and_missing_ffn_length(tmp_path):
+    """tests/from_reader_path.rs (missing path, empty file) and the missing-KV
+    case of tests/inference.rs (no ffn_length: an error, not a crash)."""
+    with pytest.raises(OSError):
+        loader.GgufFile.open(tmp_path / "does-not-exist.gguf")
+    empty = tmp_path / "empty.gguf"
+    empty.write_bytes(b"")
+    with pytest.raises(loader.GgufFormatError, match="empty"):
+        loader.GgufFile.open(empty)
+    p = tmp_path / "noffn.gguf"
+    kv = [("general.architecture", T_STR, "llama"), ("general.alignment", T_U32, 32), ("llama.vocab_size", T_U32, 8),
+          ("llama.embedding_length", T_U32, 4), ("llama.attention.head_count", T_U32, 2), ("llama.block_count", T_U32, 1)]
+    loader.write_gguf(p, kv, [])
+    with pytest.raises(loader.GgufFormatError, match="feed_forward_length"):
+        loader.hparams(loader.GgufFile.open(p))
+
+
 def test_hparams_keys_and_defaults(tmp_path):
     p = tmp_path / "q.gguf"
     kv = [("general.architecture", T_STR, "qwen2"), ("qwen2.embedding_length", T_U32, 64),
