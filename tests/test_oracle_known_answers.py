@@ -413,3 +413,29 @@ def test_oracle_sampler_basics(orc):
     # min-p 0.9 keeps only probabilities within 90 % of the top: indices 1 and 3
     assert all(orc.sample(lg, dict(top_k=0, top_p=1.0, min_p=0.9, repeat_penalty=1.0), u=u) in (1, 3)
                for u in np.linspace(0, 0.99, 50))
+
+
+def test_oracle_sampler_reference_unit_tests(orc):   # sampler.rs:230-327, over a sweep of uniform draws
+    import numpy as np
+    us = [float(u) for u in np.linspace(0.0, 0.999, 41)]
+    greedy = dict(temperature=0.0, top_k=40, top_p=0.95, repeat_penalty=1.0)
+    assert orc.sample(np.array([1.0, 5.0, 3.0, 2.0], np.float32), greedy) == 1          # test_greedy / temperature 0
+    top_k2 = dict(temperature=1.0, top_k=2, top_p=1.0, repeat_penalty=1.0)
+    lg = np.array([9.0, 10.0, -100.0, -100.0], np.float32)
+    assert {orc.sample(lg, top_k2, u=u) for u in us} <= {0, 1}                         # test_top_k
+    top_p = dict(temperature=1.0, top_k=100, top_p=0.5, repeat_penalty=1.0)
+    assert {orc.sample(np.array([10.0, 9.0, -100.0, -100.0], np.float32), top_p, u=u) for u in us} <= {0, 1}   # test_top_p
+    pen = dict(temperature=0.0, top_k=40, top_p=1.0, min_p=0.0, repeat_penalty=10.0)
+    assert orc.sample(np.array([5.0, 5.0], np.float32), pen, seen=[0]) == 1            # test_repeat_penalty
+    min_p = dict(temperature=1.0, top_k=100, top_p=1.0, min_p=0.5, repeat_penalty=1.0)
+    assert {orc.sample(np.array([10.0, 0.0, -100.0], np.float32), min_p, u=u) for u in us} == {0}   # test_min_p
+    ramp = (np.arange(100) * 0.1).astype(np.float32)
+    cfg = dict(temperature=1.0, top_k=40, top_p=0.95, repeat_penalty=1.0)
+    assert all(orc.sample(ramp, cfg, u=u) == orc.sample(ramp, cfg, u=u) for u in us)  # test_deterministic_with_seed
+    lg50 = (np.arange(50) * 0.5 - 12.0).astype(np.float32)
+    cfg = dict(temperature=0.8, top_k=20, top_p=0.9, repeat_penalty=1.0)
+    seen = []
+    for u in us[:20]:                                                                 # test_sample_valid_range
+        tid = orc.sample(lg50, cfg, seen, u=u)
+        assert 0 <= tid < 50
+        seen.append(tid)
