@@ -138,6 +138,8 @@ class GgufFile:
         n_kv = c.take("<q")
         if n_tensors < 0 or n_kv < 0:
             raise GgufFormatError("negative tensor or KV count")
+        if n_kv > len(buf) or n_tensors > len(buf):   # every entry takes bytes: a corrupt count (InvalidCount)
+            raise GgufFormatError(f"tensor count {n_tensors} or KV count {n_kv} exceeds the file size {len(buf)}")
         self.kv = {}
         for _ in range(n_kv):
             key = c.string()

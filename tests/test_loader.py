@@ -112,6 +112,26 @@ def test_reader_edge_cases():
     assert f.alignment == 16 and f.data_offset % 16 == 0 and f.data_offset <= f.file_size
 
 
+def test_reader_counts_dims_and_alignment():
+    """The parser cases of src/file.rs tests: counts, dimension limits, alignment 0."""
+    for nt, nk in ((0, -1), (-5, 0), (0, 1_000_000)):                    # negative, or beyond the file size
+        with pytest.raises(loader.GgufFormatError, match="count"):
+            _open(_header(nt, nk))
+
+    def tensor(name, dims, dtype=F32):
+        return _gstr(name) + struct.pack("<I", len(dims)) + struct.pack(f"<{len(dims)}q", *dims) + \
+            struct.pack("<iQ", dtype, 0)
+
+    with pytest.raises(loader.GgufFormatError, match="9 dims"):
+        _open(_header(1, 0) + tensor(b"t", [1] * 9))
+    f = _open(_header(1, 0) + tensor(b"s", []))                          # a scalar: no dims, one element
+    assert f.tensors[0].shape == [] and f.tensors[0].num_elements() == 1
+    f = _open(_header(2, 0) + tensor(b"a", [2, 3, 4, 5, 6]) + tensor(b"b", list(range(1, 9))))
+    assert f.tensors[0].shape == [2, 3, 4, 5, 6] and f.tensors[1].shape == list(range(1, 9))
+    zero = _gstr(b"general.alignment") + struct.pack("<iI", T_U32, 0)
+    assert _open(_header(0, 1) + zero).alignment == 32                   # alignment 0 falls back
+
+
 def test_open_errors_and_missing_ffn_length(tmp_path):
     """tests/from_reader_path.rs (missing path, empty file) and the missing-KV
     case of tests/inference.rs (no ffn_length: an error, not a crash)."""
