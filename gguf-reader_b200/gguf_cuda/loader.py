@@ -33,6 +33,7 @@ from . import _lib as L
 GGUF_MAGIC = 0x46554747            # "GGUF", little-endian
 GGUF_VERSION = 3
 GGUF_DEFAULT_ALIGNMENT = 32
+U64_MAX = (1 << 64) - 1
 
 # metadata value types (src/types.rs:7-21)
 T_U8, T_I8, T_U16, T_I16, T_U32, T_I32, T_F32, T_BOOL, T_STR, T_ARR, T_U64, T_I64, T_F64 = range(13)
@@ -60,9 +61,10 @@ class TensorInfo:
         self.name, self.shape, self.dtype, self.offset = name, shape, dtype, offset
 
     def num_elements(self) -> int:
+        """Product of the dims, saturating at 2^64 - 1 (src/tensor.rs:18-22)."""
         n = 1
         for d in self.shape:
-            n *= d
+            n = min(n * d, U64_MAX)
         return n
 
     def data_size(self) -> int:

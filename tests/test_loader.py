@@ -132,6 +132,19 @@ def test_reader_counts_dims_and_alignment():
     assert _open(_header(0, 1) + zero).alignment == 32                   # alignment 0 falls back
 
 
+def test_tensor_sizes():   # src/tensor.rs tests: element counts (saturating) and block data sizes
+    T = loader.TensorInfo
+    assert T("t", [0, 5], F32, 0).num_elements() == 0 and T("s", [], F32, 0).num_elements() == 1
+    assert T("h", [loader.U64_MAX, 2], F32, 0).num_elements() == loader.U64_MAX
+    assert T("h", [loader.U64_MAX // 2] * 2, F32, 0).num_elements() == loader.U64_MAX
+    assert T("t", [4096], Q4_0, 0).data_size() == 128 * 18
+    assert T("t", [1024], Q8_0, 0).data_size() == 32 * 34
+    assert T("t", [4096, 4096], Q4_K, 0).data_size() == 65536 * 144
+    assert T("t", [256], 15, 0).data_size() == 292                       # Q8_K
+    with pytest.raises(loader.GgufFormatError, match="multiple"):
+        T("bad", [33], Q4_0, 0).data_size()
+
+
 def test_open_errors_and_missing_ffn_length(tmp_path):
     """tests/from_reader_path.rs (missing path, empty file) and the missing-KV
     case of tests/inference.rs (no ffn_length: an error, not a crash)."""
