@@ -190,6 +190,17 @@ def lib() -> C.CDLL:
     return _lib
 
 
+def host_error(cls, message: str, **fields) -> GgufError:
+    """An error of the reference's kind raised by host code (the loader), with
+    the same payload fields as one raised through the C ABI."""
+    info = ErrorInfo()
+    info.status = cls.status
+    info.message = message.encode()[:255]
+    for k, v in fields.items():
+        setattr(info, k, v.encode()[:15] if isinstance(v, str) else v)
+    return cls(info)
+
+
 def check(status: int):
     if status != OK:
         info = ErrorInfo()

@@ -17,6 +17,9 @@ returns one token id.  Tokenizing and UTF-8 streaming stay with the caller:
     (engine.rs:516-521).
   * The sampler's RNG stays here: ``draw()`` returns the uniform the reference's
     StdRng would give (a seeded numpy generator by default).
+  * Configurations that keep more than 1024 candidates after top-k (top_k = 0
+    or above 1024) are sampled on the host from the logits of the last forward
+    (``sampling.sample_host``), since the device kernel holds at most 1024.
 """
 from __future__ import annotations
 
@@ -24,6 +27,8 @@ from collections import Counter
 from typing import Callable
 
 import numpy as np
+
+from .sampling import device_can_sample, sample_host
 
 IM_START, IM_END, TOK_USER, TOK_ASSISTANT, TOK_SYSTEM = 151644, 151645, 872, 77091, 8948
 SYSTEM_PROMPT = "You are a helpful assistant."
@@ -45,10 +50,20 @@ class Engine:
         self.seen = Counter()          # Sampler::record counts (sampler.rs:80-83)
         self.chat_prefilled = False
         self.chat_history = []         # (user text, reply ids)
+        self.host_sampling = not device_can_sample(self.sampler, model.vocab)
+        self._logits = None
 
-    # Sampler::sample over the model's last logits, on the device
+    def _forward(self, ids, pos):
+        out = self.model.forward(ids, pos, want_logits=self.host_sampling)
+        if self.host_sampling:
+            self._logits = out
+
+    # Sampler::sample over the model's last logits (on the device unless it keeps > 1024 candidates)
     def _sample(self) -> int:
-        return self.model.sample(self.sampler, [t for t, c in self.seen.items() if c > 0], self.draw())
+        seen = [t for t, c in self.seen.items() if c > 0]
+        if self.host_sampling:
+            return sample_host(self._logits, self.sampler, seen, self.draw())
+        return self.model.sample(self.sampler, seen, self.draw())
 
     def _loop(self, max_tokens: int, pos=None) -> list:
         out = []
@@ -59,7 +74,7 @@ class Engine:
             out.append(tid)
             self.seen[tid] += 1
             p = self.model.cache_len() if pos is None else pos
-            self.model.forward([tid], [p], want_logits=False)
+            self._forward([tid], [p])
             if pos is not None:
                 pos += 1
         return out
@@ -69,7 +84,7 @@ class Engine:
         ids = [int(t) for t in prompt_ids]
         if not ids:
             raise ValueError("prompt tokenize empty")
-        self.model.forward(ids, list(range(len(ids))), want_logits=False)
+        self._forward(ids, list(range(len(ids))))
         return self._loop(max_tokens, pos=len(ids))
 
     def chat(self, text: str, max_tokens: int) -> list:
@@ -84,7 +99,7 @@ class Engine:
         if limit is not None and self.model.cache_len() + len(new) > limit:
             raise ValueError(f"context exceeded: {self.model.cache_len()} + {len(new)} > {limit}")
         start = self.model.cache_len()
-        self.model.forward(new, list(range(start, start + len(new))), want_logits=False)   # only the new tokens
+        self._forward(new, list(range(start, start + len(new))))   # only the new tokens
         self.seen = Counter()                                   # sampler.reset() then the history (:325-334)
         for user, reply in self.chat_history:
             self.seen.update(int(t) for t in self.encode(user))

@@ -68,13 +68,16 @@ class TensorInfo:
         return n
 
     def data_size(self) -> int:
-        """Bytes by the marked dtype's block structure (src/tensor.rs:64-80)."""
+        """Bytes by the marked dtype's block structure (src/tensor.rs:64-80):
+        InferenceError for an unknown dtype, InvalidTensorShape {name, elements,
+        block} when the element count is not a multiple of the block size."""
         if self.dtype not in L.BLOCK:
-            raise GgufFormatError(f"tensor {self.name}: unknown dtype {self.dtype}")
+            raise L.host_error(L.InferenceError, f"tensor {self.name}: unknown dtype {self.dtype}")
         bs, bb = L.BLOCK[self.dtype]
         n = self.num_elements()
         if n % bs:
-            raise GgufFormatError(f"tensor {self.name}: {n} elements not a multiple of block {bs}")
+            raise L.host_error(L.InvalidTensorShape, f"tensor {self.name}: {n} elements not a multiple of block {bs}",
+                               elements=n, block=bs)
         return n // bs * bb
 
 
@@ -142,10 +145,15 @@ class GgufFile:
             raise GgufFormatError("negative tensor or KV count")
         if n_kv > len(buf) or n_tensors > len(buf):   # every entry takes bytes: a corrupt count (InvalidCount)
             raise GgufFormatError(f"tensor count {n_tensors} or KV count {n_kv} exceeds the file size {len(buf)}")
-        self.kv = {}
+        # lookups return the first occurrence of a key or tensor name, as
+        # GgufFile::get / find_tensor do (file.rs:367-374)
+        self.kv, self.kv_types = {}, {}
         for _ in range(n_kv):
             key = c.string()
-            self.kv[key] = c.value(c.take("<i"))
+            ty = c.take("<i")
+            val = c.value(ty)
+            if key not in self.kv:
+                self.kv[key], self.kv_types[key] = val, ty
         self.tensors = []
         for _ in range(n_tensors):
             name = c.string()
@@ -158,11 +166,16 @@ class GgufFile:
             dtype = c.take("<i")
             offset = c.take("<Q")
             self.tensors.append(TensorInfo(name, shape, dtype, offset))
-        a = self.kv.get("general.alignment", GGUF_DEFAULT_ALIGNMENT)
-        self.alignment = int(a) if a else GGUF_DEFAULT_ALIGNMENT
+        # general.alignment counts only as a U32 value, 0 meaning the default
+        # (file.rs:166-174); any other type keeps the default
+        self.alignment = GGUF_DEFAULT_ALIGNMENT
+        if self.kv_types.get("general.alignment") == T_U32 and self.kv["general.alignment"]:
+            self.alignment = int(self.kv["general.alignment"])
         self.data_offset = _align_up(c.pos, self.alignment)
         self.file_size = len(buf)
-        self._by_name = {t.name: t for t in self.tensors}
+        self._by_name = {}
+        for t in self.tensors:
+            self._by_name.setdefault(t.name, t)
         self._sorted = sorted(t.offset for t in self.tensors)
 
     @classmethod

@@ -106,7 +106,9 @@ int ggc_quant_matvec(ggc_ctx* ctx, int dtype, const void* w, uint64_t w_len, uin
  *     other errors are those of ggc_quant_matvec, in the same order.
  *   - The first call on each device does a one-time set-up
  *     (cudaGetSymbolAddress of the scratch, with that device current); make
- *     that first call before any stream capture on the device.
+ *     that first call before any stream capture on the device.  The address is
+ *     cached per device for the life of the process: after a cudaDeviceReset
+ *     it is stale, so do not call this entry again in that process.
  *   - Each call clears the tickets it uses (cudaMemsetAsync on `stream`).
  *   - One scratch per device: calls that overlap on a device (several streams
  *     or host threads at once) race on it; the caller serialises them.

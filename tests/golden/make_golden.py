@@ -2,7 +2,7 @@
 dequantisers (tools/gguf_forward_check.py in chaos-asimo/gguf-reader).
 
 Run in a container where the reference is mounted (it is read, never copied):
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/reference
 
 That script computes each element in double precision from the exact f16/int
 operands and rounds once to f32, which equals the Rust f32 result for Q5_0,
@@ -23,7 +23,9 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+if len(sys.argv) != 2:
+    sys.exit("usage: make_golden.py /path/to/reference  (the gguf-reader checkout to read the tool from)")
+REF = Path(sys.argv[1])
 
 # GGUF ids and block geometry (src/types.rs)
 FORMATS = {  # name: (gguf id, block elems, block bytes, f16 scale offsets, tool function)

@@ -20,6 +20,7 @@ class OracleModel:
 
     def __init__(self, orc, hp, ts):
         self.orc, self.m, self.logits = orc, orc.Model(hp, ts), None
+        self.vocab = hp["vocab_size"]
 
     def forward(self, ids, pos, want_logits=True):
         self.logits = self.m.forward(np.asarray(ids, np.uint32), np.asarray(pos, np.int64))
@@ -63,3 +64,15 @@ def test_generate_matches_oracle_and_eos(ggc, orc, ctx):
     # EOS ends the loop before the id is emitted
     e = Engine(ggc.LlamaModel(hp, ts, max_ctx=256, ctx=ctx), encode, sampler=s, seed=5, eos=a[3])
     assert e.generate(prompt, 16) == a[:3]
+
+
+def test_generate_top_k_0_samples_on_the_host(ggc, orc, ctx):
+    """top_k = 0 keeps the whole vocabulary (151936 candidates): the engine reads
+    the logits back and samples on the host; same ids as the oracle's loop."""
+    hp, ts = synth.make_model("qwen2-0.5b-q8_0", n_layers=2, seed=13)
+    s = dict(temperature=40.0, top_k=0, top_p=0.9, repeat_penalty=1.1)
+    dev = Engine(ggc.LlamaModel(hp, ts, max_ctx=256, ctx=ctx), encode, sampler=s, seed=7)
+    ref = Engine(OracleModel(orc, hp, ts), encode, sampler=s, seed=7)
+    assert dev.host_sampling
+    prompt = encode("a prompt for the host sampler")
+    assert dev.generate(prompt, 12) == ref.generate(prompt, 12)

@@ -7,6 +7,7 @@ import struct
 import numpy as np
 import pytest
 
+import gguf_cuda as ggc
 from gguf_cuda import loader, synth
 from gguf_cuda.loader import (T_ARR, T_BOOL, T_F32, T_F64, T_I8, T_I16, T_I32, T_I64, T_STR, T_U8, T_U16, T_U32,
                               T_U64)
@@ -101,7 +102,7 @@ def test_reader_edge_cases():
         _open(_header(1, 0) + tensor(b"neg", [-5, 3], F32))
     f = _open(_header(1, 0) + tensor(b"z", [2, 2], 99))                  # unknown dtype: parses ...
     assert f.tensors[0].dtype == 99
-    with pytest.raises(loader.GgufFormatError, match="unknown dtype 99"):  # ... and fails when sized
+    with pytest.raises(ggc.InferenceError, match="unknown dtype 99"):    # ... and fails when sized (tensor.rs:64-80)
         f.tensors[0].data_size()
     kvs = b"".join(_gstr(k) + struct.pack("<iI", T_U32, i) for i, k in enumerate([b"first", b"second", b"third"]))
     assert list(_open(_header(0, 3) + kvs).kv) == ["first", "second", "third"]   # KV order kept
@@ -132,6 +133,27 @@ def test_reader_counts_dims_and_alignment():
     assert _open(_header(0, 1) + zero).alignment == 32                   # alignment 0 falls back
 
 
+def test_alignment_only_from_u32_and_first_occurrence_wins():
+    """file.rs:166-174 takes general.alignment only from a U32 value and stops at
+    the first such key; get / find_tensor return the first occurrence (file.rs:367-374)."""
+    def tensor(name, dims, offset):
+        return _gstr(name) + struct.pack("<I", len(dims)) + struct.pack(f"<{len(dims)}q", *dims) + \
+            struct.pack("<iQ", F32, offset)
+
+    one = tensor(b"a", [10], 0)
+    u64 = _gstr(b"general.alignment") + struct.pack("<iQ", T_U64, 64)
+    assert _open(_header(1, 1) + u64 + one + bytes(128)).alignment == 32          # U64: ignored
+    st = _gstr(b"general.alignment") + struct.pack("<i", T_STR) + _gstr(b"64")
+    assert _open(_header(1, 1) + st + one + bytes(128)).alignment == 32           # string: ignored
+    u32 = _gstr(b"general.alignment") + struct.pack("<iI", T_U32, 16)
+    f = _open(_header(0, 2) + u64 + u32)                                           # the first key decides
+    assert f.alignment == 32 and f.kv["general.alignment"] == 64
+    dup = _gstr(b"k") + struct.pack("<iI", T_U32, 1) + _gstr(b"k") + struct.pack("<iI", T_U32, 2)
+    assert _open(_header(0, 2) + dup).kv["k"] == 1
+    f = _open(_header(2, 0) + tensor(b"w", [8], 0) + tensor(b"w", [8], 32) + bytes(128))
+    assert f.find_tensor("w").offset == 0
+
+
 def test_tensor_sizes():   # src/tensor.rs tests: element counts (saturating) and block data sizes
     T = loader.TensorInfo
     assert T("t", [0, 5], F32, 0).num_elements() == 0 and T("s", [], F32, 0).num_elements() == 1
@@ -141,8 +163,9 @@ def test_tensor_sizes():   # src/tensor.rs tests: element counts (saturating) an
     assert T("t", [1024], Q8_0, 0).data_size() == 32 * 34
     assert T("t", [4096, 4096], Q4_K, 0).data_size() == 65536 * 144
     assert T("t", [256], 15, 0).data_size() == 292                       # Q8_K
-    with pytest.raises(loader.GgufFormatError, match="multiple"):
+    with pytest.raises(ggc.InvalidTensorShape, match="multiple") as e:   # InvalidTensorShape {name, elements, block}
         T("bad", [33], Q4_0, 0).data_size()
+    assert e.value.elements == 33 and e.value.block == 32
 
 
 def test_open_errors_and_missing_ffn_length(tmp_path):

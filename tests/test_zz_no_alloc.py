@@ -1,6 +1,7 @@
 """ggc_quant_matvec_static -- the allocation-free entry point (scratch in a
-file-scope device array) -- against the existing ggc_quant_matvec entry, both
-called through the C ABI on the same device buffers.
+file-scope device array) -- against the oracle's quant_matvec (the reference's
+quant.rs:526-570) and against the existing ggc_quant_matvec entry, both called
+through the C ABI on the same device buffers.
 
 Kept in its own file, collected last, so it runs both alone and after every
 other GPU test in the same process (the static scratch then has seen earlier
@@ -57,11 +58,12 @@ def call_static(lib, dt, dw, rows, cols, dx, dy, stream):
 
 
 @pytest.mark.parametrize("case", CASES, ids=lambda c: f"{DTYPE_NAMES[c[0]]}-{c[1]}x{c[2]}")
-def test_static_matches_existing_entry_twice(ggc, ctx, case):
+def test_static_matches_oracle_and_existing_entry_twice(ggc, orc, ctx, case):
     import torch
     dt, rows, cols = case
     lib = ggc.lib()
     dw, dx = device_case(dt, rows, cols, 91)
+    want_orc = orc.quant_matvec(dw.cpu().numpy(), dt, rows, cols, dx.cpu().numpy())
     y_ref = torch.zeros(rows, dtype=torch.float32, device="cuda")
     torch.cuda.synchronize()
     ggc._lib.check(lib.ggc_quant_matvec(ctx.h, dt, dw.data_ptr(), dw.numel(), rows, cols, dx.data_ptr(),
@@ -79,6 +81,7 @@ def test_static_matches_existing_entry_twice(ggc, ctx, case):
         got.append(y.cpu().numpy())
     for g in got:
         assert np.all(np.isfinite(g))
+        assert rel_l2(g, want_orc) <= REL_L2, (rel_l2(g, want_orc), DTYPE_NAMES[dt])
         assert rel_l2(g, want) <= REL_L2, (rel_l2(g, want), DTYPE_NAMES[dt])
     assert np.array_equal(got[0], got[1])    # fixed split order: deterministic
 
