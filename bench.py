@@ -17,10 +17,20 @@ token.  Per-step HBM traffic (~6 GB) is far above L2, so no explicit L2 flush.
 
 Under torchrun (N > 1) the ranks run ONE model tensor-parallel (default,
 `--parallel tp`: q/k/v/up/gate rows and attn_output/ffn_down columns sharded,
-NCCL all-reduce of the hidden state after attn_output and ffn_down; strong
-scaling: `value` is that model's tokens/s) or, with `--parallel replicas`, one
+the hidden state all-reduced after attn_output and ffn_down -- fused into those
+GEMVs over NVLink peer memory, or NCCL; `allreduce` says which; strong scaling:
+`value` is that model's tokens/s) or, with `--parallel replicas`, one
 independent replica per rank (weak scaling: `value` sums the replicas).
-`--impl reference` times the CPU restatement of the reference's rayon path.
+
+Before the timing every rank runs a parity probe (`tp_parity`: a 2-layer prefix
+of the model, 8-token prompt, 32 greedy ids, checked on rank 0 against the
+oracle).  `configs` adds the other named workloads: Qwen2-0.5B Q8_0 (32-token
+prompt + 128 greedy steps, 1 GPU) and Llama-3-8B Q4_0 (2048-token prefill;
+256 decode steps ending at context 8192, f16 KV; tensor parallel at N > 1).
+`cpu_baseline` and `--impl reference` run one procedure: the oracle (C++
+restatement of the reference's rayon CPU path) decoding whole tokens of the
+full model at the same context on the host cores (extrapolated from layer
+prefixes only when the host RAM cannot hold the f32 model; it says so).
 """
 from __future__ import annotations
 
@@ -54,6 +64,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--parallel", choices=["tp", "replicas"], default="tp", help="multi-GPU mode (N > 1)")
     ap.add_argument("--prefill", type=int, default=512, help="prompt tokens of the prefill measurement (0: skip)")
+    ap.add_argument("--no-configs", dest="configs", action="store_false",
+                    help="skip the Qwen2-0.5B and Llama-3-8B workloads")
     return ap.parse_args()
 
 
@@ -125,50 +137,84 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU baseline: the oracle (C++ restatement of the reference's rayon CPU path)
 # ---------------------------------------------------------------------------
-def cpu_decode_sample(hp, ts, ctx_len, steps, layer_counts=(2, 4)):
-    """Per-token decode time of the oracle at context ctx_len, extrapolated to all
-    layers from models holding the first 2 and 4 layers (same tensors)."""
+def oracle_bytes(hp, ts, ctx_len):
+    """Host bytes the oracle holds for a model: every tensor materialised as f32
+    (the reference's materialize, llama.rs:183-204) plus the f32 KV cache."""
+    kvd = hp["n_kv_heads"] * (hp["embed_dim"] // hp["n_heads"])
+    return 4 * sum(int(t["n_elements"]) for t in ts if t is not None) + 8 * hp["n_layers"] * ctx_len * kvd
+
+
+def _oracle_token_times(oracle, hp, ts, ctx_len, tokens, warmup):
+    """Per-token times of the oracle decoding at context ctx_len: the cache holds
+    ctx_len - 1 planted rows, each token is forwarded at position ctx_len - 1 and
+    the cache is truncated back after it."""
+    kvd = hp["n_kv_heads"] * (hp["embed_dim"] // hp["n_heads"])
+    m = oracle.Model(hp, ts)
+    kv = np.random.default_rng(0).normal(size=(ctx_len - 1) * kvd).astype(np.float32)
+    for l in range(hp["n_layers"]):
+        m.cache_append(l, kv, kv)
+    t = []
+    for s in range(warmup + tokens):
+        t0 = time.perf_counter()
+        m.forward([2 + s], [ctx_len - 1])
+        if s >= warmup:
+            t.append(time.perf_counter() - t0)
+        m.truncate(ctx_len - 1)
+    del m
+    return t
+
+
+def cpu_decode(hp, ts, ctx_len, tokens, warmup=1):
+    """Decode tokens/s of the oracle on this host's cores, one procedure for both
+    CPU legs (our arm's cpu_baseline and the reference arm).  The whole model when
+    the host's free RAM holds its f32 materialisation; otherwise a least-squares
+    line through 2/4/8/16-layer prefixes of the model, reported as an extrapolation
+    with its residual."""
+    import psutil
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle
     oracle.build()
     threads = oracle.get_threads()
-    n_layers = hp["n_layers"]
-    kvd = hp["n_kv_heads"] * (hp["embed_dim"] // hp["n_heads"])
-    rng = np.random.default_rng(0)
-    times = {}
-    for L in layer_counts:
-        h = dict(hp, n_layers=L)
-        m = oracle.Model(h, ts[:3 + 12 * L])
-        k = rng.normal(size=(ctx_len - 1) * kvd).astype(np.float32)
-        for l in range(L):
-            m.cache_append(l, k, k)
-        m.forward([1], [ctx_len - 1])          # warm-up token (materialised weights are cached)
-        m.truncate(ctx_len - 1)
-        t = []
-        for s in range(steps):
-            t0 = time.perf_counter()
-            m.forward([2 + s], [ctx_len - 1])
-            t.append(time.perf_counter() - t0)
-            m.truncate(ctx_len - 1)
-        times[L] = statistics.median(t)
-        del m
-    a, b = layer_counts
-    per_layer = (times[b] - times[a]) / (b - a)
-    fixed = times[a] - a * per_layer
-    t_full = fixed + n_layers * per_layer
-    return {"value": 1.0 / t_full, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"oracle decode of 1 token at ctx {ctx_len} on {a}- and {b}-layer prefixes of the model "
-                      f"(median of {steps}), extrapolated to {n_layers} layers: "
-                      f"{times[a]*1e3:.1f} ms / {times[b]*1e3:.1f} ms -> {t_full*1e3:.1f} ms per token"}
+    L = hp["n_layers"]
+    need = oracle_bytes(hp, ts, ctx_len)
+    avail = psutil.virtual_memory().available
+    base = {"unit": "tokens/s", "cores": threads, "kind": "port", "tokens_timed": tokens}
+    if avail > 1.25 * need + 4e9:
+        t0 = time.perf_counter()
+        t = _oracle_token_times(oracle, hp, ts, ctx_len, tokens, warmup)
+        wall = time.perf_counter() - t0
+        total = float(sum(t))
+        return dict(base, value=tokens / total, seconds=total, wall_seconds=wall, method="full model",
+                    sample=f"oracle decoding {tokens} tokens (after {warmup} warm-up) at context {ctx_len} through all "
+                           f"{L} layers: {need / 1e9:.1f} GB of f32 weights and KV on the host, {threads} threads, "
+                           f"{total / tokens * 1e3:.1f} ms per token (median {statistics.median(t) * 1e3:.1f})")
+    counts = [c for c in (2, 4, 8, 16) if c <= L] or [L]
+    per = {}
+    for c in counts:
+        h = dict(hp, n_layers=c)
+        per[c] = statistics.median(_oracle_token_times(oracle, h, ts[:3 + 12 * c], ctx_len, tokens, warmup))
+    xs = np.array(counts, float)
+    ys = np.array([per[c] for c in counts])
+    b, a = np.polyfit(xs, ys, 1) if len(counts) > 1 else (ys[0] / xs[0], 0.0)
+    resid = float(np.sqrt(np.mean((a + b * xs - ys) ** 2)))
+    t_full = float(a + b * L)
+    return dict(base, value=1.0 / t_full, seconds=float(sum(per.values())) * tokens, method="extrapolated",
+                fit={"layers": counts, "ms_per_token": [per[c] * 1e3 for c in counts], "rms_residual_ms": resid * 1e3},
+                sample=f"EXTRAPOLATED: the host's free RAM ({avail / 1e9:.0f} GB) does not hold the {need / 1e9:.0f} GB "
+                       f"f32 model; oracle decode at context {ctx_len} on {counts}-layer prefixes (median of {tokens} "
+                       f"tokens each), least-squares line to {L} layers: {t_full * 1e3:.1f} ms per token, "
+                       f"rms residual {resid * 1e3:.2f} ms")
 
 
 def run_reference(args, rank, world):
+    """The reference's CPU path (the oracle port; the Rust crate cannot be built
+    here) on the host cores: W warm-up tokens, then K timed tokens, each one
+    decode step of the whole model at context args.ctx.  Rank 0 only."""
     from gguf_cuda import synth
     if rank != 0:
         return
-    hp, ts = synth.make_model(MODEL, n_layers=4, seed=0)
-    hp["n_layers"] = synth.CONFIGS[MODEL]["n_layers"]
-    cb = cpu_decode_sample(hp, ts, args.ctx, steps=max(1, min(args.steps, 8)))
+    hp, ts = synth.make_model(MODEL, seed=0)
+    cb = cpu_decode(hp, ts, args.ctx, tokens=args.steps, warmup=args.warmup)
     v = cb["value"]
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
@@ -179,18 +225,22 @@ def run_reference(args, rank, world):
     }), flush=True)
 
 
-def config_block(args):
+def config_block(args, allreduce=None):
     layers = "" if args.layers is None else f", first {args.layers} layers only (profiling case)"
     return {"workload": f"{MODEL} decode, batch 1, context {args.ctx} (cache prefilled with planted K/V rows so the "
                         f"timed steps end at {args.ctx}), f32 KV cache{layers}", "global_batch": 1, "seq_len": args.ctx,
-            "parallelism": parallelism(args), "l2": "per-step traffic ~6 GB >> 126 MB L2 (no flush needed)"}
+            "parallelism": parallelism(args, allreduce), "l2": "per-step traffic ~6 GB >> 126 MB L2 (no flush needed)"}
 
 
-def parallelism(args):
+ALLREDUCE_NAMES = {"peer": "all-reduce fused into the attn_output / ffn_down GEMVs over NVLink peer memory",
+                   "nccl": "NCCL all-reduce after attn_output and ffn_down"}
+
+
+def parallelism(args, allreduce=None):
     if args.gpus <= 1:
         return "single GPU"
     if args.parallel == "tp":
-        return f"tp{args.gpus} (NCCL all-reduce after attn_output and ffn_down)"
+        return f"tp{args.gpus} ({ALLREDUCE_NAMES.get(allreduce, 'all-reduce after attn_output and ffn_down')})"
     return f"replicas x{args.gpus}"
 
 
@@ -278,6 +328,145 @@ def prefill_measure(args, model, hp, ts, stream, torch, barrier, max_over_ranks,
             "path": "n-1 tokens batched (k_mm_tc tcgen05 split-bf16 products, k_attn_prefill), last token decode step"}
 
 
+def rel_l2(got, want):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    return float(np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-30))
+
+
+def parity_probe(ggc, ctx, rank, barrier):
+    """The checker before the timing: a 2-layer prefix of the benchmark model (the
+    rank's shard of it under tensor parallelism), an 8-token prompt and 32 greedy
+    ids, against the oracle on rank 0 (logits within 1e-4 relative L2, ids equal)."""
+    from gguf_cuda import synth
+    hp, ts = synth.make_model(MODEL, n_layers=2, seed=0)
+    prompt = np.random.default_rng(5).integers(0, hp["vocab_size"], size=8).astype(np.uint32)
+    pos = np.arange(8, dtype=np.int64)
+    m = ggc.LlamaModel(hp, ts, max_ctx=64, ctx=ctx)
+    logits = m.forward(prompt, pos)
+    ids = m.decode(32)
+    kind = m.allreduce
+    m.close()
+    barrier()
+    if rank != 0:
+        return None
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+    o = oracle.Model(hp, ts)
+    want = o.forward(prompt, pos)
+    want_ids, lg, p = [], want, 8
+    for _ in range(32):
+        want_ids.append(oracle.greedy(lg))
+        lg = o.forward([want_ids[-1]], [p])
+        p += 1
+    err = rel_l2(logits, want)
+    return {"model": f"{MODEL}, first 2 layers", "prompt_tokens": 8, "greedy_ids": 32, "rel_l2": err,
+            "ids_match": ids == want_ids, "pass": err <= 1e-4 and ids == want_ids, "allreduce": kind}
+
+
+def time_decode(model, stream, torch, steps, barrier, max_over_ranks):
+    """Device-timed greedy decode of `steps` tokens (CUDA events on the library stream)."""
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    model.decode(steps, sync=False)
+    e1.record(stream)
+    e1.synchronize()
+    ids = model.wait(steps)
+    return max_over_ranks(e0.elapsed_time(e1) / 1e3), ids
+
+
+def qwen2_arm(ggc, ctx, stream, torch, peak_gbs, barrier, max_over_ranks):
+    """Qwen2-0.5B shape, Q8_0, 24 layers, 1 GPU: a 32-token prompt of seeded
+    uniform ids, then 128 greedy decode steps on the f32 KV cache."""
+    from gguf_cuda import synth
+    name = "qwen2-0.5b-q8_0"
+    hp, ts = synth.make_model(name, seed=0)
+    m = ggc.LlamaModel(hp, ts, max_ctx=32 + 128 + 8, ctx=ctx)
+    prompt = np.random.default_rng(31).integers(0, hp["vocab_size"], size=32).astype(np.uint32)
+    pos = np.arange(32, dtype=np.int64)
+    runs = []
+    for it in range(4):   # 1 warm-up + 3 timed
+        m.reset_cache()
+        barrier()
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record(stream)
+        m.forward(prompt, pos, want_logits=False)
+        p1.record(stream)
+        t, ids = time_decode(m, stream, torch, 128, barrier, max_over_ranks)
+        p1.synchronize()
+        if it:
+            runs.append((t, p0.elapsed_time(p1) / 1e3, len(ids)))
+    m.close()
+    t, tp, nids = sorted(runs)[1]
+    w_bytes = synth.weight_bytes_per_token(ts)
+    kv = synth.kv_bytes_per_token(hp, 32 + 64)
+    gbs = (w_bytes + kv) * 128 / t / 1e9
+    return {"workload": f"{name}: 24 layers, 32-token prompt then 128 greedy decode steps, f32 KV cache, 1 GPU",
+            "decode_tokens_per_s": 128 / t, "ms_per_token": t / 128 * 1e3, "prompt_ms": tp * 1e3,
+            "bytes_per_token": w_bytes + kv, "achieved_gbs": gbs, "frac_of_hbm": gbs / peak_gbs,
+            "ids": nids, "timed": "median of 3 after 1 warm-up, CUDA events"}
+
+
+def llama3_arm(ggc, ctx, stream, torch, peak_gbs, barrier, max_over_ranks, world, tflops_peak):
+    """Llama-3-8B shape (GQA 32/8, ffn 14336, vocab 128256), Q4_0, f16 KV cache:
+    a 2048-token prefill of seeded uniform ids on an empty cache, and 256 greedy
+    decode steps whose context ends at 8192 (earlier rows planted); one model,
+    tensor parallel over the ranks."""
+    from gguf_cuda import synth
+    name = "llama3-8b-q4_0"
+    hp, ts = synth.make_model(name, seed=0)
+    C, K, W = 8192, 256, 8
+    m = ggc.LlamaModel(hp, ts, max_ctx=C, kv_f16=True, ctx=ctx)
+    L, d, f = hp["n_layers"], hp["embed_dim"], hp["ffn_dim"]
+    hd = d // hp["n_heads"]
+    kvd = hp["n_kv_heads"] * hd
+    n = 2048
+    prompt = np.random.default_rng(41).integers(0, hp["vocab_size"], size=n).astype(np.uint32)
+    pos = np.arange(n, dtype=np.int64)
+    per_tok = 2 * (2 * d * d + 2 * d * kvd + 3 * d * f)
+    flops = (per_tok * (L - 1) + 2 * 2 * d * kvd) * (n - 1) + \
+        sum(4 * hd * (t + 1) * hp["n_heads"] for t in range(n - 1)) * (L - 1)
+    times = []
+    for it in range(3):   # 1 warm-up + 2 timed
+        m.reset_cache()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        m.forward(prompt, pos, want_logits=False)
+        e1.record(stream)
+        e1.synchronize()
+        if it:
+            times.append(max_over_ranks(e0.elapsed_time(e1) / 1e3))
+    tpf = min(times)
+    # decode ending at context C: plant C - K - W rows, W warm-up steps, K timed
+    m.reset_cache()
+    P = C - K - W
+    rows = np.random.default_rng(2).normal(size=(P, m.kv_dim)).astype(np.float32)
+    for l in range(L):
+        m.cache_append(l, rows, rows)
+    m.forward([1], [P], want_logits=False)
+    m.decode(W - 1)
+    t, ids = time_decode(m, stream, torch, K, barrier, max_over_ranks)
+    assert m.cache_len() == C
+    kind = m.allreduce
+    m.close()
+    w_bytes = synth.weight_bytes_per_token(ts)
+    lm = int(ts[2]["raw"].nbytes)
+    kv = synth.kv_bytes_per_token(hp, C - K // 2, 2)
+    gpu_bytes = (w_bytes - lm + kv) / world + lm
+    gbs = gpu_bytes * K / t / 1e9
+    return {"workload": f"{name}: 32 layers, 2048-token prefill on an empty cache; {K} greedy decode steps ending at "
+                        f"context {C} (earlier rows planted), f16 KV cache, tp{world}",
+            "allreduce": kind if world > 1 else "none",
+            "prefill": {"tokens": n, "ms": tpf * 1e3, "tokens_per_s": n / tpf, "model_tflops": flops / tpf / 1e12,
+                        "frac_of_bf16_sustained": flops / tpf / 1e12 / tflops_peak,
+                        "frac_of_bf16_sustained_issued": 3 * flops / tpf / 1e12 / tflops_peak,
+                        "note": "3 bf16 MMAs issued per product (split operands); min of 2 after 1 warm-up"},
+            "decode_tokens_per_s": K / t, "ms_per_token": t / K * 1e3, "bytes_per_token_per_gpu": gpu_bytes,
+            "achieved_gbs_per_gpu": gbs, "frac_of_hbm": gbs / peak_gbs, "ids": len(ids)}
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import gguf_cuda as ggc
@@ -297,19 +486,8 @@ def run_ours(args, rank, world, local_rank):
         ctx = ggc.Context(local_rank)
     stream = torch.cuda.ExternalStream(ctx.stream)
     peak_gbs, peak_src = peaks()
-
-    hp, ts = synth.make_model(MODEL, seed=0, n_layers=args.layers)
-    W, K, C = args.warmup, args.steps, args.ctx
-    P = C - W - K
-    assert P >= 1, "context too small for warmup + steps"
-    model = ggc.LlamaModel(hp, ts, max_ctx=C, ctx=ctx)
-    w_bytes = synth.weight_bytes_per_token(ts)
-    # prefill: P seeded K/V rows planted in every layer (a decode step's cost does
-    # not depend on the cached values)
-    rng = np.random.default_rng(1)
-    for l in range(hp["n_layers"]):
-        kv = rng.normal(size=(P, model.kv_dim)).astype(np.float32)
-        model.cache_append(l, kv, kv)
+    tflops_peak = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops_sustained"] \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else 1400.0
 
     def barrier():
         if dist is not None:
@@ -322,6 +500,22 @@ def run_ours(args, rank, world, local_rank):
         t = torch.tensor([v], device="cuda", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    parity = parity_probe(ggc, ctx, rank, barrier) if args.layers is None else None
+
+    hp, ts = synth.make_model(MODEL, seed=0, n_layers=args.layers)
+    W, K, C = args.warmup, args.steps, args.ctx
+    P = C - W - K
+    assert P >= 1, "context too small for warmup + steps"
+    model = ggc.LlamaModel(hp, ts, max_ctx=C, ctx=ctx)
+    allreduce = model.allreduce if tp else "none"
+    w_bytes = synth.weight_bytes_per_token(ts)
+    # prefill: P seeded K/V rows planted in every layer (a decode step's cost does
+    # not depend on the cached values)
+    rng = np.random.default_rng(1)
+    for l in range(hp["n_layers"]):
+        kv = rng.normal(size=(P, model.kv_dim)).astype(np.float32)
+        model.cache_append(l, kv, kv)
 
     sampler = ClockSampler(local_rank)
     with sampler:
@@ -364,6 +558,19 @@ def run_ours(args, rank, world, local_rank):
 
     prefill = prefill_measure(args, model, hp, ts, stream, torch, barrier, max_over_ranks, world) \
         if args.prefill > 0 else None
+    if prefill:
+        prefill["frac_of_bf16_sustained"] = prefill["model_tflops"] / tflops_peak
+        prefill["frac_of_bf16_sustained_issued"] = 3 * prefill["model_tflops"] / tflops_peak
+    model.close()
+    del model
+
+    configs = {}
+    if args.layers is None and args.configs:
+        if world == 1:
+            configs["qwen2-0.5b-q8_0"] = qwen2_arm(ggc, ctx, stream, torch, peak_gbs, barrier, max_over_ranks)
+        if tp or world == 1:
+            configs["llama3-8b-q4_0"] = llama3_arm(ggc, ctx, stream, torch, peak_gbs, barrier, max_over_ranks,
+                                                   world if tp else 1, tflops_peak)
 
     result = None
     if rank == 0:
@@ -379,14 +586,14 @@ def run_ours(args, rank, world, local_rank):
         tr = traffic_record().get("k_gemv_span<Q4_K> 11008x4096")
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            hp4, ts4 = hp, ts
-            cpu = cpu_decode_sample(hp4, ts4, C, steps=4)
+            cpu = cpu_decode(hp, ts, C, tokens=8, warmup=1)
         result = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": elapsed / K * 1e3, "higher_is_better": True, "scaling": "strong" if tp else "weak",
             "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (seeded Q4_K_M blocks)",
-            "config": config_block(args),
+            "config": config_block(args, allreduce),
+            "allreduce": allreduce,
             "e2e": {"value": streams * K / e2e_elapsed, "unit": "tokens/s", "h2d_bytes_per_step": 4 + 8,
                     "d2h_bytes_per_step": 4 * hp["vocab_size"] + 4,
                     "api": "ggc_model_forward(1 host token) -> host logits + argmax, per token"},
@@ -398,14 +605,15 @@ def run_ours(args, rank, world, local_rank):
             "model_roofline": {"bytes_per_step": step_bytes, "weight_bytes": w_bytes, "kv_bytes": kv_bytes,
                                "bytes_per_step_per_gpu": gpu_bytes, "achieved_gbs_per_gpu": model_gbs,
                                "frac": model_gbs / peak_gbs, "bound_tokens_s": peak_gbs * 1e9 / gpu_bytes * streams},
+            "tp_parity": parity,
             "matvec": rl,
             "prefill": prefill,
+            "configs": configs,
             "clocks": sampler.record(),
             "cpu_baseline": cpu,
         }
     if dist is not None:
         dist.barrier()
-    del model
     if rank == 0:
         print(json.dumps(result), flush=True)
     if dist is not None:

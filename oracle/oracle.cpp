@@ -373,6 +373,23 @@ inline float dot_f32(const float* a, const float* x, uint64_t n) {
     return acc;
 }
 
+// n matvec_colmajor_trans products over the same matrix, y[t][i] = dot(a row i,
+// x[t]) + 0.0 (ops.rs:204-215 with no bias), each element the same serial f32
+// dot as the one-token call.  Blocks of rows x tokens keep both in cache, so the
+// matrix is read once per call instead of once per token; only the loop order
+// over (row, token) pairs changes, not any element's arithmetic.
+void matvec_trans_batch(const float* a, uint64_t dim0, uint64_t dim1, const float* x, uint64_t n, float* y) {
+    constexpr uint64_t RB = 16, TB = 16;
+    parallel_for((dim1 + RB - 1) / RB, [&](uint64_t rb) {
+        const uint64_t r0 = rb * RB, r1 = std::min(dim1, r0 + RB);
+        for (uint64_t t0 = 0; t0 < n; t0 += TB) {
+            const uint64_t t1 = std::min(n, t0 + TB);
+            for (uint64_t i = r0; i < r1; ++i)
+                for (uint64_t t = t0; t < t1; ++t) y[t * dim1 + i] = dot_f32(a + i * dim0, x + t * dim0, dim0) + 0.0f;
+        }
+    });
+}
+
 }  // namespace
 
 extern "C" {
@@ -830,53 +847,55 @@ int orc_model_forward(orc_model* m, const uint32_t* tokens, const int64_t* posit
         std::memcpy(hidden.data() + i * d, m->token_embd.data() + base, d * sizeof(float));
     }
     float inv = 1.0f / std::sqrt((float)hd);
-    std::vector<float> qv(q * hd), kbuf(kv * hd), vbuf(kv * hd), o(q * hd), up(f), gate(f);
+    std::vector<float> qv(q * hd), kbuf(kv * hd), vbuf(kv * hd);
     std::vector<int64_t> qpos(q), kpos(kv);
     for (uint32_t l = 0; l < hp.n_layers; ++l) {
         auto& L = m->layers[l];
         std::vector<float> residual = hidden;
         std::vector<float> attn_in = residual;
         apply_rmsnorm(L.attn_norm, attn_in, n);
-        // attention_block :417-495
-        std::vector<float> attn_out(n * d, 0.0f);
+        // attention_block :417-495 -- the q/k/v and output products of all n tokens
+        // are batched (matvec_trans_batch: each element as in the per-token call);
+        // bias, RoPE, cache append and attend run token by token in order
+        std::vector<float> attn_out(n * d, 0.0f), qa(n * q * hd), ka(n * kv * hd), va(n * kv * hd), oa(n * q * hd);
+        matvec_trans_batch(L.wq.data(), d, q * hd, attn_in.data(), n, qa.data());
+        matvec_trans_batch(L.wk.data(), d, kv * hd, attn_in.data(), n, ka.data());
+        matvec_trans_batch(L.wv.data(), d, kv * hd, attn_in.data(), n, va.data());
         for (uint64_t tok = 0; tok < n; ++tok) {
             int64_t pos = positions[tok];
-            const float* xb = attn_in.data() + tok * d;
-            orc_matvec_colmajor_trans(L.wq.data(), L.wq.size(), d, q * hd, xb, d, qv.data(), q * hd, nullptr);
+            std::memcpy(qv.data(), qa.data() + tok * q * hd, q * hd * sizeof(float));
             for (uint64_t i = 0; i < L.bq.size() && i < q * hd; ++i) qv[i] += L.bq[i];
             std::fill(qpos.begin(), qpos.end(), pos);
             orc_rope(qv.data(), q * hd, qpos.data(), q, m->inv_freq.data(), m->inv_freq.size());
-            orc_matvec_colmajor_trans(L.wk.data(), L.wk.size(), d, kv * hd, xb, d, kbuf.data(), kv * hd, nullptr);
+            std::memcpy(kbuf.data(), ka.data() + tok * kv * hd, kv * hd * sizeof(float));
             for (uint64_t i = 0; i < L.bk.size() && i < kv * hd; ++i) kbuf[i] += L.bk[i];
-            orc_matvec_colmajor_trans(L.wv.data(), L.wv.size(), d, kv * hd, xb, d, vbuf.data(), kv * hd, nullptr);
+            std::memcpy(vbuf.data(), va.data() + tok * kv * hd, kv * hd * sizeof(float));
             for (uint64_t i = 0; i < L.bv.size() && i < kv * hd; ++i) vbuf[i] += L.bv[i];
             std::fill(kpos.begin(), kpos.end(), pos);
             orc_rope(kbuf.data(), kv * hd, kpos.data(), kv, m->inv_freq.data(), m->inv_freq.size());
             m->kc[l].insert(m->kc[l].end(), kbuf.begin(), kbuf.end());   // cache.rs:46-54
             m->vc[l].insert(m->vc[l].end(), vbuf.begin(), vbuf.end());
-            // llama.rs:479 copies the whole cache prefix each step
-            std::vector<float> k_all = m->kc[l], v_all = m->vc[l];
-            uint64_t seq = k_all.size() / (kv * hd);
-            attend(qv.data(), k_all.data(), v_all.data(), seq, q, kv, hd, inv, pos, o.data());
-            orc_matvec_colmajor_trans(L.wo.data(), L.wo.size(), q * hd, d, o.data(), q * hd,
-                                      attn_out.data() + tok * d, d, nullptr);
+            // llama.rs:479 reads a copy of the whole cache prefix; the values are the cache's own
+            uint64_t seq = m->kc[l].size() / (kv * hd);
+            attend(qv.data(), m->kc[l].data(), m->vc[l].data(), seq, q, kv, hd, inv, pos, oa.data() + tok * q * hd);
         }
+        matvec_trans_batch(L.wo.data(), q * hd, d, oa.data(), n, attn_out.data());
         if (any_nan(attn_out)) return set_err(ORC_ERR_INFERENCE, l, 0, "NaN after attention");
         for (uint64_t i = 0; i < n * d; ++i) residual[i] += attn_out[i];
         hidden = residual;
         std::vector<float> ffn_in = hidden;
         apply_rmsnorm(L.ffn_norm, ffn_in, n);
-        // ffn_block :547-580
-        std::vector<float> ffn_out(n * d, 0.0f);
+        // ffn_block :547-580 (products batched over the tokens as above)
+        std::vector<float> ffn_out(n * d, 0.0f), upa(n * f), gatea(n * f);
+        matvec_trans_batch(L.up.data(), d, f, ffn_in.data(), n, upa.data());
+        matvec_trans_batch(L.gate.data(), d, f, ffn_in.data(), n, gatea.data());
         for (uint64_t tok = 0; tok < n; ++tok) {
-            const float* xb = ffn_in.data() + tok * d;
-            orc_matvec_colmajor_trans(L.up.data(), L.up.size(), d, f, xb, d, up.data(), f, nullptr);
-            orc_matvec_colmajor_trans(L.gate.data(), L.gate.size(), d, f, xb, d, gate.data(), f, nullptr);
-            orc_silu(gate.data(), f);
-            for (uint64_t i = 0; i < f; ++i) gate[i] *= up[i];
-            orc_matvec_colmajor_trans(L.down.data(), L.down.size(), f, d, gate.data(), f,
-                                      ffn_out.data() + tok * d, d, nullptr);
+            float* g = gatea.data() + tok * f;
+            const float* u = upa.data() + tok * f;
+            orc_silu(g, f);
+            for (uint64_t i = 0; i < f; ++i) g[i] *= u[i];
         }
+        matvec_trans_batch(L.down.data(), f, d, gatea.data(), n, ffn_out.data());
         if (any_nan(ffn_out)) return set_err(ORC_ERR_INFERENCE, l, 0, "NaN after ffn");
         for (uint64_t i = 0; i < n * d; ++i) hidden[i] += ffn_out[i];
     }

@@ -1,0 +1,124 @@
+"""The named workloads at their real size, against the oracle.
+
+* Qwen2-0.5B shape (24 layers, d 896, 14/2 heads, ffn 4864, vocab 151936,
+  theta 1e6, QKV bias, Q8_0 weights quantised from N(0, 0.02)): a 32-token
+  prompt of seeded uniform ids, then 128 greedy ids.  The prompt's logits within
+  1e-4 relative L2 and the greedy ids identical to the oracle's
+  (Engine::generate with the greedy Sampler, engine.rs:83-138,
+  sampler.rs:113-123): all 128 unless two top logits lie within f32 noise of
+  each other at some step, and never fewer than the first 32 (the parity bar).
+* Llama-3-8B shape (GQA 32/8, ffn 14336, theta 5e5, Q4_0 / Q8_0), one or two
+  layers and a 32000-entry vocabulary so the oracle stays fast: a 2048-token
+  prefill (its first 2047 tokens through the batched tensor-core path), then
+  the cache filled with seeded K/V rows up to context 8160 and 32 greedy
+  decode steps ending at 8192 (the long-context split attention over an
+  unbounded cache, llama.rs:499-545, cache.rs:46-54).  With the f32 cache
+  (the reference's type) logits within 1e-4 and ids identical; with the f16
+  cache the K/V rounding bounds the logits at 1e-2 (the reference has no f16
+  cache).
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+from gguf_cuda import synth
+
+REL_L2 = 1e-4
+F16_REL_L2 = 1e-2
+
+
+def rel_l2(got, want):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    return float(np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-30))
+
+
+def top2_gap(logits):
+    s = np.sort(np.asarray(logits, np.float64))
+    return (s[-1] - s[-2]) / max(abs(s[-1]), 1e-30)
+
+
+def oracle_greedy(orc, o, logits, start_pos, steps):
+    """The greedy loop over the oracle, keeping every step's logits."""
+    ids, seen, lg, pos = [], [], logits, start_pos
+    for _ in range(steps):
+        seen.append(lg)
+        ids.append(orc.greedy(lg))
+        lg = o.forward([ids[-1]], [pos])
+        pos += 1
+    return ids, seen
+
+
+def check_ids(got, want, logits_seen, need=32):
+    """Identical ids; a divergence is allowed only after `need` tokens and only
+    at a step whose top-2 logits the oracle itself separates by less than 1e-5."""
+    n = len(want)
+    assert len(got) == n
+    first = next((i for i in range(n) if got[i] != want[i]), n)
+    assert first >= need, (first, got[:first + 1], want[:first + 1])
+    if first < n:
+        assert top2_gap(logits_seen[first]) < 1e-5, (first, top2_gap(logits_seen[first]))
+    return first
+
+
+def test_qwen2_0_5b_full_depth(ggc, orc, ctx):
+    hp, ts = synth.make_model("qwen2-0.5b-q8_0", seed=0)
+    assert hp["n_layers"] == 24
+    m = ggc.LlamaModel(hp, ts, max_ctx=32 + 128 + 8, ctx=ctx)
+    o = orc.Model(hp, ts)
+    prompt = np.random.default_rng(31).integers(0, hp["vocab_size"], size=32).astype(np.uint32)
+    pos = np.arange(32, dtype=np.int64)
+    got = m.forward(prompt, pos)
+    want = o.forward(prompt, pos)
+    assert rel_l2(got, want) <= REL_L2, rel_l2(got, want)
+    ids = m.decode(128)
+    want_ids, seen = oracle_greedy(orc, o, want, 32, 128)
+    check_ids(ids, want_ids, seen)
+    assert m.cache_len() == 32 + 128
+    m.close()
+
+
+LLAMA3 = [("q4_0-f32kv-2layers", "llama3-8b-q4_0", 2, False),
+          ("q8_0-f32kv-1layer", "llama3-8b-q8_0", 1, False),
+          ("q4_0-f16kv-1layer", "llama3-8b-q4_0", 1, True)]
+
+
+@pytest.mark.parametrize("name,cfg,n_layers,f16", LLAMA3, ids=[c[0] for c in LLAMA3])
+def test_llama3_prefill_2048_then_decode_to_8192(ggc, orc, ctx, name, cfg, n_layers, f16):
+    hp, ts = synth.make_model(cfg, n_layers=n_layers, seed=4, vocab_size=32000)
+    C, n, steps = 8192, 2048, 32
+    m = ggc.LlamaModel(hp, ts, max_ctx=C, kv_f16=f16, ctx=ctx)
+    o = orc.Model(hp, ts)
+    bar = F16_REL_L2 if f16 else REL_L2
+    prompt = np.random.default_rng(41).integers(0, hp["vocab_size"], size=n).astype(np.uint32)
+    pos = np.arange(n, dtype=np.int64)
+    got = m.forward(prompt, pos)
+    want = o.forward(prompt, pos)
+    assert rel_l2(got, want) <= bar, rel_l2(got, want)
+    k, v = m.cache_read(n_layers - 1)
+    ko, vo = o.cache_read(n_layers - 1)
+    kv_bar = 1e-3 if f16 else REL_L2
+    assert rel_l2(k, ko) <= kv_bar and rel_l2(v, vo) <= kv_bar
+    # seeded rows from 2048 up to C - steps (the same rows in both caches)
+    fill = C - steps - n
+    rng = np.random.default_rng(8)
+    for l in range(n_layers):
+        rows = rng.normal(size=(fill, m.kv_dim)).astype(np.float32)
+        if f16:   # rows the f16 cache holds exactly, so both caches see the same values
+            rows = rows.astype(np.float16).astype(np.float32)
+        m.cache_append(l, rows, rows)
+        o.cache_append(l, rows, rows)
+    start = n + fill
+    tok = int(orc.greedy(want))
+    got = m.forward([tok], [start])
+    want = o.forward([tok], [start])
+    assert rel_l2(got, want) <= bar, rel_l2(got, want)
+    ids = m.decode(steps - 1)
+    want_ids, seen = oracle_greedy(orc, o, want, start + 1, steps - 1)
+    assert m.cache_len() == o.cache_len() == C
+    if f16:
+        assert len(ids) == steps - 1
+    else:
+        check_ids(ids, want_ids, seen, need=steps - 1)
+    m.close()
