@@ -281,7 +281,8 @@ SpanCfg make_span_cfg(uint32_t pcols, uint32_t total_rb, uint32_t ctas, size_t s
 // x of one GEMV into the span limb layout for every column tile: xl[ct][24][lane][4]
 // limb words and xfs[ct] (gs per lane, then [3][lane] float4 of x sums).  Run by the 256 consumer
 // threads (named barrier 1); activations are read through L2 (written by other
-// CTAs of a persistent grid).  `red`: GS_WARPS doubles, `s_scale`: one float.
+// CTAs of a persistent grid).  `red`: NWARPS doubles, `s_scale`: one float.  Run by
+// the NWARPS consumer warps (named barrier 1).
 // The prologue's input by value (kernel parameters cannot alias the stores the
 // prologue makes; fields read through a reference to global memory would be
 // re-loaded after each of them).
@@ -305,11 +306,93 @@ __device__ __forceinline__ float span_xval(const SpanX a, uint32_t e, float scal
     return x;
 }
 
-// Returns (thread 0) whether the RMSNorm sum of squares is NaN; the caller reports it.
+// The 16 x values of item `it` (span it / 8, quarter it % 8) of a GEMV input:
+// plain, ops::rmsnorm with `scale` (ops.rs:262-274) or silu(gate) * up.  Zero
+// past xcols and for dead items.
+__device__ __forceinline__ void span_item_load(const SpanX a, uint32_t it, bool live, float scale, float (&v)[16]) {
+    const uint32_t sp = it >> 3, q = it & 7;
+    const uint32_t e0 = sp * SPAN + 16 * q;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) v[k] = 0.f;
+    if (live && e0 + 16 <= a.xcols) {
+        const float4* x4 = reinterpret_cast<const float4*>(a.x + e0);
+        float4 xa[4], ya[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) xa[k] = __ldcg(x4 + k);
+        if (a.pro != PRO_PLAIN) {
+            const float4* y4 = reinterpret_cast<const float4*>(a.x2 + e0);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) ya[k] = __ldcg(y4 + k);
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float xx[4] = {xa[k].x, xa[k].y, xa[k].z, xa[k].w};
+            const float yy[4] = {ya[k].x, ya[k].y, ya[k].z, ya[k].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                v[4 * k + j] = a.pro == PRO_RMSNORM ? __fmul_rn(__fmul_rn(xx[j], scale), yy[j])   // ops.rs:272
+                             : a.pro == PRO_SWIGLU ? ffn_silu_mul(xx[j], yy[j])
+                             : xx[j];
+            }
+        }
+    } else if (live) {
+#pragma unroll
+        for (int k = 0; k < 16; ++k) v[k] = span_xval(a, e0 + k, scale);   // checks e < xcols
+    }
+}
+
+// Item `it`'s 16 values -> the span's power-of-two scale gs (max |x| of the span
+// below 2^22 gs), three 8-bit limb words per step in xl, and the quarter / half
+// sums in xfs.  Called by all 32 lanes of a warp together (the 8 quarters of a
+// span are 8 consecutive lanes).
 template <int DT>
-__device__ bool span_x_prologue(const SpanX a, uint32_t nct, uint32_t* xl, float* xfs, double* red, float* s_scale) {
+__device__ __forceinline__ void span_item_store(const float (&v)[16], uint32_t it, bool live, uint32_t* xl, float* xfs) {
     using F = SpanFmt<DT>;
-    constexpr uint32_t CT = GS_WARPS * 32;
+    const uint32_t sp = it >> 3, q = it & 7;
+    float mx = 0.f, sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) { mx = fmaxf(mx, fabsf(v[k])); sum += v[k]; }
+    bool finite = isfinite(mx) && isfinite(sum);
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        finite = __shfl_xor_sync(0xffffffffu, (int)finite, o) && finite;
+    }
+    const float pair = __shfl_xor_sync(0xffffffffu, sum, 1);   // the other quarter of the 32-element half
+    int ex = 0;
+    frexpf(mx, &ex);
+    const float mul = (mx > 0.f && finite) ? ldexpf(1.f, 22 - ex) : 0.f;
+    const float gs = !finite ? __int_as_float(0x7FC00000) : (mx > 0.f ? ldexpf(1.f, ex - 22) : 0.f);
+    if (live) {
+        const uint32_t ct = sp / SPAN_LANES, l = sp % SPAN_LANES;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const int s = F::step_of((int)q, t);
+            uint32_t w0 = 0, w1 = 0, w2 = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int xi = __float2int_rn(v[F::qoff(t, j)] * mul);
+                w0 |= (uint32_t)(xi & 0xFF) << (8 * j);
+                w1 |= (uint32_t)((xi >> 8) & 0xFF) << (8 * j);
+                w2 |= (uint32_t)((xi >> 16) & 0xFF) << (8 * j);
+            }
+            const uint32_t wi[3] = {(uint32_t)(3 * s), (uint32_t)(3 * s + 1), (uint32_t)(3 * s + 2)};
+            const uint32_t wv[3] = {w0, w1, w2};
+#pragma unroll
+            for (int k = 0; k < 3; ++k)
+                xl[(((size_t)ct * 24 + wi[k] / 4) * SPAN_LANES + l) * 4 + wi[k] % 4] = wv[k];
+        }
+        float* xc = xfs + (size_t)ct * GS_XF * SPAN_LANES;   // [gs x 32][3][32] float4
+        xc[SPAN_LANES + ((q >> 2) * SPAN_LANES + l) * 4 + (q & 3)] = sum;
+        if ((q & 1) == 0) xc[SPAN_LANES + (2 * SPAN_LANES + l) * 4 + (q >> 1)] = sum + pair;
+        if (q == 0) xc[l] = gs;
+    }
+}
+
+// Returns (thread 0) whether the RMSNorm sum of squares is NaN; the caller reports it.
+template <int DT, int NWARPS = GS_WARPS>
+__device__ bool span_x_prologue(const SpanX a, uint32_t nct, uint32_t* xl, float* xfs, double* red, float* s_scale) {
+    constexpr uint32_t CT = NWARPS * 32;
     auto cbar = [] { asm volatile("bar.sync 1, %0;" ::"r"(CT) : "memory"); };
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     float scale = 0.f;
@@ -332,7 +415,7 @@ __device__ bool span_x_prologue(const SpanX a, uint32_t nct, uint32_t* xl, float
         cbar();
         if (tid == 0) {
             double t = 0.0;
-            for (int w = 0; w < GS_WARPS; ++w) t += red[w];
+            for (int w = 0; w < NWARPS; ++w) t += red[w];
             *s_scale = (float)sqrt(1.0 / (t / (double)a.xcols + (double)1e-6f));   // ops.rs:262-274
             x_nan = isnan(t);   // NaN in x <=> NaN sum
         }
@@ -344,76 +427,10 @@ __device__ bool span_x_prologue(const SpanX a, uint32_t nct, uint32_t* xl, float
         const uint32_t nsp = nct * SPAN_LANES, items = nsp * 8;
         for (uint32_t base = 0; base < items; base += CT) {
             const uint32_t it = base + tid;
-            const uint32_t sp = it >> 3, q = it & 7;
             const bool live = it < items;
             float v[16];
-            const uint32_t e0 = sp * SPAN + 16 * q;
-#pragma unroll
-            for (int k = 0; k < 16; ++k) v[k] = 0.f;
-            if (live && e0 + 16 <= a.xcols) {
-                const float4* x4 = reinterpret_cast<const float4*>(a.x + e0);
-                float4 xa[4], ya[4];
-#pragma unroll
-                for (int k = 0; k < 4; ++k) xa[k] = __ldcg(x4 + k);
-                if (a.pro != PRO_PLAIN) {
-                    const float4* y4 = reinterpret_cast<const float4*>(a.x2 + e0);
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) ya[k] = __ldcg(y4 + k);
-                }
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const float xx[4] = {xa[k].x, xa[k].y, xa[k].z, xa[k].w};
-                    const float yy[4] = {ya[k].x, ya[k].y, ya[k].z, ya[k].w};
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        v[4 * k + j] = a.pro == PRO_RMSNORM ? __fmul_rn(__fmul_rn(xx[j], scale), yy[j])   // ops.rs:272
-                                     : a.pro == PRO_SWIGLU ? ffn_silu_mul(xx[j], yy[j])
-                                     : xx[j];
-                    }
-                }
-            } else if (live) {
-#pragma unroll
-                for (int k = 0; k < 16; ++k) v[k] = span_xval(a, e0 + k, scale);   // checks e < xcols
-            }
-            float mx = 0.f, sum = 0.f;
-#pragma unroll
-            for (int k = 0; k < 16; ++k) { mx = fmaxf(mx, fabsf(v[k])); sum += v[k]; }
-            bool finite = isfinite(mx) && isfinite(sum);
-            // the 8 quarters of a span are 8 consecutive threads of one warp
-#pragma unroll
-            for (int o = 1; o < 8; o <<= 1) {
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-                finite = __shfl_xor_sync(0xffffffffu, (int)finite, o) && finite;
-            }
-            const float pair = __shfl_xor_sync(0xffffffffu, sum, 1);   // the other quarter of the 32-element half
-            int ex = 0;
-            frexpf(mx, &ex);
-            const float mul = (mx > 0.f && finite) ? ldexpf(1.f, 22 - ex) : 0.f;
-            const float gs = !finite ? __int_as_float(0x7FC00000) : (mx > 0.f ? ldexpf(1.f, ex - 22) : 0.f);
-            if (live) {
-                const uint32_t ct = sp / SPAN_LANES, l = sp % SPAN_LANES;
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const int s = F::step_of((int)q, t);
-                    uint32_t w0 = 0, w1 = 0, w2 = 0;
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const int xi = __float2int_rn(v[F::qoff(t, j)] * mul);
-                        w0 |= (uint32_t)(xi & 0xFF) << (8 * j);
-                        w1 |= (uint32_t)((xi >> 8) & 0xFF) << (8 * j);
-                        w2 |= (uint32_t)((xi >> 16) & 0xFF) << (8 * j);
-                    }
-                    const uint32_t wi[3] = {(uint32_t)(3 * s), (uint32_t)(3 * s + 1), (uint32_t)(3 * s + 2)};
-                    const uint32_t wv[3] = {w0, w1, w2};
-#pragma unroll
-                    for (int k = 0; k < 3; ++k)
-                        xl[(((size_t)ct * 24 + wi[k] / 4) * SPAN_LANES + l) * 4 + wi[k] % 4] = wv[k];
-                }
-                float* xc = xfs + (size_t)ct * GS_XF * SPAN_LANES;   // [gs x 32][3][32] float4
-                xc[SPAN_LANES + ((q >> 2) * SPAN_LANES + l) * 4 + (q & 3)] = sum;
-                if ((q & 1) == 0) xc[SPAN_LANES + (2 * SPAN_LANES + l) * 4 + (q >> 1)] = sum + pair;
-                if (q == 0) xc[l] = gs;
-            }
+            span_item_load(a, it, live, scale, v);
+            span_item_store<DT>(v, it, live, xl, xfs);
         }
     }
     cbar();

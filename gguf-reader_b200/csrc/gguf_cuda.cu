@@ -25,6 +25,7 @@
 #include "planes.cuh"
 #include "gemv.cuh"
 #include "gemv_span.cuh"
+#include "chain.cuh"
 #include "attention.cuh"
 #include "noalloc.cuh"
 #include "prefill.cuh"
@@ -628,6 +629,10 @@ int init_kernel_attrs() {
                            GGC_Q2_K, GGC_Q3_K_S, GGC_Q3_K_M, GGC_Q3_K_L, GGC_Q4_K, GGC_Q5_K, GGC_Q6_K, GGC_Q8_K};
         for (int dt : dts) dispatch_dtype<SetGemvSmem>(dt, &ok);
         if (cudaFuncSetAttribute(k_attn_av, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024) != cudaSuccess) ok = 0;
+        for (uint32_t mask = 1; mask < 16; ++mask)
+            if (cudaFuncSetAttribute(chain_kernel(mask), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)GEMV_SMEM_LIMIT) != cudaSuccess)
+                ok = 0;
         if (cudaFuncSetAttribute(k_attn_prefill<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pa_smem<64>()) !=
                 cudaSuccess ||
             cudaFuncSetAttribute(k_attn_prefill<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pa_smem<128>()) !=
@@ -1336,6 +1341,12 @@ struct ggc_model {
     bool ar_p2p = false;
     ArGroup* ar = nullptr;                 // device copy
     std::vector<void*> ar_peer_maps;       // IPC mappings of the other ranks' buffers
+    // decode-step GEMVs run as chains (chain.cuh): per chain CH_MAX_OPS op slots
+    // and completion counters on the device, filled from chain_host after capture
+    bool chain = false;
+    ChainOp* chain_ops = nullptr;
+    uint32_t* chain_cnt = nullptr;
+    std::vector<ChainOp> chain_host;
     cudaGraphExec_t graph = nullptr;
     uint64_t launches_per_step = 0;
     uint64_t cache_len = 0;
@@ -1433,8 +1444,11 @@ std::vector<uint32_t> rope_row_order(uint32_t heads, uint32_t hd) {
 }
 
 // Group segments by dtype into as few k_gemv launches as possible.
-int run_segments(ggc_model* m, std::vector<std::pair<int, Seg>> segs, int pro, const float* x, const float* x2,
-                 uint32_t cols, uint32_t xcols, const GemvArgs& tmpl) {
+// The launches of one GEMV over segments: one per dtype (up to three segments each).
+std::vector<std::pair<int, GemvArgs>> split_segments(std::vector<std::pair<int, Seg>> segs, int pro, const float* x,
+                                                     const float* x2, uint32_t cols, uint32_t xcols,
+                                                     const GemvArgs& tmpl) {
+    std::vector<std::pair<int, GemvArgs>> out;
     while (!segs.empty()) {
         const int dt = segs.front().first;
         GemvArgs a = tmpl;
@@ -1449,11 +1463,103 @@ int run_segments(ggc_model* m, std::vector<std::pair<int, Seg>> segs, int pro, c
         a.x2 = x2;
         a.cols = cols;
         a.xcols = xcols;
-        GGC_TRY(run_gemv(m->ctx, dt, a));
+        out.emplace_back(dt, a);
         segs.swap(rest);
     }
-    return GGC_OK;
+    return out;
 }
+
+// The GEMVs between two attention launches of the decode step, gathered into
+// groups (a group's ops read what the group before wrote) and launched as one
+// k_gemv_chain when every op has a span format and the shared memory holds the
+// largest x and two tiles; otherwise each op is its own launch, as before.
+struct ChainBuilder {
+    ggc_model* m;
+    uint32_t index = 0;                              // chains launched so far in this step
+    std::vector<std::pair<int, GemvArgs>> ops;
+    std::vector<std::pair<int, int>> deps;           // per op: first op waited for, count
+    int last0 = 0, last1 = 0;                         // the last group's op range
+
+    explicit ChainBuilder(ggc_model* mm) : m(mm) {}
+
+    // ops that read what the previous group (if any, in this chain) wrote
+    int group(std::vector<std::pair<int, GemvArgs>> g) {
+        const int b = (int)ops.size();
+        for (auto& op : g) {
+            ops.push_back(op);
+            deps.emplace_back(last0, last1 - last0);
+        }
+        last0 = b;
+        last1 = (int)ops.size();
+        return m->chain ? GGC_OK : flush();
+    }
+
+    bool chainable(ChainArgs& c) const {
+        if (!m->chain || ops.empty() || ops.size() > (size_t)CH_MAX_OPS) return false;
+        uint32_t xl = 0, part = 0, slot = 0;
+        const uint32_t sms = (uint32_t)m->ctx->num_sms;
+        for (auto& op : ops) {
+            if (!is_span_dt(op.first) || op.second.cols % SPAN) return false;
+            const TileLayout L = make_layout(op.first, TILE_ROWS, op.second.cols);
+            const SpanSpec sp = span_spec(op.first);
+            uint32_t sb = 0;
+            for (int p = 0; p < sp.n; ++p) sb += (TILE_ROWS * L.tp_full[p] + 127u) / 128u * 128u;
+            slot = std::max(slot, sb);
+            xl = std::max(xl, (L.nct * SPAN_LANES * (GS_WORDS + GS_XF) * 4u + 127u) / 128u * 128u);
+            uint32_t total = 0;
+            for (int i = 0; i < op.second.nseg; ++i) total += op.second.seg[i].m.L.nrb;
+            part = std::max(part, ((total + sms - 1) / sms) * TILE_ROWS * 4u);   // every op's row sums
+        }
+        part = (part + 127u) / 128u * 128u;
+        if ((size_t)xl + part + 128 + 2ull * slot > GEMV_SMEM_LIMIT) return false;
+        c.xl_bytes = xl;
+        c.part_bytes = part;
+        c.ring_bytes = (uint32_t)(GEMV_SMEM_LIMIT - xl - part - 128) / 128u * 128u;
+        return true;
+    }
+
+    int flush() {
+        ChainArgs c{};
+        if (!chainable(c)) {
+            for (auto& op : ops) GGC_TRY(run_gemv(m->ctx, op.first, op.second));
+        } else {
+            const uint32_t sms = (uint32_t)m->ctx->num_sms;
+            ChainOp* host = m->chain_host.data() + (size_t)index * CH_MAX_OPS;
+            for (size_t k = 0; k < ops.size(); ++k) {
+                ChainOp& o = host[k];
+                o = ChainOp{};
+                o.a = ops[k].second;
+                o.dt = ops[k].first;
+                o.dep = deps[k].first;
+                o.ndep = deps[k].second;
+                const TileLayout L = make_layout(o.dt, TILE_ROWS, o.a.cols);
+                const SpanSpec sp = span_spec(o.dt);
+                uint32_t off = 0;
+                for (int p = 0; p < 4; ++p) {
+                    o.poff[p] = off;
+                    off += p < sp.n ? (TILE_ROWS * L.tp_full[p] + 127u) / 128u * 128u : 0u;
+                }
+                o.slot_bytes = off;
+                uint32_t total = 0;
+                for (int i = 0; i < o.a.nseg; ++i) total += o.a.seg[i].m.L.nrb;
+                o.part_rows = ((total + sms - 1) / sms) * TILE_ROWS;
+            }
+            c.ops = m->chain_ops + (size_t)index * CH_MAX_OPS;
+            c.nops = (int)ops.size();
+            c.cnt = m->chain_cnt + (size_t)index * CH_MAX_OPS;
+            c.step = &m->st->ar_step;
+            c.errf = m->errf;
+            uint32_t mask = 0;
+            for (auto& op : ops) mask |= chain_bit(op.first);
+            GGC_CUDA_TRY(launch(m->ctx, chain_kernel(mask), dim3(sms), dim3(CH_THREADS), (size_t)GEMV_SMEM_LIMIT, c));
+            ++index;
+        }
+        ops.clear();
+        deps.clear();
+        last0 = last1 = 0;
+        return GGC_OK;
+    }
+};
 
 // Enqueues one decode step (one token through every layer) on the context stream.
 int enqueue_step(ggc_model* m) {
@@ -1491,6 +1597,8 @@ int enqueue_step(ggc_model* m) {
         const ncclResult_t r = nccl().AllReduce(m->hidden, m->hidden, d, ncclFloat, ncclSum, ctx->comm, ctx->stream);
         return r == ncclSuccess ? GGC_OK : nccl_error("ncclAllReduce", r);
     };
+    // the GEMVs between two attention launches form one chain (chain.cuh)
+    ChainBuilder cb(m);
     for (uint32_t l = 0; l < hp.n_layers; ++l) {
         ModelLayer& L = m->layers[l];
         void* kc = (uint8_t*)m->kcache + l * layer_kv;
@@ -1501,11 +1609,11 @@ int enqueue_step(ggc_model* m) {
             rq.pro_err_slot = ERRF_NAN_FFN;
             rq.pro_err_val = (int)l;   // layer l - 1
         }
-        GGC_TRY(run_segments(m,
-                             {{L.wq.dtype, make_seg(L.wq, EPI_ROPE_Q, m->q, nullptr, L.bq)},
-                              {L.wk.dtype, make_seg(L.wk, EPI_ROPE_KC, nullptr, kc, L.bk)},
-                              {L.wv.dtype, make_seg(L.wv, EPI_VC, nullptr, vc, L.bv)}},
-                             PRO_RMSNORM, m->hidden, L.attn_norm, L.wq.cols, d, rq));
+        GGC_TRY(cb.group(split_segments({{L.wq.dtype, make_seg(L.wq, EPI_ROPE_Q, m->q, nullptr, L.bq)},
+                                         {L.wk.dtype, make_seg(L.wk, EPI_ROPE_KC, nullptr, kc, L.bk)},
+                                         {L.wv.dtype, make_seg(L.wv, EPI_VC, nullptr, vc, L.bv)}},
+                                        PRO_RMSNORM, m->hidden, L.attn_norm, L.wq.cols, d, rq)));
+        GGC_TRY(cb.flush());
         AttnArgs aa{};
         aa.q = m->q;
         aa.kc = kc;
@@ -1543,8 +1651,8 @@ int enqueue_step(ggc_model* m) {
             ro.ar = m->ar;
             ro.ar_k = 2 * l + 1;
         }
-        GGC_TRY(run_segments(m, {{L.wo.dtype, make_seg(L.wo, resid_epi, m->hidden, nullptr, nullptr)}}, PRO_PLAIN, m->o,
-                             nullptr, L.wo.cols, L.wo.xcols, ro));
+        GGC_TRY(cb.group(split_segments({{L.wo.dtype, make_seg(L.wo, resid_epi, m->hidden, nullptr, nullptr)}},
+                                        PRO_PLAIN, m->o, nullptr, L.wo.cols, L.wo.xcols, ro)));
         GGC_TRY(allreduce_hidden());
         // ffn_block (llama.rs:547-580): rmsnorm -> up, gate -> silu(gate)*up -> down + residual
         GemvArgs ru = base;
@@ -1560,25 +1668,25 @@ int enqueue_step(ggc_model* m) {
             rd.ar_k = 2 * l + 2;
         }
         if (L.ug.base) {   // fused up/gate: h = silu(gate) * up in the epilogue (into ubuf), then down
-            GGC_TRY(run_segments(m, {{L.ug.dtype, make_seg(L.ug, EPI_SWIGLU, m->ubuf, nullptr, nullptr)}}, PRO_RMSNORM,
-                                 m->hidden, L.ffn_norm, L.ug.cols, d, ru));
-            GGC_TRY(run_segments(m, {{L.down.dtype, make_seg(L.down, resid_epi, m->hidden, nullptr, nullptr)}},
-                                 PRO_PLAIN, m->ubuf, nullptr, L.down.cols, L.f_l, rd));
+            GGC_TRY(cb.group(split_segments({{L.ug.dtype, make_seg(L.ug, EPI_SWIGLU, m->ubuf, nullptr, nullptr)}},
+                                            PRO_RMSNORM, m->hidden, L.ffn_norm, L.ug.cols, d, ru)));
+            GGC_TRY(cb.group(split_segments({{L.down.dtype, make_seg(L.down, resid_epi, m->hidden, nullptr, nullptr)}},
+                                            PRO_PLAIN, m->ubuf, nullptr, L.down.cols, L.f_l, rd)));
         } else {
-            GGC_TRY(run_segments(m,
-                                 {{L.up.dtype, make_seg(L.up, EPI_STORE, m->ubuf, nullptr, nullptr)},
-                                  {L.gate.dtype, make_seg(L.gate, EPI_STORE, m->gbuf, nullptr, nullptr)}},
-                                 PRO_RMSNORM, m->hidden, L.ffn_norm, L.up.cols, d, ru));
-            GGC_TRY(run_segments(m, {{L.down.dtype, make_seg(L.down, resid_epi, m->hidden, nullptr, nullptr)}},
-                                 PRO_SWIGLU, m->gbuf, m->ubuf, L.down.cols, L.f_l, rd));
+            GGC_TRY(cb.group(split_segments({{L.up.dtype, make_seg(L.up, EPI_STORE, m->ubuf, nullptr, nullptr)},
+                                             {L.gate.dtype, make_seg(L.gate, EPI_STORE, m->gbuf, nullptr, nullptr)}},
+                                            PRO_RMSNORM, m->hidden, L.ffn_norm, L.up.cols, d, ru)));
+            GGC_TRY(cb.group(split_segments({{L.down.dtype, make_seg(L.down, resid_epi, m->hidden, nullptr, nullptr)}},
+                                            PRO_SWIGLU, m->gbuf, m->ubuf, L.down.cols, L.f_l, rd)));
         }
         GGC_TRY(allreduce_hidden());
     }
     // final norm + lm_head for the last token only (llama.rs:333, :582-616) + greedy argmax
     GemvArgs lh = base;
     lh.st_skip = &m->st->in_idx;   // skip while in_idx < n_in (a prompt token that is not the last)
-    GGC_TRY(run_segments(m, {{m->output.dtype, make_seg(m->output, EPI_LOGITS, m->logits, nullptr, nullptr)}},
-                         PRO_RMSNORM, m->hidden, m->output_norm, m->output.cols, d, lh));
+    GGC_TRY(cb.group(split_segments({{m->output.dtype, make_seg(m->output, EPI_LOGITS, m->logits, nullptr, nullptr)}},
+                                    PRO_RMSNORM, m->hidden, m->output_norm, m->output.cols, d, lh)));
+    GGC_TRY(cb.flush());
     GGC_CUDA_TRY(launch(ctx, k_step_end, dim3(1), dim3(nccl_tp ? 256 : 32), 0, m->st,
                         (const unsigned long long*)m->argmax_key, m->out_ids, m->errf,
                         nccl_tp ? (const float*)m->hidden : nullptr, d, (int)hp.n_layers));
@@ -1684,6 +1792,9 @@ int build_graph(ggc_model* m) {
         return st;
     }
     GGC_CUDA_TRY(e);
+    if (m->chain)
+        GGC_CUDA_TRY(cudaMemcpy(m->chain_ops, m->chain_host.data(), m->chain_host.size() * sizeof(ChainOp),
+                                cudaMemcpyHostToDevice));
     e = cudaGraphInstantiate(&m->graph, g, 0);
     cudaGraphDestroy(g);
     GGC_CUDA_TRY(e);
@@ -1980,6 +2091,17 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
     s0.max_ctx = hp.max_ctx;
     GGC_CUDA_TRY(cudaMemcpy(m->st, &s0, sizeof(s0), cudaMemcpyHostToDevice));
     GGC_TRY(setup_allreduce(m.get()));
+    {   // decode GEMVs as chains (chain.cuh), opt-in with GGC_DECODE_CHAIN=1 (slower than the per-op
+        // kernels today: 369 vs 450 tokens/s on the Llama-2-7B Q4_K_M step), never around an NCCL all-reduce
+        const char* ce = getenv("GGC_DECODE_CHAIN");
+        m->chain = (ce && strcmp(ce, "1") == 0) && !(ctx->world > 1 && !m->ar_p2p);
+        if (m->chain) {
+            const size_t slots = (size_t)(hp.n_layers + 1) * CH_MAX_OPS;
+            m->chain_host.assign(slots, ChainOp{});
+            GGC_TRY(dalloc(m.get(), &m->chain_ops, slots));
+            GGC_TRY(dalloc(m.get(), &m->chain_cnt, slots));
+        }
+    }
     GGC_TRY(build_graph(m.get()));
     GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
     *out = m.release();
