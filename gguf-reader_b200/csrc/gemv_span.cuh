@@ -253,7 +253,7 @@ struct SpanCfg {
     uint32_t poff[4];       // plane offsets inside a stage
     uint32_t stage_bytes, stages;
     uint32_t xl_bytes;      // limb words + per-span floats of every column tile
-    uint32_t part_rows;     // partial row sums kept per CTA (multi-tile rows)
+    uint32_t part_rows;     // row sums kept per CTA (its rows, added over the column tiles)
     uint32_t smem;          // dynamic shared memory
 };
 
@@ -270,7 +270,7 @@ SpanCfg make_span_cfg(uint32_t pcols, uint32_t total_rb, uint32_t ctas, size_t s
     c.stage_bytes = off;
     const uint32_t nsp_full = L.nct * SPAN_LANES;
     c.xl_bytes = (nsp_full * (GS_WORDS + GS_XF) * 4u + 127u) / 128u * 128u;
-    c.part_rows = L.nct > 1 ? ((total_rb + ctas - 1) / ctas) * TILE_ROWS : 0u;
+    c.part_rows = ((total_rb + ctas - 1) / ctas) * TILE_ROWS;   // every row's sum, gathered for the epilogues
     const size_t fixed = (size_t)c.xl_bytes + c.part_rows * 4u + 128;
     const size_t st = smem_limit > fixed ? (smem_limit - fixed) / c.stage_bytes : 0;
     c.stages = (uint32_t)(st > (size_t)GS_MAX_STAGES ? GS_MAX_STAGES : st);
@@ -395,6 +395,47 @@ __device__ bool span_x_prologue(const SpanX a, uint32_t nct, uint32_t* xl, float
     constexpr uint32_t CT = NWARPS * 32;
     auto cbar = [] { asm volatile("bar.sync 1, %0;" ::"r"(CT) : "memory"); };
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t items = nct * SPAN_LANES * 8;
+    if (a.pro == PRO_RMSNORM && items <= CT) {
+        // one item per thread: x and the norm weight read once (one L2 round trip),
+        // the sum of squares and the limbs from the same registers
+        const uint32_t e0 = (tid >> 3) * SPAN + 16 * (tid & 7);
+        float xv[16], wv[16];
+        if ((uint32_t)tid < items && e0 + 16 <= a.xcols) {
+            const float4* x4 = reinterpret_cast<const float4*>(a.x + e0);
+            const float4* w4 = reinterpret_cast<const float4*>(a.x2 + e0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 v = __ldcg(x4 + q), w = __ldg(w4 + q);
+                xv[4 * q] = v.x; xv[4 * q + 1] = v.y; xv[4 * q + 2] = v.z; xv[4 * q + 3] = v.w;
+                wv[4 * q] = w.x; wv[4 * q + 1] = w.y; wv[4 * q + 2] = w.z; wv[4 * q + 3] = w.w;
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const bool in = (uint32_t)tid < items && e0 + e < a.xcols;
+                xv[e] = in ? __ldcg(a.x + e0 + e) : 0.f;
+                wv[e] = in ? __ldg(a.x2 + e0 + e) : 0.f;
+            }
+        }
+        double ss = 0.0;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) ss += (double)xv[e] * (double)xv[e];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) red[warp] = ss;
+        cbar();
+        double t = 0.0;
+#pragma unroll
+        for (int w = 0; w < NWARPS; ++w) t += red[w];
+        const float scale = (float)sqrt(1.0 / (t / (double)a.xcols + (double)1e-6f));   // ops.rs:262-274
+        float v[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) v[e] = __fmul_rn(__fmul_rn(xv[e], scale), wv[e]);   // ops.rs:272
+        span_item_store<DT>(v, (uint32_t)tid, (uint32_t)tid < items, xl, xfs);
+        cbar();
+        return tid == 0 && isnan(t);   // NaN in x <=> NaN sum
+    }
     float scale = 0.f;
     bool x_nan = false;
     if (a.pro == PRO_RMSNORM) {
@@ -424,7 +465,6 @@ __device__ bool span_x_prologue(const SpanX a, uint32_t nct, uint32_t* xl, float
     }
     // x -> limbs: 8 threads per span (one quarter of 16 elements each)
     {
-        const uint32_t nsp = nct * SPAN_LANES, items = nsp * 8;
         for (uint32_t base = 0; base < items; base += CT) {
             const uint32_t it = base + tid;
             const bool live = it < items;
@@ -447,7 +487,7 @@ __global__ void __launch_bounds__(GS_THREADS, 1) k_gemv_span(const GemvArgs a, c
     __shared__ double red[GS_WARPS];
     __shared__ float s_scale;
     __shared__ unsigned long long s_best[GS_WARPS];
-    __shared__ int s_nan;
+    __shared__ int s_dead;   // a tile never arrived: no more waits, no epilogues
 
     uint32_t* xl = reinterpret_cast<uint32_t*>(smem);                                // [ct][24][lane][4]
     const uint32_t nct = a.seg[0].m.L.nct;
@@ -464,7 +504,7 @@ __global__ void __launch_bounds__(GS_THREADS, 1) k_gemv_span(const GemvArgs a, c
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], GS_WARPS);
         }
-        s_nan = 0;
+        s_dead = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (tid < GS_WARPS) s_best[tid] = 0ull;
@@ -547,16 +587,18 @@ __global__ void __launch_bounds__(GS_THREADS, 1) k_gemv_span(const GemvArgs a, c
     uint32_t L[GS_WORDS];
     float gs = 0.f;             // x scale of this lane's span in the current column tile
     const float* xq = nullptr;  // its x sums (shared memory)
-    unsigned long long best = 0ull;
-    bool nan_logit = false;
     // tile i = (column tile ct, row block rb0 + rbl); counters advance instead of dividing
-    uint32_t s = 0, ph = 0, rbl = 0, ct = 0, rb = 0;
-    int si = 0;
-    locate(rb0, si, rb);
+    uint32_t s = 0, ph = 0, rbl = 0, ct = 0;
     int nl = 0;
     uint32_t rowoff[2][4];
     for (uint32_t i = 0; i < ntiles; ++i) {
-        if (!mbar_wait(&full[s], ph, a.errf)) return;
+        // a tile that never arrives ends all waiting; the warps still meet below
+        if (!*(volatile int*)&s_dead && !mbar_wait(&full[s], ph, a.errf)) s_dead = 1;
+        if (*(volatile int*)&s_dead) {
+            if (++s == cfg.stages) { s = 0; ph ^= 1u; }
+            if (++rbl == nrb) { rbl = 0; ++ct; }
+            continue;
+        }
         if (rbl == 0) {   // a new column tile: x of this lane's span into registers, tile geometry
             const TileLayout& L0 = sseg[0].m.L;
             nl = ct + 1 == L0.nct ? (int)((L0.pcols - ct * SPAN_KC) / SPAN) : SPAN_LANES;
@@ -595,49 +637,52 @@ __global__ void __launch_bounds__(GS_THREADS, 1) k_gemv_span(const GemvArgs a, c
             y[1] = __shfl_sync(0xffffffffu, v, 16);
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        // this tile's (segment, row block, column tile); then advance the counters
-        const int tsi = si;
-        const uint32_t trb = rb, trbl = rbl, tct = ct;
-        if (++s == cfg.stages) { s = 0; ph ^= 1u; }
-        if (++rbl == nrb) {
-            rbl = 0;
-            ++ct;
-            locate(rb0, si, rb);
-        } else if (++rb == sseg[si].m.L.nrb) {
-            rb = 0;
-            ++si;
-        }
-        const uint32_t nrows = min((uint32_t)TILE_ROWS, sseg[tsi].m.L.rows - trb * TILE_ROWS);
-        if ((uint32_t)r0 >= nrows) continue;
-        const uint32_t nv = min(2u, nrows - (uint32_t)r0);
-        if (nct > 1) {
-            float* pp = part + trbl * TILE_ROWS + r0;
-            if (tct + 1 < nct) {
-                if (lane == 0) { pp[0] += y[0]; pp[1] += y[1]; }
-                continue;
-            }
-            y[0] += pp[0];
-            y[1] += pp[1];
-        }
         if (lane == 0) {
-            const Seg& sg = sseg[tsi];
-            const uint32_t row = trb * TILE_ROWS + (uint32_t)r0;
-            if (sg.epi == EPI_LOGITS) {   // logits + running argmax (one atomic per warp at the end)
-                for (uint32_t k = 0; k < nv; ++k) {
-                    sg.out[row + k] = y[k];
-                    nan_logit |= isnan(y[k]);
-                    const unsigned long long key = argmax_key_of(y[k], row + k);
-                    best = key > best ? key : best;
-                }
-            } else {
-                gemv_epilogue(a, sg, row, nv, y);
+            mbar_arrive(&empty[s]);
+            float* pp = part + rbl * TILE_ROWS + r0;   // row sums of the CTA's rows (added over column tiles)
+            pp[0] += y[0];
+            pp[1] += y[1];
+        }
+        if (++s == cfg.stages) { s = 0; ph ^= 1u; }
+        if (++rbl == nrb) { rbl = 0; ++ct; }
+    }
+    // epilogues of all the CTA's rows at once, a row pair per thread, so their global
+    // loads (residual, RoPE position and table, bias) overlap instead of following each tile
+    cbar();
+    if (*(volatile int*)&s_dead) return;
+    unsigned long long best = 0ull;
+    bool nan_logit = false;
+    for (uint32_t p = tid; p < nrb * (TILE_ROWS / 2); p += CT) {
+        int psi;
+        uint32_t prb;
+        locate(rb0 + p / (TILE_ROWS / 2), psi, prb);
+        const Seg& sg = sseg[psi];
+        const uint32_t row = prb * TILE_ROWS + 2 * (p % (TILE_ROWS / 2));
+        if (row >= sg.m.L.rows) continue;
+        const uint32_t nv = min(2u, sg.m.L.rows - row);
+        const float* yy = part + 2 * p;
+        if (sg.epi == EPI_LOGITS) {   // logits + greedy argmax (one atomic per warp)
+            for (uint32_t k = 0; k < nv; ++k) {
+                sg.out[row + k] = yy[k];
+                nan_logit |= isnan(yy[k]);
+                const unsigned long long key = argmax_key_of(yy[k], row + k);
+                best = key > best ? key : best;
             }
+        } else {
+            gemv_epilogue(a, sg, row, nv, yy);
         }
     }
-    if (lane == 0 && (best || nan_logit)) {
-        if (nan_logit) atomicMax(&a.errf[ERRF_NAN_LOGITS], 1);
-        atomicMax(a.argmax_key, best);
+    if (sseg[0].epi == EPI_LOGITS) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+            best = other > best ? other : best;
+        }
+        nan_logit = __any_sync(0xffffffffu, nan_logit);
+        if (lane == 0 && (best || nan_logit)) {
+            if (nan_logit) atomicMax(&a.errf[ERRF_NAN_LOGITS], 1);
+            atomicMax(a.argmax_key, best);
+        }
     }
     if (a.ar_k)   // tensor parallel: this warp's row pair of each row block, summed over the ranks
         ar_reduce_rows(

@@ -256,3 +256,30 @@ def test_determinism(ggc, ctx):
     la = a.forward([1, 2, 3], [0, 1, 2])
     lb = b.forward([1, 2, 3], [0, 1, 2])
     assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+
+
+# ---- decode GEMV chains (GGC_DECODE_CHAIN=1: one persistent launch per run of GEMVs) ----
+CHAIN_CASES = [
+    ("mini-q4_k_m", MINI, None, None),
+    ("qwen2-0.5b-q8_0-2layers", "qwen2-0.5b-q8_0", 2, None),
+    ("llama2-7b-q4_k_m-2layers", "llama2-7b-q4_k_m", 2, None),   # Q4_K and Q6_K ops in one chain
+    ("llama3-8b-q4_0-1layer", "llama3-8b-q4_0", 1, 32000),
+]
+
+
+@pytest.mark.parametrize("name,cfg,n_layers,vocab", CHAIN_CASES, ids=[c[0] for c in CHAIN_CASES])
+def test_chain_decode_matches_oracle(ggc, orc, ctx, monkeypatch, name, cfg, n_layers, vocab):
+    monkeypatch.setenv("GGC_DECODE_CHAIN", "1")
+    hp, m, o = model_pair(ggc, orc, ctx, cfg, n_layers, vocab)
+    prompt = np.random.default_rng(9).integers(0, hp["vocab_size"], size=6).astype(np.uint32)
+    got = m.forward(prompt, np.arange(6, dtype=np.int64))
+    want = o.forward(prompt, np.arange(6, dtype=np.int64))
+    assert rel_l2(got, want) <= REL_L2, rel_l2(got, want)
+    ids = m.decode(32)
+    want_ids, lg, pos = [], want, 6
+    for _ in range(32):
+        want_ids.append(orc.greedy(lg))
+        lg = o.forward([want_ids[-1]], [pos])
+        pos += 1
+    assert ids == want_ids
+    m.close()
