@@ -224,6 +224,7 @@ inline size_t attn_av_smem(uint32_t G, uint32_t hd) { return (size_t)ATTN_WARPS 
 constexpr int FA_WARPS = 8;
 constexpr int FA_THREADS = FA_WARPS * 32;
 constexpr int FA_STAGES = 3;
+constexpr uint32_t FA_MAX_SPLITS = 64;   // splits of a kv head's positions (the combine's weights)
 
 template <int HD, bool F16, int MAXG>
 struct FaCfg {
@@ -302,6 +303,7 @@ __global__ void __launch_bounds__(FA_THREADS, 2) k_attn_decode(const AttnArgs a)
     float* ssc = reinterpret_cast<float*>(fsm + 2 * FA_STAGES * TB);       // [TR][MAXG] scores of a tile
     __shared__ __align__(8) uint64_t full[FA_STAGES];
     __shared__ float s_fin[2][MAXG];
+    __shared__ float s_w[MAXG][FA_MAX_SPLITS];   // split weights exp(m_k - M) of the combine
     __shared__ bool s_last;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int sub = lane / LPR, gl = lane % LPR;
@@ -492,7 +494,9 @@ __global__ void __launch_bounds__(FA_THREADS, 2) k_attn_decode(const AttnArgs a)
     if (!s_last) return;
     __threadfence();
     // last CTA of the kv head: M = max m_k, S = sum exp(m_k - M) l_k,
-    // o = (sum exp(m_k - M) o_k) * (1/S), splits in index order
+    // o = (sum exp(m_k - M) o_k) * (1/S), splits in index order.  The split weights
+    // exp(m_k - M) go to shared memory once, so the output sums load the partials
+    // without a data-dependent branch (several loads in flight).
     if (warp < (int)G) {
         const uint32_t h = h0 + warp;
         float M = -INFINITY;
@@ -502,24 +506,29 @@ __global__ void __launch_bounds__(FA_THREADS, 2) k_attn_decode(const AttnArgs a)
         float S = 0.f;
         for (uint32_t k = lane; k < a.nsplit; k += 32) {
             const float mk = __ldcg(&a.pmax[(size_t)k * a.n_heads + h]);
-            if (mk != -INFINITY) S += expf(mk - M) * __ldcg(&a.psum[(size_t)k * a.n_heads + h]);
+            const float w = mk != -INFINITY ? expf(mk - M) : 0.f;
+            s_w[warp][k] = w;
+            if (mk != -INFINITY) S += w * __ldcg(&a.psum[(size_t)k * a.n_heads + h]);
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
-        if (lane == 0) {
-            s_fin[0][warp] = M;
-            s_fin[1][warp] = __fdiv_rn(1.0f, S);
-        }
+        if (lane == 0) s_fin[1][warp] = __fdiv_rn(1.0f, S);
     }
     __syncthreads();
     for (uint32_t e = tid; e < G * HD; e += FA_THREADS) {
         const uint32_t g = e / HD, i = e % HD, h = h0 + g;
-        const float M = s_fin[0][g];
+        const float* op = a.opart + (size_t)h * HD + i;
+        const size_t stride = (size_t)a.n_heads * HD;
         float sum = 0.f;
-        for (uint32_t k = 0; k < a.nsplit; ++k) {
-            const float mk = __ldcg(&a.pmax[(size_t)k * a.n_heads + h]);
-            if (mk != -INFINITY) sum += expf(mk - M) * __ldcg(&a.opart[((size_t)k * a.n_heads + h) * HD + i]);
+        uint32_t k = 0;
+        for (; k + 8 <= a.nsplit; k += 8) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = __ldcg(op + (k + u) * stride);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) sum += s_w[g][k + u] * v[u];
         }
+        for (; k < a.nsplit; ++k) sum += s_w[g][k] * __ldcg(op + k * stride);
         a.o[(size_t)h * HD + i] = sum * s_fin[1][g];
     }
     if (tid == 0) a.tickets[kvhead] = 0;

@@ -2060,8 +2060,10 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
     }
     // fused attention: two resident CTAs per SM over (kv head, split); general pair: ~2 per SM, <= 64 splits
     m->attn = attn_decode_sel(hd, hp.kv_f16 != 0, hp.n_heads / hp.n_kv_heads);
-    if (m->attn.kernel) {
-        const uint32_t ns = (uint32_t)ctx->num_sms * 2 / m->kv_heads_l;
+    if (m->attn.kernel) {   // at most two CTAs per SM, >= 128 positions per split at max_ctx, <= 64 splits
+        uint32_t ns = (uint32_t)ctx->num_sms * 2 / m->kv_heads_l;
+        ns = std::min(ns, cdiv<uint32_t>(hp.max_ctx, 128));
+        ns = std::min(ns, FA_MAX_SPLITS);
         m->nsplit = ns < 1 ? 1 : ns;
     } else {
         const uint32_t ns = cdiv<uint32_t>((uint32_t)ctx->num_sms * 2, m->kv_heads_l);
