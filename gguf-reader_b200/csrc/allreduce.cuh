@@ -107,4 +107,21 @@ __device__ __forceinline__ void ar_reduce_rows(const ArGroup* gp, uint32_t k, ui
     }
 }
 
+// One fused all-reduce step of a world-2 group run on a single GPU (the probe of
+// ggc_allreduce_probe): this rank's partial words are stored by the kernel, the
+// peer's too when peer_writes, else never, so the bounded poll must give up.
+// One warp: ar_reduce_rows strides a row list over the lanes of a warp.
+__global__ void k_ar_probe(const ArGroup* g, uint32_t rows, const float* part0, const float* part1, int peer_writes,
+                           float* out, int* errf) {
+    const uint32_t k = 1u, ph = 0u;
+    const unsigned long long tag = (unsigned long long)ar_epoch(*g, k) << 32;
+    for (uint32_t r = threadIdx.x; r < rows; r += 32) {
+        st_relaxed_sys_u64(g->buf[0] + ((size_t)ph * g->world + 0) * g->stride + r, tag | __float_as_uint(part0[r]));
+        if (peer_writes)
+            st_relaxed_sys_u64(g->buf[0] + ((size_t)ph * g->world + 1) * g->stride + r, tag | __float_as_uint(part1[r]));
+    }
+    __syncwarp();
+    ar_reduce_rows(g, k, rows, [](uint32_t j) { return j; }, rows, out, errf, ERRF_NAN_ATTN, 0);
+}
+
 }  // namespace ggc

@@ -6,6 +6,7 @@
 // arithmetic is never contracted into FMAs (bit-exact with the reference).
 #include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <cmath>
 #include <cstdarg>
 #include <cstdlib>
@@ -111,6 +112,14 @@ NcclApi& nccl() {
 int nccl_error(const char* what, ncclResult_t r) {
     return set_error(GGC_ERR_NCCL, "%s: %s", what, nccl().GetErrorString ? nccl().GetErrorString(r) : "?");
 }
+
+// Host deadline of a wait on work that includes collectives (GGC_NCCL_TIMEOUT_MS,
+// default 10 minutes).
+double nccl_deadline_ms() {
+    const char* e = getenv("GGC_NCCL_TIMEOUT_MS");
+    const double v = e ? atof(e) : 0.0;
+    return v > 0.0 ? v : 600000.0;
+}
 }  // namespace
 
 // ===========================================================================
@@ -130,9 +139,43 @@ struct ggc_ctx {
     void* stage[8] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
     size_t stage_cap[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     int* errf = nullptr;   // device error flags of the context's own launches
+    bool comm_failed = false;   // the communicator was aborted (a rank lost or an NCCL error)
 };
 
 namespace {
+
+// Waits for the context stream.  Without a communicator: cudaStreamSynchronize.
+// With one (tensor parallelism), a rank that died or stalls would leave the others
+// blocked in a collective forever, so the stream is polled against a host
+// deadline together with ncclCommGetAsyncError; on an NCCL error or expiry the
+// communicator is aborted (its kernels in flight return; the fused all-reduce's
+// own waits are bounded) and the call fails with GGC_ERR_NCCL.  The context's
+// collectives fail from then on.
+int ctx_sync(ggc_ctx* ctx) {
+    if (ctx->comm_failed) return set_error(GGC_ERR_NCCL, "communicator aborted earlier (a rank was lost)");
+    if (!ctx->comm) {
+        GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+        return GGC_OK;
+    }
+    const auto t0 = std::chrono::steady_clock::now();
+    for (uint64_t it = 0;; ++it) {
+        const cudaError_t e = cudaStreamQuery(ctx->stream);
+        if (e == cudaSuccess) return GGC_OK;
+        if (e != cudaErrorNotReady) return set_error(GGC_ERR_CUDA, "stream: %s", cudaGetErrorString(e));
+        ncclResult_t ar = ncclSuccess;
+        const bool async_err = nccl().CommGetAsyncError && nccl().CommGetAsyncError(ctx->comm, &ar) == ncclSuccess &&
+                               ar != ncclSuccess && ar != ncclInProgress;
+        const double ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+        if (async_err || ms > nccl_deadline_ms()) {
+            if (nccl().CommAbort) nccl().CommAbort(ctx->comm);
+            ctx->comm = nullptr;
+            ctx->comm_failed = true;
+            if (async_err) return nccl_error("NCCL asynchronous error (communicator aborted)", ar);
+            return set_error(GGC_ERR_NCCL, "no progress within %.0f ms: a rank lost? (communicator aborted)", ms);
+        }
+        if (it > 2000) std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
 
 struct DeviceGuard {
     int prev = -1;
@@ -157,7 +200,7 @@ bool is_device_ptr(const void* p) {
 
 int ensure_stage(ggc_ctx* ctx, int i, size_t bytes) {
     if (ctx->stage_cap[i] >= bytes) return GGC_OK;
-    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    GGC_TRY(ctx_sync(ctx));
     if (ctx->stage[i]) cudaFree(ctx->stage[i]);
     ctx->stage[i] = nullptr;
     ctx->stage_cap[i] = 0;
@@ -322,7 +365,7 @@ extern "C" uint64_t ggc_ctx_kernel_launches(ggc_ctx* ctx) { return ctx ? ctx->la
 extern "C" int ggc_ctx_synchronize(ggc_ctx* ctx) {
     if (!ctx) return set_error(GGC_ERR_INVALID_ARG, "null ctx");
     DeviceGuard g(ctx->device);
-    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    GGC_TRY(ctx_sync(ctx));
     return GGC_OK;
 }
 
@@ -347,7 +390,7 @@ extern "C" int ggc_dequantize(ggc_ctx* ctx, int dtype, const void* raw, uint64_t
     GGC_CUDA_TRY(err);
     if (staged) {
         GGC_CUDA_TRY(cudaMemcpyAsync(out, dout, n * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
-        GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+        GGC_TRY(ctx_sync(ctx));
     }
     return GGC_OK;
 }
@@ -377,7 +420,7 @@ extern "C" int ggc_quant_matvec(ggc_ctx* ctx, int dtype, const void* w, uint64_t
     GGC_CUDA_TRY(err);
     if (staged) {
         GGC_CUDA_TRY(cudaMemcpyAsync(y, dy, rows * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
-        GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+        GGC_TRY(ctx_sync(ctx));
     }
     return GGC_OK;
 }
@@ -773,7 +816,7 @@ extern "C" int ggc_tensor_matvec(ggc_ctx* ctx, const ggc_tensor* t, const float*
     }
     if (staged) {
         GGC_CUDA_TRY(cudaMemcpyAsync(y, dy, rows * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
-        GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+        GGC_TRY(ctx_sync(ctx));
     }
     return GGC_OK;
 }
@@ -986,7 +1029,7 @@ extern "C" int ggc_tensor_matmul(ggc_ctx* ctx, const ggc_tensor* t, const float*
     int hf[ERRF_COUNT];
     GGC_CUDA_TRY(cudaMemcpyAsync(hf, errf, sizeof(hf), cudaMemcpyDeviceToHost, ctx->stream));
     if (staged) GGC_CUDA_TRY(cudaMemcpyAsync(y, dy, m * rows * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
-    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    GGC_TRY(ctx_sync(ctx));
     if (hf[ERRF_TIMEOUT]) {
         cudaMemset(errf, 0, sizeof(int) * ERRF_COUNT);
         return set_error(GGC_ERR_TIMEOUT, "a bounded device wait expired");
@@ -1020,7 +1063,7 @@ struct InOut {
     }
     int done() {
         if (staged && bytes) GGC_CUDA_TRY(cudaMemcpyAsync(user, dev, bytes, cudaMemcpyDeviceToHost, ctx->stream));
-        GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+        GGC_TRY(ctx_sync(ctx));
         return GGC_OK;
     }
 };
@@ -1313,6 +1356,7 @@ struct ggc_model {
     float2* rope = nullptr;
     // activations / scratch
     float *hidden = nullptr, *q = nullptr, *o = nullptr, *ubuf = nullptr, *gbuf = nullptr, *logits = nullptr;
+    float* logits_host = nullptr;   // pinned mirror of logits (host copies out of forward)
     float *scores = nullptr, *pmax = nullptr, *psum = nullptr, *opart = nullptr;
     AttnDecodeSel attn;   // fused decode attention, or null for the general pair
     float2* stats = nullptr;
@@ -1381,7 +1425,7 @@ int upload_vec(ggc_model* m, const ggc_tensor_desc& t, uint64_t expect, float** 
     float* d = nullptr;
     GGC_TRY(dalloc(m, &d, elements));
     GGC_TRY(ggc_dequantize(m->ctx, t.dtype, t.data, t.nbytes, elements, d));
-    GGC_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    GGC_TRY(ctx_sync(m->ctx));
     *out = d;
     return GGC_OK;
 }
@@ -1734,7 +1778,7 @@ int setup_allreduce(ggc_model* m) {
     if (r != ncclSuccess) return nccl_error("ncclAllGather", r);
     std::vector<Rec> recs(world);
     GGC_CUDA_TRY(cudaMemcpyAsync(recs.data(), drec, sizeof(Rec) * world, cudaMemcpyDeviceToHost, ctx->stream));
-    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    GGC_TRY(ctx_sync(ctx));
     bool ok = want;
     for (int p = 0; p < world && ok; ++p) {
         ok = recs[p].ok != 0;
@@ -1761,7 +1805,7 @@ int setup_allreduce(ggc_model* m) {
     if (r != ncclSuccess) return nccl_error("ncclAllReduce", r);
     int32_t all = 0;
     GGC_CUDA_TRY(cudaMemcpyAsync(&all, dok, sizeof(all), cudaMemcpyDeviceToHost, ctx->stream));
-    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    GGC_TRY(ctx_sync(ctx));
     if (!all) {
         for (void* q : m->ar_peer_maps) cudaIpcCloseMemHandle(q);
         m->ar_peer_maps.clear();
@@ -1818,6 +1862,7 @@ void destroy_model(ggc_model* m) {
         for (void* p : m->ar_peer_maps) cudaIpcCloseMemHandle(p);
         for (void* p : m->allocs) cudaFree(p);
         if (m->rb) cudaFreeHost(m->rb);
+        if (m->logits_host) cudaFreeHost(m->logits_host);
     }
     delete m;
     ctx_release(ctx);
@@ -2088,6 +2133,7 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
     GGC_TRY(dalloc(m.get(), &m->in_pos, hp.max_ctx));
     GGC_TRY(dalloc(m.get(), &m->out_ids, hp.max_ctx));
     GGC_CUDA_TRY(cudaMallocHost((void**)&m->rb, sizeof(*m->rb)));
+    GGC_CUDA_TRY(cudaMallocHost((void**)&m->logits_host, (size_t)hp.vocab_size * sizeof(float)));
     StepState s0{};
     s0.done = 1;
     s0.max_ctx = hp.max_ctx;
@@ -2105,7 +2151,7 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
         }
     }
     GGC_TRY(build_graph(m.get()));
-    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    GGC_TRY(ctx_sync(ctx));
     *out = m.release();
     return GGC_OK;
 }
@@ -2121,7 +2167,7 @@ namespace {
 int run_steps(ggc_model* m, uint64_t n_in, uint64_t max_new, int64_t eos, uint64_t steps) {
     ggc_ctx* ctx = m->ctx;
     int32_t ctl[6] = {0, (int32_t)n_in, (int32_t)max_new, (int32_t)(eos < 0 ? -1 : eos), 0, 0};
-    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));   // the pinned control block may still be in flight
+    GGC_TRY(ctx_sync(ctx));   // the pinned control block may still be in flight
     memcpy(&m->rb->ctl, ctl, sizeof(ctl));
     GGC_CUDA_TRY(cudaMemcpyAsync(m->st, &m->rb->ctl, sizeof(ctl), cudaMemcpyHostToDevice, ctx->stream));
     for (uint64_t i = 0; i < steps; ++i) {
@@ -2305,7 +2351,7 @@ int prefill_batch(ggc_model* m, const uint32_t* tokens, const int64_t* positions
     }
     int hf[ERRF_COUNT];
     GGC_CUDA_TRY(cudaMemcpyAsync(hf, m->errf, sizeof(hf), cudaMemcpyDeviceToHost, ctx->stream));
-    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    GGC_TRY(ctx_sync(ctx));
     const int status = errf_status(m, hf);
     if (status != GGC_OK) {
         cudaMemset(m->errf, 0, sizeof(int) * ERRF_COUNT);
@@ -2342,11 +2388,15 @@ extern "C" int ggc_model_forward(ggc_model* m, const uint32_t* tokens, const int
     GGC_CUDA_TRY(cudaMemcpyAsync(m->in_tok, tokens + first, (n - first) * sizeof(uint32_t), k1, ctx->stream));
     GGC_CUDA_TRY(cudaMemcpyAsync(m->in_pos, positions + first, (n - first) * sizeof(int64_t), k2, ctx->stream));
     GGC_TRY(run_steps(m, n - first, 0, -1, n - first));
-    if (logits) {
-        const cudaMemcpyKind k = is_device_ptr(logits) ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
-        GGC_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, (size_t)m->hp.vocab_size * sizeof(float), k, ctx->stream));
-    }
-    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    // host logits go through the model's pinned buffer: a copy into pageable memory
+    // would block the host until the stream drains, past ctx_sync's deadline
+    const size_t lbytes = (size_t)m->hp.vocab_size * sizeof(float);
+    const bool dev_logits = logits && is_device_ptr(logits);
+    if (logits)
+        GGC_CUDA_TRY(cudaMemcpyAsync(dev_logits ? (void*)logits : (void*)m->logits_host, m->logits, lbytes,
+                                     dev_logits ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, ctx->stream));
+    GGC_TRY(ctx_sync(ctx));
+    if (logits && !dev_logits) memcpy(logits, m->logits_host, lbytes);
     GGC_TRY(check_run(m));
     if (argmax) {
         const uint32_t id = (uint32_t)(m->rb->key & 0xFFFFFFFFull);
@@ -2380,7 +2430,7 @@ extern "C" int ggc_model_generate_greedy(ggc_model* m, const uint32_t* prompt, u
     GGC_CUDA_TRY(cudaMemcpyAsync(m->in_pos, pos.data() + first, rest * sizeof(int64_t), cudaMemcpyHostToDevice,
                                  ctx->stream));
     GGC_TRY(run_steps(m, rest, max_tokens, eos, rest + max_tokens));
-    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    GGC_TRY(ctx_sync(ctx));
     const uint64_t got = (uint64_t)m->rb->st.n_out;
     if (got) GGC_CUDA_TRY(cudaMemcpy(out_ids, m->out_ids, got * sizeof(uint32_t), cudaMemcpyDeviceToHost));
     *n_out = got;
@@ -2402,7 +2452,7 @@ extern "C" int ggc_model_decode(ggc_model* m, uint64_t steps, int64_t eos, int s
     ggc_ctx* ctx = m->ctx;
     DeviceGuard g(ctx->device);
     int32_t ctl[6] = {0, 0, (int32_t)steps, (int32_t)(eos < 0 ? -1 : eos), 0, 0};
-    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));   // the pinned control block may still be in flight
+    GGC_TRY(ctx_sync(ctx));   // the pinned control block may still be in flight
     memcpy(&m->rb->ctl, ctl, sizeof(ctl));
     GGC_CUDA_TRY(cudaMemcpyAsync(m->st, &m->rb->ctl, sizeof(ctl), cudaMemcpyHostToDevice, ctx->stream));
     GGC_CUDA_TRY(launch(ctx, k_decode_start, dim3(1), dim3(32), 0, m->st, (const unsigned long long*)m->argmax_key,
@@ -2424,7 +2474,7 @@ extern "C" int ggc_model_wait(ggc_model* m, uint32_t* out_ids, uint64_t* n_out) 
     GGC_CUDA_TRY(cudaMemcpyAsync(&m->rb->st, m->st, sizeof(StepState), cudaMemcpyDeviceToHost, ctx->stream));
     GGC_CUDA_TRY(cudaMemcpyAsync(m->rb->errf, m->errf, sizeof(int) * ERRF_COUNT, cudaMemcpyDeviceToHost, ctx->stream));
     GGC_CUDA_TRY(cudaMemcpyAsync(&m->rb->key, m->argmax_key, sizeof(unsigned long long), cudaMemcpyDeviceToHost, ctx->stream));
-    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    GGC_TRY(ctx_sync(ctx));
     const uint64_t got = (uint64_t)m->rb->st.n_out;
     if (out_ids && got) GGC_CUDA_TRY(cudaMemcpy(out_ids, m->out_ids, got * sizeof(uint32_t), cudaMemcpyDeviceToHost));
     if (n_out) *n_out = got;
@@ -2465,7 +2515,7 @@ extern "C" int ggc_sample(ggc_ctx* ctx, const float* logits, uint64_t vocab, con
                         (int*)(io + 1)));
     uint32_t res[2] = {0, 0};
     GGC_CUDA_TRY(cudaMemcpyAsync(res, io, sizeof(res), cudaMemcpyDeviceToHost, ctx->stream));
-    GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    GGC_TRY(ctx_sync(ctx));
     if (res[1]) return set_error(GGC_ERR_INFERENCE, "NaN in logits");
     *out_id = res[0];
     return GGC_OK;
@@ -2476,6 +2526,57 @@ extern "C" int ggc_model_sample(ggc_model* m, const ggc_sampler_config* cfg, con
                                 float u, uint32_t* out_id) {
     if (!m) return set_error(GGC_ERR_INVALID_ARG, "null model");
     return ggc_sample(m->ctx, m->logits, m->hp.vocab_size, cfg, seen, n_seen, u, out_id);
+}
+
+extern "C" int ggc_allreduce_probe(ggc_ctx* ctx, uint32_t rows, int peer_writes, const float* part0,
+                                   const float* part1, float* out) {
+    if (!ctx || !part0 || !part1 || !out || rows == 0) return set_error(GGC_ERR_INVALID_ARG, "null argument or no rows");
+    DeviceGuard g(ctx->device);
+    // the group's buffers: rank 0's receive words [2 phases][2 ranks][rows], a
+    // second buffer standing in for the peer's, the step counter, partials, result
+    const size_t words = 2u * 2u * rows;
+    unsigned long long* buf = nullptr;
+    float* d = nullptr;
+    uint32_t* step = nullptr;
+    ArGroup* dg = nullptr;
+    int* errf = nullptr;
+    int st = ctx_errf(ctx, &errf);
+    cudaError_t e = st == GGC_OK ? cudaMalloc(&buf, 2 * words * sizeof(unsigned long long)) : cudaErrorUnknown;
+    if (e == cudaSuccess) e = cudaMalloc(&d, 3u * rows * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&step, sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMalloc(&dg, sizeof(ArGroup));
+    if (e == cudaSuccess) e = cudaMemsetAsync(buf, 0, 2 * words * sizeof(unsigned long long), ctx->stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(errf, 0, sizeof(int) * ERRF_COUNT, ctx->stream);
+    ArGroup hg{};
+    hg.buf[0] = buf;
+    hg.buf[1] = buf + words;
+    hg.world = 2;
+    hg.rank = 0;
+    hg.stride = rows;
+    hg.step = step;
+    hg.per_step = 2;
+    const uint32_t one = 1;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(step, &one, sizeof(one), cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dg, &hg, sizeof(hg), cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d, part0, rows * sizeof(float), cudaMemcpyDefault, ctx->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d + rows, part1, rows * sizeof(float), cudaMemcpyDefault, ctx->stream);
+    if (e == cudaSuccess) {
+        k_ar_probe<<<1, 32, 0, ctx->stream>>>(dg, rows, d, d + rows, peer_writes, d + 2 * rows, errf);
+        e = cudaGetLastError();
+    }
+    int flags[ERRF_COUNT] = {0};
+    if (e == cudaSuccess) e = cudaMemcpyAsync(flags, errf, sizeof(flags), cudaMemcpyDeviceToHost, ctx->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, d + 2 * rows, rows * sizeof(float), cudaMemcpyDefault, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    cudaFree(buf);
+    cudaFree(d);
+    cudaFree(step);
+    cudaFree(dg);
+    if (st != GGC_OK) return st;
+    if (e != cudaSuccess) return set_error(GGC_ERR_CUDA, "allreduce probe: %s", cudaGetErrorString(e));
+    if (flags[ERRF_TIMEOUT])
+        return set_error(GGC_ERR_TIMEOUT, "all-reduce: the peer's partials did not arrive within the bounded poll");
+    return GGC_OK;
 }
 
 extern "C" int ggc_model_allreduce_kind(const ggc_model* m) {
@@ -2489,7 +2590,7 @@ extern "C" int ggc_model_truncate(ggc_model* m, uint64_t new_len) {
     DeviceGuard g(m->ctx->device);
     const uint32_t slot = (uint32_t)new_len;
     GGC_CUDA_TRY(cudaMemcpyAsync(&m->st->slot, &slot, sizeof(slot), cudaMemcpyHostToDevice, m->ctx->stream));
-    GGC_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    GGC_TRY(ctx_sync(m->ctx));
     m->cache_len = new_len;
     return GGC_OK;
 }
@@ -2524,7 +2625,7 @@ extern "C" int ggc_model_cache_append(ggc_model* m, uint32_t layer, const float*
         return set_error(GGC_ERR_KV_CACHE_OVERFLOW, "KvCacheOverflow { seq_len: %llu, max_seq: %u }",
                          (unsigned long long)(base + seq), m->hp.max_ctx);
     DeviceGuard g(m->ctx->device);
-    GGC_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    GGC_TRY(ctx_sync(m->ctx));
     const size_t layer_kv = (size_t)m->hp.max_ctx * m->kvdim * m->kv_elem;
     const size_t n = (size_t)seq * m->kvdim;
     uint8_t* kd = (uint8_t*)m->kcache + layer * layer_kv;
@@ -2555,7 +2656,7 @@ extern "C" int ggc_model_cache_read(ggc_model* m, uint32_t layer, float* k, floa
     if (!m || !k || !v) return set_error(GGC_ERR_INVALID_ARG, "null argument");
     if (layer >= m->hp.n_layers) return set_error(GGC_ERR_INVALID_ARG, "layer %u out of range", layer);
     DeviceGuard g(m->ctx->device);
-    GGC_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    GGC_TRY(ctx_sync(m->ctx));
     const size_t layer_kv = (size_t)m->hp.max_ctx * m->kvdim * m->kv_elem;
     const uint64_t len = m->cache_len;
     const size_t n = (size_t)len * m->kvdim;

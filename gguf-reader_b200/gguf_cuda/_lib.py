@@ -150,6 +150,7 @@ SIGNATURES = {
     "ggc_model_forward": (_i32, [_vp, _vp, _vp, _u64, _vp, _vp]),
     "ggc_model_cache_len": (_u64, [_vp]),
     "ggc_model_allreduce_kind": (_i32, [_vp]),
+    "ggc_allreduce_probe": (_i32, [_vp, _u32, _i32, _vp, _vp, _vp]),
     "ggc_model_sample": (_i32, [_vp, C.POINTER(SamplerConfig), _vp, _u64, C.c_float, C.POINTER(_u32)]),
     "ggc_ops_matvec": (_i32, [_vp, _vp, _u64, _u64, _u64, _vp, _u64, _vp, _u64, _vp]),
     "ggc_ops_matvec_colmajor": (_i32, [_vp, _vp, _u64, _u64, _u64, _vp, _u64, _vp, _u64, _vp]),

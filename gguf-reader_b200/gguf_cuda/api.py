@@ -200,6 +200,20 @@ def _hparams(hp: dict, max_ctx: int = 0, kv_f16: bool = False):
                      hp["n_layers"], float(hp["rope_freq_base"]), max_ctx, 1 if kv_f16 else 0)
 
 
+def allreduce_probe(part0, part1, peer_writes: bool = True, ctx: Context | None = None):
+    """One fused all-reduce step of a world-2 group on this GPU alone
+    (ggc_allreduce_probe): part0 + part1 when the peer's words are written; with
+    peer_writes=False they never arrive and DeviceTimeout is raised once the
+    bounded poll gives up."""
+    ctx = ctx or default_context()
+    p0 = np.ascontiguousarray(part0, dtype=np.float32)
+    p1 = np.ascontiguousarray(part1, dtype=np.float32)
+    out = np.zeros_like(p0)
+    check(lib().ggc_allreduce_probe(ctx.h, p0.size, 1 if peer_writes else 0, p0.ctypes.data, p1.ctypes.data,
+                                    out.ctypes.data))
+    return out
+
+
 def tp_plan(hp: dict, attn_output_dtype: int, ffn_down_dtype: int, rank: int, world: int) -> dict:
     """The tensor-parallel shard of one layer kept by `rank` of `world` (ggc_tp_plan):
     q heads, kv heads and ffn rows as (first, count) pairs."""

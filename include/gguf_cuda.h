@@ -277,6 +277,15 @@ int ggc_model_sample(ggc_model* m, const ggc_sampler_config* cfg, const uint32_t
  * (none), 1 = NCCL all-reduce, 2 = fused into the GEMVs over peer memory. */
 int ggc_model_allreduce_kind(const ggc_model* m);
 
+/* No counterpart in the reference (a diagnostic of the fused tensor-parallel
+ * all-reduce's bounded wait, allreduce.cuh): one all-reduce step of a world-2
+ * group run on this GPU alone.  With peer_writes != 0 the peer's partials are
+ * stored too and out[r] = part0[r] + part1[r] (rank order); with 0 they never
+ * arrive, the bounded poll gives up and the call returns GGC_ERR_TIMEOUT after
+ * about a second, the context staying usable.  Host or device part0/part1/out. */
+int ggc_allreduce_probe(ggc_ctx* ctx, uint32_t rows, int peer_writes, const float* part0, const float* part1,
+                        float* out);
+
 /* Number of kernels this context launched so far (for launch accounting). */
 uint64_t ggc_ctx_kernel_launches(ggc_ctx* ctx);
 

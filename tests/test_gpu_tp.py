@@ -42,29 +42,79 @@ def _need_gpus():
         pytest.skip(f"needs {WORLD} GPUs")
 
 
-def _worker(rank, world, nid, job, q, allreduce):
-    """One rank: build the sharded model and run `job` (same calls on every rank)."""
-    if allreduce == "nccl":
-        os.environ["GGC_TP_ALLREDUCE"] = "nccl"
-    else:
-        os.environ.pop("GGC_TP_ALLREDUCE", None)
+class LostRankJob:
+    """A rank lost between steps, in the form that faults no GPU: every rank makes
+    the model (its set-up collectives complete), then rank 0 forwards a token
+    through the NCCL all-reduce path while the others stay alive and idle,
+    never joining it.  Rank 0's wait must end at the host deadline
+    (GGC_NCCL_TIMEOUT_MS) with the communicator aborted and an NcclError, not hang;
+    the idle ranks leave afterwards without touching their communicators."""
+
+    def __call__(self, ggc, ctx):
+        import time
+        os.environ["GGC_NCCL_TIMEOUT_MS"] = "4000"
+        hp, ts = synth.make_model(dict(MINI, weights=0, qkv_bias=False), seed=2)
+        m = ggc.LlamaModel(hp, ts, max_ctx=8, ctx=ctx)
+        if ctx.rank != 0:
+            time.sleep(12)
+            return "idle"
+        t0 = time.perf_counter()
+        try:
+            m.forward([1], [0])
+            return "completed"
+        except ggc.NcclError as e:
+            return f"NcclError after {time.perf_counter() - t0:.1f} s: {e}"
+
+
+def _worker(rank, world, nid, jobs, q):
+    """One rank: one context, then every job (same calls on every rank), each
+    with its all-reduce path (GGC_TP_ALLREDUCE is read when a model is made).
+    A collective that never completes ends at the library's host deadline."""
+    import time
+    os.environ.setdefault("GGC_NCCL_TIMEOUT_MS", "120000")
+    out = {}
     try:
         import torch  # noqa: F401  -- loads the NCCL the parent's unique id came from
         import gguf_cuda as ggc
         ctx = ggc.Context(device=rank, rank=rank, world=world, nccl_id=nid)
-        q.put((rank, job(ggc, ctx)))
-    except Exception as e:   # reported to the parent (as text: the library's errors do not pickle)
-        q.put((rank, RuntimeError(f"rank {rank}: {type(e).__name__}: {e}")))
+        log = os.environ.get("GGC_TEST_TP_LOG")
+        for key, job, allreduce in jobs:
+            if log:   # progress per rank, so a stall names its job
+                with open(f"{log}.rank{rank}", "a") as f:
+                    f.write(f"{time.time():.1f} start {key}\n")
+            if allreduce == "nccl":
+                os.environ["GGC_TP_ALLREDUCE"] = "nccl"
+            else:
+                os.environ.pop("GGC_TP_ALLREDUCE", None)
+            try:
+                out[key] = job(ggc, ctx)
+            except Exception as e:   # reported to the parent (as text: the library's errors do not pickle)
+                out[key] = RuntimeError(f"rank {rank}: {type(e).__name__}: {e}")
+            if log:
+                with open(f"{log}.rank{rank}", "a") as f:
+                    f.write(f"{time.time():.1f} done {key}\n")
+    except Exception as e:
+        out = RuntimeError(f"rank {rank}: {type(e).__name__}: {e}")
+    q.put((rank, out))
+    if any(key == ("lost",) for key, _, _ in jobs):
+        # the lost-rank job leaves communicators that must not be destroyed
+        # collectively (rank 0's is aborted, the others never joined it): exit as is
+        q.close()
+        q.join_thread()
+        os._exit(0)
 
 
-def run_ranks(job, timeout=600, allreduce="peer"):
+def run_ranks(jobs, timeout=1200):
+    """Spawns WORLD ranks once and runs `jobs` [(key, job, allreduce)] in each;
+    returns {key: [result of rank 0, rank 1, ...]}."""
     import multiprocessing as mp
     import torch  # noqa: F401  -- the library binds the NCCL already loaded (PyTorch's)
     import gguf_cuda as ggc
+    os.environ["NCCL_NVLS_ENABLE"] = "0"   # no NVLink multicast objects while a rank may leave
     nid = ggc.Context.nccl_unique_id()
     mctx = mp.get_context("spawn")
     q = mctx.Queue()
-    procs = [mctx.Process(target=_worker, args=(r, WORLD, nid, job, q, allreduce)) for r in range(WORLD)]
+    procs = [mctx.Process(target=_worker, args=(r, WORLD, nid, jobs, q)) for r in range(WORLD)]
     for p in procs:
         p.start()
     try:
@@ -74,7 +124,10 @@ def run_ranks(job, timeout=600, allreduce="peer"):
             p.join(timeout=120)
             if p.is_alive():
                 p.kill()
-    return [res[r] for r in range(WORLD)]
+    for r in range(WORLD):
+        if isinstance(res[r], Exception):
+            raise res[r]
+    return {key: [res[r][key] for r in range(WORLD)] for key, _, _ in jobs}
 
 
 class PromptJob:
@@ -93,14 +146,30 @@ class PromptJob:
         return dict(logits=logits, k=k, v=v, step=step, ids=ids, cache_len=m.cache_len(), allreduce=m.allreduce)
 
 
+@pytest.fixture(scope="module")
+def tp_results():
+    """Every job of this module in one spawn of WORLD ranks."""
+    _need_gpus()
+    jobs = []
+    for allreduce in ("peer", "nccl"):
+        for name, cfg, n_layers, vocab in CASES:
+            hp = synth.hparams(cfg if isinstance(cfg, dict) else synth.CONFIGS[cfg], n_layers)
+            if hp["n_kv_heads"] % WORLD == 0:
+                jobs.append((("prompt", name, allreduce), PromptJob(cfg, n_layers, vocab), allreduce))
+        if 2 % WORLD == 0:
+            jobs.append((("nan", allreduce), NanJob(), allreduce))
+    jobs.append((("long",), LongPromptJob(), "peer"))
+    jobs.append((("lost",), LostRankJob(), "nccl"))   # last: it aborts rank 0's communicator
+    return run_ranks(jobs)
+
+
 @pytest.mark.parametrize("allreduce", ["peer", "nccl"])
 @pytest.mark.parametrize("name,cfg,n_layers,vocab", CASES, ids=[c[0] for c in CASES])
-def test_tp_matches_oracle(ggc, orc, name, cfg, n_layers, vocab, allreduce):
-    _need_gpus()
+def test_tp_matches_oracle(ggc, orc, tp_results, name, cfg, n_layers, vocab, allreduce):
     hp, ts = synth.make_model(cfg, n_layers=n_layers, seed=0, vocab_size=vocab)
     if hp["n_kv_heads"] % WORLD:
         pytest.skip(f"{WORLD} ranks do not divide {hp['n_kv_heads']} kv heads")
-    res = run_ranks(PromptJob(cfg, n_layers, vocab), allreduce=allreduce)
+    res = tp_results[("prompt", name, allreduce)]
     for r in res:
         if isinstance(r, Exception):
             raise r
@@ -144,9 +213,8 @@ class LongPromptJob:
         return dict(logits=logits, ids=ids)
 
 
-def test_tp_long_prompt_prefill_matches_oracle(ggc, orc):
-    _need_gpus()
-    res = run_ranks(LongPromptJob())
+def test_tp_long_prompt_prefill_matches_oracle(ggc, orc, tp_results):
+    res = tp_results[("long",)]
     for r in res:
         if isinstance(r, Exception):
             raise r
@@ -179,10 +247,40 @@ class NanJob:
 
 
 @pytest.mark.parametrize("allreduce", ["peer", "nccl"])
-def test_tp_nan_guard_same_on_every_rank(ggc, allreduce):
-    _need_gpus()
+def test_tp_nan_guard_same_on_every_rank(ggc, tp_results, allreduce):
     if 2 % WORLD:
         pytest.skip("the planted model has 2 kv heads")
-    res = run_ranks(NanJob(), allreduce=allreduce)
+    res = tp_results[("nan", allreduce)]
     for r in res:
         assert isinstance(r, str) and "NaN after layer 0 attention" in r, r
+
+
+# ---- the fused all-reduce's bounded wait, on one GPU ------------------------------
+def test_allreduce_probe_sums_in_rank_order(ggc, ctx):
+    rng = np.random.default_rng(3)
+    p0 = rng.normal(size=1000).astype(np.float32)
+    p1 = rng.normal(size=1000).astype(np.float32)
+    got = ggc.allreduce_probe(p0, p1, peer_writes=True, ctx=ctx)
+    assert np.array_equal(got, (p0 + p1).astype(np.float32))
+
+
+def test_allreduce_probe_lost_peer_times_out_and_context_stays_usable(ggc, ctx):
+    """The peer's words never arrive: the poll gives up (a bounded wait, no GPU
+    fault or hang), the call returns DeviceTimeout, and the context still works."""
+    import time
+    p = np.ones(64, np.float32)
+    t0 = time.perf_counter()
+    with pytest.raises(ggc.DeviceTimeout, match="bounded poll"):
+        ggc.allreduce_probe(p, p, peer_writes=False, ctx=ctx)
+    assert time.perf_counter() - t0 < 30
+    assert np.array_equal(ggc.allreduce_probe(p, 2 * p, peer_writes=True, ctx=ctx), 3 * p)
+
+
+def test_tp_lost_rank_ends_in_nccl_error_at_the_host_deadline(ggc, tp_results):
+    res = tp_results[("lost",)]
+    for r in res:
+        if isinstance(r, Exception):
+            raise r
+    assert res[0].startswith("NcclError after"), res[0]
+    assert float(res[0].split()[2]) < 10.0
+    assert all(r == "idle" for r in res[1:])

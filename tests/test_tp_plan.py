@@ -143,3 +143,47 @@ def test_gloo_two_ranks_partial_sums_equal_full_product(ggc, orc):
         total = 1024 if name == "attn_output" else 2816
         assert_partition(spans, total)
     assert errs["ffn_down"][1] == [(0, 1536), (1536, 1280)]
+
+
+def _gloo_withholding_rank(rank, world, port, out_q):
+    """Rank 1 computes its shard but never joins the all-reduce (a rank lost
+    between steps); rank 0's collective must end with an error after the short
+    process-group timeout instead of waiting forever."""
+    import os
+    import time
+    from datetime import timedelta
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch
+    import torch.distributed as dist
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=3))
+    partial = torch.ones(64)
+    if rank == 1:
+        time.sleep(8)          # alive, but withholding its partial sum
+        out_q.put((rank, "withheld"))
+        return
+    t0 = time.perf_counter()
+    try:
+        dist.all_reduce(partial)
+        out_q.put((rank, "completed"))
+    except Exception as e:   # the timeout surfaces as an exception on the waiting rank
+        out_q.put((rank, f"error after {time.perf_counter() - t0:.1f} s: {type(e).__name__}"))
+
+
+def test_gloo_rank_withholding_its_partial_ends_the_others_collective_with_an_error():
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gloo_withholding_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        res = dict(q.get(timeout=60) for _ in procs)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    assert res[1] == "withheld"
+    assert res[0].startswith("error after"), res[0]
+    assert float(res[0].split()[2]) < 8.0
