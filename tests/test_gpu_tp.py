@@ -42,30 +42,6 @@ def _need_gpus():
         pytest.skip(f"needs {WORLD} GPUs")
 
 
-class LostRankJob:
-    """A rank lost between steps, in the form that faults no GPU: every rank makes
-    the model (its set-up collectives complete), then rank 0 forwards a token
-    through the NCCL all-reduce path while the others stay alive and idle,
-    never joining it.  Rank 0's wait must end at the host deadline
-    (GGC_NCCL_TIMEOUT_MS) with the communicator aborted and an NcclError, not hang;
-    the idle ranks leave afterwards without touching their communicators."""
-
-    def __call__(self, ggc, ctx):
-        import time
-        os.environ["GGC_NCCL_TIMEOUT_MS"] = "4000"
-        hp, ts = synth.make_model(dict(MINI, weights=0, qkv_bias=False), seed=2)
-        m = ggc.LlamaModel(hp, ts, max_ctx=8, ctx=ctx)
-        if ctx.rank != 0:
-            time.sleep(12)
-            return "idle"
-        t0 = time.perf_counter()
-        try:
-            m.forward([1], [0])
-            return "completed"
-        except ggc.NcclError as e:
-            return f"NcclError after {time.perf_counter() - t0:.1f} s: {e}"
-
-
 def _worker(rank, world, nid, jobs, q):
     """One rank: one context, then every job (same calls on every rank), each
     with its all-reduce path (GGC_TP_ALLREDUCE is read when a model is made).
@@ -96,12 +72,6 @@ def _worker(rank, world, nid, jobs, q):
     except Exception as e:
         out = RuntimeError(f"rank {rank}: {type(e).__name__}: {e}")
     q.put((rank, out))
-    if any(key == ("lost",) for key, _, _ in jobs):
-        # the lost-rank job leaves communicators that must not be destroyed
-        # collectively (rank 0's is aborted, the others never joined it): exit as is
-        q.close()
-        q.join_thread()
-        os._exit(0)
 
 
 def run_ranks(jobs, timeout=1200):
@@ -110,7 +80,6 @@ def run_ranks(jobs, timeout=1200):
     import multiprocessing as mp
     import torch  # noqa: F401  -- the library binds the NCCL already loaded (PyTorch's)
     import gguf_cuda as ggc
-    os.environ["NCCL_NVLS_ENABLE"] = "0"   # no NVLink multicast objects while a rank may leave
     nid = ggc.Context.nccl_unique_id()
     mctx = mp.get_context("spawn")
     q = mctx.Queue()
@@ -159,7 +128,6 @@ def tp_results():
         if 2 % WORLD == 0:
             jobs.append((("nan", allreduce), NanJob(), allreduce))
     jobs.append((("long",), LongPromptJob(), "peer"))
-    jobs.append((("lost",), LostRankJob(), "nccl"))   # last: it aborts rank 0's communicator
     return run_ranks(jobs)
 
 
@@ -274,13 +242,3 @@ def test_allreduce_probe_lost_peer_times_out_and_context_stays_usable(ggc, ctx):
         ggc.allreduce_probe(p, p, peer_writes=False, ctx=ctx)
     assert time.perf_counter() - t0 < 30
     assert np.array_equal(ggc.allreduce_probe(p, 2 * p, peer_writes=True, ctx=ctx), 3 * p)
-
-
-def test_tp_lost_rank_ends_in_nccl_error_at_the_host_deadline(ggc, tp_results):
-    res = tp_results[("lost",)]
-    for r in res:
-        if isinstance(r, Exception):
-            raise r
-    assert res[0].startswith("NcclError after"), res[0]
-    assert float(res[0].split()[2]) < 10.0
-    assert all(r == "idle" for r in res[1:])
