@@ -251,41 +251,54 @@ def tp_mode(args, world):
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
-def gemv_roofline(ggc, ctx, torch, stream, peak_gbs):
-    """Dominant kernel (k_gemv<Q4_K>, the 11008 x 4096 ffn shape) timed live with
-    CUDA events over back-to-back launches on rotating weight copies (> 2x L2)."""
+def time_matvec(ggc, ctx, torch, stream, dt, rows, cols, peak_gbs, seed=77, min_reps=200):
+    """One weight shape timed live with CUDA events over back-to-back launches
+    (ggc_tensor_matvec_batch: no host call per launch) on rotating copies of the
+    weight whose total exceeds 2x L2, so every launch streams from HBM."""
     from gguf_cuda import synth
+    raw = synth.random_blocks(dt, rows * cols, synth.rng_for(seed, dt, rows, cols))
+    wbytes = raw.nbytes
+    copies = max(2, int(np.ceil(2 * 126e6 / wbytes)) + 1)
+    tensors = [ggc.Tensor(raw, dt, (cols, rows), ctx=ctx) for _ in range(copies)]
+    x = torch.randn(cols, device="cuda", dtype=torch.float32)
+    y = torch.empty(rows, device="cuda", dtype=torch.float32)
+    torch.cuda.synchronize()
+    for t in tensors:
+        t.matvec(x, y)
+    ctx.synchronize()
+    reps = max(3, min_reps // copies) * copies
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    seq = [tensors[i % copies] for i in range(reps)]
+    name = f"{ggc.DTYPE_NAMES[dt]}_{rows}x{cols}"
+    torch.cuda.nvtx.range_push(f"matvec_{name}")   # ncu --nvtx-include "matvec_<name>/" picks these launches
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        ggc.Tensor.matvec_batch(seq, x, y)
+        e1.record(stream)
+    torch.cuda.nvtx.range_pop()
+    e1.synchronize()
+    per = e0.elapsed_time(e1) / 1e3 / reps
+    alg = wbytes + 4 * cols + 4 * rows
+    del tensors
+    return name, {"us_per_launch": per * 1e6, "algorithmic_bytes": alg, "gbs": alg / per / 1e9,
+                  "frac_of_peak": alg / per / 1e9 / peak_gbs,
+                  "kernel": "k_gemv_span" if dt in (ggc.Q4_K, ggc.Q6_K, ggc.Q4_0, ggc.Q8_0) else "k_gemv"}
+
+
+SWEEP_SHAPES = [(4096, 4096), (11008, 4096), (4096, 11008)]
+
+
+def gemv_roofline(ggc, ctx, torch, stream, peak_gbs):
+    """The dominant kernel (k_gemv_span<Q4_K> at the 11008 x 4096 ffn shape) and the
+    format sweep: the 15 quantized and half formats at 4096 x 4096, 11008 x 4096 and
+    4096 x 11008 (rows x cols), each timed as time_matvec does."""
     out = {}
-    rows, cols = 11008, 4096
-    shapes = {"Q4_K_11008x4096": (ggc.Q4_K, 11008, 4096), "Q6_K_4096x11008": (ggc.Q6_K, 4096, 11008),
-              "Q4_0_4096x4096": (ggc.Q4_0, 4096, 4096), "Q4_K_4096x4096": (ggc.Q4_K, 4096, 4096),
-              "Q8_0_4096x4096": (ggc.Q8_0, 4096, 4096)}
-    for name, (dt, rows, cols) in shapes.items():
-        raw = synth.random_blocks(dt, rows * cols, synth.rng_for(77, dt))
-        wbytes = raw.nbytes
-        copies = max(2, int(np.ceil(2 * 126e6 / wbytes)) + 1)
-        tensors = [ggc.Tensor(raw, dt, (cols, rows), ctx=ctx) for _ in range(copies)]
-        x = torch.randn(cols, device="cuda", dtype=torch.float32)
-        y = torch.empty(rows, device="cuda", dtype=torch.float32)
-        torch.cuda.synchronize()
-        for t in tensors:
-            t.matvec(x, y)
-        ctx.synchronize()
-        reps = max(3, 200 // copies) * copies
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        seq = [tensors[i % copies] for i in range(reps)]
-        torch.cuda.nvtx.range_push(f"matvec_{name}")   # ncu --nvtx-include "matvec_<name>/" picks these launches
-        with torch.cuda.stream(stream):
-            e0.record(stream)
-            ggc.Tensor.matvec_batch(seq, x, y)           # back to back from C: no host call per launch
-            e1.record(stream)
-        torch.cuda.nvtx.range_pop()
-        e1.synchronize()
-        per = e0.elapsed_time(e1) / 1e3 / reps
-        alg = wbytes + 4 * cols + 4 * rows
-        out[name] = {"us_per_launch": per * 1e6, "algorithmic_bytes": alg, "gbs": alg / per / 1e9,
-                     "frac_of_peak": alg / per / 1e9 / peak_gbs}
-        del tensors
+    for dt in [d for d in ggc.ALL_DTYPES if d != ggc.F32]:
+        for rows, cols in SWEEP_SHAPES:
+            name, rec = time_matvec(ggc, ctx, torch, stream, dt, rows, cols, peak_gbs, min_reps=60)
+            out[name] = rec
+    name, rec = time_matvec(ggc, ctx, torch, stream, ggc.Q4_K, 11008, 4096, peak_gbs)   # the roofline line: more reps
+    out[name] = rec
     return out
 
 
@@ -583,6 +596,7 @@ def run_ours(args, rank, world, local_rank):
         model_gbs = gpu_bytes * (K / elapsed) / 1e9   # per GPU
         rl = gemv_roofline(ggc, ctx, torch, stream, peak_gbs)
         dom = rl["Q4_K_11008x4096"]
+        sweep_fracs = {k: round(v["frac_of_peak"], 3) for k, v in rl.items()}
         tr = traffic_record().get("k_gemv_span<Q4_K> 11008x4096")
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
@@ -607,6 +621,7 @@ def run_ours(args, rank, world, local_rank):
                                "frac": model_gbs / peak_gbs, "bound_tokens_s": peak_gbs * 1e9 / gpu_bytes * streams},
             "tp_parity": parity,
             "matvec": rl,
+            "matvec_frac_summary": sweep_fracs,
             "prefill": prefill,
             "configs": configs,
             "clocks": sampler.record(),
