@@ -66,6 +66,8 @@ def parse_args():
     ap.add_argument("--prefill", type=int, default=512, help="prompt tokens of the prefill measurement (0: skip)")
     ap.add_argument("--no-configs", dest="configs", action="store_false",
                     help="skip the Qwen2-0.5B and Llama-3-8B workloads")
+    ap.add_argument("--no-matvec-sweep", dest="sweep", action="store_false",
+                    help="time only the roofline matvec, not the 15-format x 3-shape sweep")
     return ap.parse_args()
 
 
@@ -288,12 +290,12 @@ def time_matvec(ggc, ctx, torch, stream, dt, rows, cols, peak_gbs, seed=77, min_
 SWEEP_SHAPES = [(4096, 4096), (11008, 4096), (4096, 11008)]
 
 
-def gemv_roofline(ggc, ctx, torch, stream, peak_gbs):
+def gemv_roofline(ggc, ctx, torch, stream, peak_gbs, sweep=True):
     """The dominant kernel (k_gemv_span<Q4_K> at the 11008 x 4096 ffn shape) and the
     format sweep: the 15 quantized and half formats at 4096 x 4096, 11008 x 4096 and
     4096 x 11008 (rows x cols), each timed as time_matvec does."""
     out = {}
-    for dt in [d for d in ggc.ALL_DTYPES if d != ggc.F32]:
+    for dt in [d for d in ggc.ALL_DTYPES if d != ggc.F32] if sweep else []:
         for rows, cols in SWEEP_SHAPES:
             name, rec = time_matvec(ggc, ctx, torch, stream, dt, rows, cols, peak_gbs, min_reps=60)
             out[name] = rec
@@ -594,7 +596,7 @@ def run_ours(args, rank, world, local_rank):
         lm_bytes = int(ts[2]["raw"].nbytes)
         gpu_bytes = (w_bytes - lm_bytes + kv_bytes) / world + lm_bytes if tp else step_bytes
         model_gbs = gpu_bytes * (K / elapsed) / 1e9   # per GPU
-        rl = gemv_roofline(ggc, ctx, torch, stream, peak_gbs)
+        rl = gemv_roofline(ggc, ctx, torch, stream, peak_gbs, sweep=args.sweep)
         dom = rl["Q4_K_11008x4096"]
         sweep_fracs = {k: round(v["frac_of_peak"], 3) for k, v in rl.items()}
         tr = traffic_record().get("k_gemv_span<Q4_K> 11008x4096")
