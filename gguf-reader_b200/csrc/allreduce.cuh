@@ -65,22 +65,32 @@ __device__ __forceinline__ void ar_store_rows(const ArGroup& g, uint32_t k, cons
 }
 
 // Sum of the ranks' partials of one row, in rank order, into out[row].
-// Returns false when a word did not arrive within the poll limit.
+// The world's words are loaded together (one memory round trip, not one per
+// rank) and only the ones still missing are polled again.  Returns false when a
+// word did not arrive within the poll limit.
 __device__ __forceinline__ bool ar_reduce_row(const ArGroup& g, uint32_t ph, uint32_t epoch, uint32_t row, float* out,
                                               const int* errf, bool* nan) {
     const unsigned long long* b = g.buf[g.rank] + (size_t)ph * g.world * g.stride + row;
+    unsigned long long w[AR_MAX_WORLD];
+    uint32_t missing = (1u << g.world) - 1u;
+    for (uint32_t it = 0;; ++it) {
+#pragma unroll
+        for (int r = 0; r < AR_MAX_WORLD; ++r)
+            if ((missing >> r) & 1u) w[r] = ld_relaxed_sys_u64(b + (size_t)r * g.stride);
+#pragma unroll
+        for (int r = 0; r < AR_MAX_WORLD; ++r)
+            if (((missing >> r) & 1u) && (uint32_t)(w[r] >> 32) == epoch) missing &= ~(1u << r);
+        if (!missing) break;
+        if (it >= AR_WAIT_LIMIT || ((it & 1023u) == 1023u && *(volatile const int*)&errf[ERRF_TIMEOUT])) return false;
+        __nanosleep(it < 64 ? 20 : 100);
+    }
     float v = 0.f;
-    for (int r = 0; r < g.world; ++r) {
-        unsigned long long w;
-        for (uint32_t it = 0;; ++it) {
-            w = ld_relaxed_sys_u64(b + (size_t)r * g.stride);
-            if ((uint32_t)(w >> 32) == epoch) break;
-            if (it >= AR_WAIT_LIMIT || ((it & 1023u) == 1023u && *(volatile const int*)&errf[ERRF_TIMEOUT]))
-                return false;
-            __nanosleep(it < 64 ? 20 : 100);
+#pragma unroll
+    for (int r = 0; r < AR_MAX_WORLD; ++r) {
+        if (r < g.world) {
+            const float x = __uint_as_float((uint32_t)w[r]);
+            v = r == 0 ? x : __fadd_rn(v, x);
         }
-        const float x = __uint_as_float((uint32_t)w);
-        v = r == 0 ? x : __fadd_rn(v, x);
     }
     out[row] = v;
     *nan |= isnan(v);

@@ -34,9 +34,12 @@
 // ERRF_TIMEOUT, stops computing, still drains every tile its producer issued and
 // still counts its ops, so no CTA waits forever.
 //
-// Formats.  One consumer body serves the four span formats, switching on the op's
-// format inside the row product and the limb conversion (a uniform branch): one
-// body per format, inlined side by side into the op loop, made the compiler spill.
+// Formats.  The consumer body switches on the op's format (a uniform branch) among
+// the formats of the kernel instance's mask: each chain launches the instance of
+// exactly its ops' formats (15 instances), so the instruction cache holds only
+// their code.  One body per format, inlined side by side into the op loop of a
+// single all-format instance, made the compiler spill and the warps wait on
+// instruction fetch.
 //
 // x.  Per op the consumers convert x into span limbs as k_gemv_span does; for an
 // RMSNorm input of up to 4096 elements x and the norm weight are read once into

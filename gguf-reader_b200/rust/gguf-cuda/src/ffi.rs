@@ -152,4 +152,8 @@ extern "C" {
                       seen: *const u32, n_seen: u64, u: f32, out_id: *mut u32) -> c_int;
     pub fn ggc_model_sample(m: *mut ggc_model, cfg: *const ggc_sampler_config, seen: *const u32, n_seen: u64,
                             u: f32, out_id: *mut u32) -> c_int;
+
+    // the fused all-reduce's bounded wait, on one GPU
+    pub fn ggc_allreduce_probe(ctx: *mut ggc_ctx, rows: u32, peer_writes: c_int, part0: *const f32,
+                               part1: *const f32, out: *mut f32) -> c_int;
 }

@@ -31,6 +31,15 @@ def test_python_binding_covers_header(ggc):
     assert set(declared_symbols()) <= set(SIGNATURES)
 
 
+def test_rust_ffi_declares_every_header_symbol():
+    """The gguf-cuda crate's raw bindings name each C entry point once (no Rust
+    toolchain here, so the declarations are checked as text)."""
+    ffi = (ROOT / "gguf-reader_b200" / "rust" / "gguf-cuda" / "src" / "ffi.rs").read_text()
+    rust = re.findall(r"pub fn (ggc_[a-z0-9_]+)\s*\(", ffi)
+    assert len(rust) == len(set(rust))
+    assert sorted(set(rust)) == declared_symbols()
+
+
 def test_block_geometry(ggc):
     from gguf_cuda._lib import BLOCK
     for dt, (bs, bb) in BLOCK.items():
