@@ -769,7 +769,8 @@ extern "C" int ggc_tensor_upload(ggc_ctx* ctx, const void* raw, uint64_t bytes, 
         t->repacked = true;
     } else {
         GGC_CUDA_TRY(cudaMalloc(&t->raw, need + 16));   // 16 bytes of slack: the product's aligned row windows
-        GGC_CUDA_TRY(cudaMemcpy(t->raw, raw, need, cudaMemcpyHostToDevice));
+        GGC_CUDA_TRY(cudaMemcpyAsync(t->raw, raw, need, cudaMemcpyDefault, ctx->stream));
+        GGC_TRY(ctx_sync(ctx));
         t->raw_bytes = need;
     }
     ctx->refs++;
@@ -973,7 +974,7 @@ struct RunMM {
 int ctx_errf(ggc_ctx* ctx, int** out) {
     if (!ctx->errf) {
         GGC_CUDA_TRY(cudaMalloc(&ctx->errf, sizeof(int) * ERRF_COUNT));
-        GGC_CUDA_TRY(cudaMemset(ctx->errf, 0, sizeof(int) * ERRF_COUNT));
+        GGC_CUDA_TRY(cudaMemsetAsync(ctx->errf, 0, sizeof(int) * ERRF_COUNT, ctx->stream));
     }
     *out = ctx->errf;
     return GGC_OK;
@@ -1031,7 +1032,7 @@ extern "C" int ggc_tensor_matmul(ggc_ctx* ctx, const ggc_tensor* t, const float*
     if (staged) GGC_CUDA_TRY(cudaMemcpyAsync(y, dy, m * rows * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
     GGC_TRY(ctx_sync(ctx));
     if (hf[ERRF_TIMEOUT]) {
-        cudaMemset(errf, 0, sizeof(int) * ERRF_COUNT);
+        cudaMemsetAsync(errf, 0, sizeof(int) * ERRF_COUNT, ctx->stream);
         return set_error(GGC_ERR_TIMEOUT, "a bounded device wait expired");
     }
     return GGC_OK;
@@ -1403,7 +1404,10 @@ template <class T>
 int dalloc(ggc_model* m, T** p, size_t count) {
     void* q = nullptr;
     GGC_CUDA_TRY(cudaMalloc(&q, count * sizeof(T) + 16));
-    GGC_CUDA_TRY(cudaMemset(q, 0, count * sizeof(T) + 16));
+    // on the context stream: it is non-blocking, so a fill on the legacy default
+    // stream is not ordered with the uploads and kernels that follow on it (a late
+    // fill once zeroed freshly uploaded norm weights)
+    GGC_CUDA_TRY(cudaMemsetAsync(q, 0, count * sizeof(T) + 16, m->ctx->stream));
     m->allocs.push_back(q);
     *p = (T*)q;
     return GGC_OK;
@@ -1773,7 +1777,7 @@ int setup_allreduce(ggc_model* m) {
     int32_t* dok = nullptr;
     GGC_TRY(dalloc(m, (uint8_t**)&drec, sizeof(Rec) * (world + 1)));
     GGC_TRY(dalloc(m, &dok, 1));
-    GGC_CUDA_TRY(cudaMemcpy(drec + world, &mine, sizeof(Rec), cudaMemcpyHostToDevice));
+    GGC_CUDA_TRY(cudaMemcpyAsync(drec + world, &mine, sizeof(Rec), cudaMemcpyHostToDevice, ctx->stream));
     ncclResult_t r = nccl().AllGather(drec + world, drec, sizeof(Rec), ncclChar, ctx->comm, ctx->stream);
     if (r != ncclSuccess) return nccl_error("ncclAllGather", r);
     std::vector<Rec> recs(world);
@@ -1800,7 +1804,7 @@ int setup_allreduce(ggc_model* m) {
     }
     // every rank takes the same path
     const int32_t vote = ok ? 1 : 0;
-    GGC_CUDA_TRY(cudaMemcpy(dok, &vote, sizeof(vote), cudaMemcpyHostToDevice));
+    GGC_CUDA_TRY(cudaMemcpyAsync(dok, &vote, sizeof(vote), cudaMemcpyHostToDevice, ctx->stream));
     r = nccl().AllReduce(dok, dok, 1, ncclInt32, ncclMin, ctx->comm, ctx->stream);
     if (r != ncclSuccess) return nccl_error("ncclAllReduce", r);
     int32_t all = 0;
@@ -1819,7 +1823,8 @@ int setup_allreduce(ggc_model* m) {
     g.step = &m->st->ar_step;
     g.per_step = 2u * m->hp.n_layers;
     GGC_TRY(dalloc(m, &m->ar, 1));
-    GGC_CUDA_TRY(cudaMemcpy(m->ar, &g, sizeof(g), cudaMemcpyHostToDevice));
+    GGC_CUDA_TRY(cudaMemcpyAsync(m->ar, &g, sizeof(g), cudaMemcpyHostToDevice, ctx->stream));
+    GGC_TRY(ctx_sync(ctx));
     m->ar_p2p = true;
     return GGC_OK;
 }
@@ -1837,8 +1842,8 @@ int build_graph(ggc_model* m) {
     }
     GGC_CUDA_TRY(e);
     if (m->chain)
-        GGC_CUDA_TRY(cudaMemcpy(m->chain_ops, m->chain_host.data(), m->chain_host.size() * sizeof(ChainOp),
-                                cudaMemcpyHostToDevice));
+        GGC_CUDA_TRY(cudaMemcpyAsync(m->chain_ops, m->chain_host.data(), m->chain_host.size() * sizeof(ChainOp),
+                                     cudaMemcpyHostToDevice, ctx->stream));
     e = cudaGraphInstantiate(&m->graph, g, 0);
     cudaGraphDestroy(g);
     GGC_CUDA_TRY(e);
@@ -1939,7 +1944,8 @@ int upload_raw(ggc_model* m, const void* data, int dt, uint64_t r0, uint64_t n, 
     const uint64_t rb = cols / (uint64_t)block_size_of(dt) * (uint64_t)block_bytes_of(dt);
     uint8_t* d = nullptr;
     GGC_TRY(dalloc(m, &d, n * rb));
-    GGC_CUDA_TRY(cudaMemcpy(d, (const uint8_t*)data + r0 * rb, n * rb, cudaMemcpyHostToDevice));
+    GGC_CUDA_TRY(cudaMemcpyAsync(d, (const uint8_t*)data + r0 * rb, n * rb, cudaMemcpyDefault, m->ctx->stream));
+    GGC_TRY(ctx_sync(m->ctx));
     out.dtype = dt;
     out.rows = (uint32_t)n;
     out.cols = (uint32_t)cols;
@@ -2003,7 +2009,8 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
         m->embd_rows = e.nbytes / row_bytes;
         m->embd_dtype = e.dtype;
         GGC_TRY(dalloc(m.get(), &m->embd, m->embd_rows * row_bytes));
-        GGC_CUDA_TRY(cudaMemcpy(m->embd, e.data, m->embd_rows * row_bytes, cudaMemcpyHostToDevice));
+        GGC_CUDA_TRY(cudaMemcpyAsync(m->embd, e.data, m->embd_rows * row_bytes, cudaMemcpyDefault, ctx->stream));
+        GGC_TRY(ctx_sync(ctx));
     }
     GGC_TRY(upload_vec(m.get(), t[1], d, &m->output_norm, "output_norm"));
     if (!m->output_norm) return set_error(GGC_ERR_MISSING_TENSOR, "MissingTensor { name: output_norm, kind: tensor }");
@@ -2101,7 +2108,9 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
                 tab[(size_t)p * half + i] = make_float2(cosf(angle), sinf(angle));
             }
         GGC_TRY(dalloc(m.get(), &m->rope, tab.size()));
-        GGC_CUDA_TRY(cudaMemcpy(m->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+        GGC_CUDA_TRY(cudaMemcpyAsync(m->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice,
+                                     ctx->stream));
+        GGC_TRY(ctx_sync(ctx));
     }
     // fused attention: two resident CTAs per SM over (kv head, split); general pair: ~2 per SM, <= 64 splits
     m->attn = attn_decode_sel(hd, hp.kv_f16 != 0, hp.n_heads / hp.n_kv_heads);
@@ -2137,7 +2146,7 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
     StepState s0{};
     s0.done = 1;
     s0.max_ctx = hp.max_ctx;
-    GGC_CUDA_TRY(cudaMemcpy(m->st, &s0, sizeof(s0), cudaMemcpyHostToDevice));
+    GGC_CUDA_TRY(cudaMemcpyAsync(m->st, &s0, sizeof(s0), cudaMemcpyHostToDevice, ctx->stream));
     GGC_TRY(setup_allreduce(m.get()));
     {   // decode GEMVs as chains (chain.cuh), opt-in with GGC_DECODE_CHAIN=1 (slower than the per-op
         // kernels today: 369 vs 450 tokens/s on the Llama-2-7B Q4_K_M step), never around an NCCL all-reduce
@@ -2354,11 +2363,13 @@ int prefill_batch(ggc_model* m, const uint32_t* tokens, const int64_t* positions
     GGC_TRY(ctx_sync(ctx));
     const int status = errf_status(m, hf);
     if (status != GGC_OK) {
-        cudaMemset(m->errf, 0, sizeof(int) * ERRF_COUNT);
+        cudaMemsetAsync(m->errf, 0, sizeof(int) * ERRF_COUNT, ctx->stream);
+        cudaStreamSynchronize(ctx->stream);
         return status;
     }
     const uint32_t slot = (uint32_t)(base + count);
-    GGC_CUDA_TRY(cudaMemcpy(&m->st->slot, &slot, sizeof(slot), cudaMemcpyHostToDevice));
+    GGC_CUDA_TRY(cudaMemcpyAsync(&m->st->slot, &slot, sizeof(slot), cudaMemcpyHostToDevice, ctx->stream));
+    GGC_TRY(ctx_sync(ctx));
     m->cache_len = base + count;
     return GGC_OK;
 }
@@ -2400,7 +2411,10 @@ extern "C" int ggc_model_forward(ggc_model* m, const uint32_t* tokens, const int
     GGC_TRY(check_run(m));
     if (argmax) {
         const uint32_t id = (uint32_t)(m->rb->key & 0xFFFFFFFFull);
-        if (is_device_ptr(argmax)) GGC_CUDA_TRY(cudaMemcpy(argmax, &id, sizeof(id), cudaMemcpyHostToDevice));
+        if (is_device_ptr(argmax)) {
+            GGC_CUDA_TRY(cudaMemcpyAsync(argmax, &id, sizeof(id), cudaMemcpyHostToDevice, ctx->stream));
+            GGC_TRY(ctx_sync(ctx));
+        }
         else *argmax = id;
     }
     return GGC_OK;
@@ -2432,7 +2446,10 @@ extern "C" int ggc_model_generate_greedy(ggc_model* m, const uint32_t* prompt, u
     GGC_TRY(run_steps(m, rest, max_tokens, eos, rest + max_tokens));
     GGC_TRY(ctx_sync(ctx));
     const uint64_t got = (uint64_t)m->rb->st.n_out;
-    if (got) GGC_CUDA_TRY(cudaMemcpy(out_ids, m->out_ids, got * sizeof(uint32_t), cudaMemcpyDeviceToHost));
+    if (got) {
+        GGC_CUDA_TRY(cudaMemcpyAsync(out_ids, m->out_ids, got * sizeof(uint32_t), cudaMemcpyDefault, ctx->stream));
+        GGC_TRY(ctx_sync(ctx));
+    }
     *n_out = got;
     return check_run(m);
 }
@@ -2476,7 +2493,10 @@ extern "C" int ggc_model_wait(ggc_model* m, uint32_t* out_ids, uint64_t* n_out) 
     GGC_CUDA_TRY(cudaMemcpyAsync(&m->rb->key, m->argmax_key, sizeof(unsigned long long), cudaMemcpyDeviceToHost, ctx->stream));
     GGC_TRY(ctx_sync(ctx));
     const uint64_t got = (uint64_t)m->rb->st.n_out;
-    if (out_ids && got) GGC_CUDA_TRY(cudaMemcpy(out_ids, m->out_ids, got * sizeof(uint32_t), cudaMemcpyDeviceToHost));
+    if (out_ids && got) {
+        GGC_CUDA_TRY(cudaMemcpyAsync(out_ids, m->out_ids, got * sizeof(uint32_t), cudaMemcpyDefault, m->ctx->stream));
+        GGC_TRY(ctx_sync(m->ctx));
+    }
     if (n_out) *n_out = got;
     return check_run(m);
 }
@@ -2603,15 +2623,19 @@ namespace {
 int kv_rows_to_cache(ggc_model* m, uint8_t* layer, const void* src, uint64_t base, uint64_t seq, size_t esz) {
     const size_t hd = m->hd, kvdim = m->kvdim;
     for (uint32_t h = 0; h < m->kv_heads_l; ++h)
-        GGC_CUDA_TRY(cudaMemcpy2D(layer + ((size_t)h * m->hp.max_ctx + base) * hd * esz, hd * esz,
-                                  (const uint8_t*)src + h * hd * esz, kvdim * esz, hd * esz, seq, cudaMemcpyDefault));
+        GGC_CUDA_TRY(cudaMemcpy2DAsync(layer + ((size_t)h * m->hp.max_ctx + base) * hd * esz, hd * esz,
+                                       (const uint8_t*)src + h * hd * esz, kvdim * esz, hd * esz, seq, cudaMemcpyDefault,
+                                       m->ctx->stream));
+    GGC_TRY(ctx_sync(m->ctx));
     return GGC_OK;
 }
 int kv_cache_to_rows(ggc_model* m, const uint8_t* layer, void* dst, uint64_t seq, size_t esz) {
     const size_t hd = m->hd, kvdim = m->kvdim;
     for (uint32_t h = 0; h < m->kv_heads_l; ++h)
-        GGC_CUDA_TRY(cudaMemcpy2D((uint8_t*)dst + h * hd * esz, kvdim * esz, layer + (size_t)h * m->hp.max_ctx * hd * esz,
-                                  hd * esz, hd * esz, seq, cudaMemcpyDefault));
+        GGC_CUDA_TRY(cudaMemcpy2DAsync((uint8_t*)dst + h * hd * esz, kvdim * esz,
+                                       layer + (size_t)h * m->hp.max_ctx * hd * esz, hd * esz, hd * esz, seq,
+                                       cudaMemcpyDefault, m->ctx->stream));
+    GGC_TRY(ctx_sync(m->ctx));
     return GGC_OK;
 }
 }  // namespace
@@ -2646,7 +2670,8 @@ extern "C" int ggc_model_cache_append(ggc_model* m, uint32_t layer, const float*
     }
     if (layer == m->hp.n_layers - 1) {
         const uint32_t slot = (uint32_t)(base + seq);
-        GGC_CUDA_TRY(cudaMemcpy(&m->st->slot, &slot, sizeof(slot), cudaMemcpyHostToDevice));
+        GGC_CUDA_TRY(cudaMemcpyAsync(&m->st->slot, &slot, sizeof(slot), cudaMemcpyHostToDevice, m->ctx->stream));
+        GGC_TRY(ctx_sync(m->ctx));
         m->cache_len = base + seq;
     }
     return GGC_OK;
@@ -2669,8 +2694,9 @@ extern "C" int ggc_model_cache_read(ggc_model* m, uint32_t layer, float* k, floa
         GGC_TRY(kv_cache_to_rows(m, vd, hv.data(), len, 2));
         std::vector<float> fk(n), fv(n);
         for (size_t i = 0; i < n; ++i) { fk[i] = __half2float(hk[i]); fv[i] = __half2float(hv[i]); }
-        GGC_CUDA_TRY(cudaMemcpy(k, fk.data(), n * 4, cudaMemcpyDefault));
-        GGC_CUDA_TRY(cudaMemcpy(v, fv.data(), n * 4, cudaMemcpyDefault));
+        GGC_CUDA_TRY(cudaMemcpyAsync(k, fk.data(), n * 4, cudaMemcpyDefault, m->ctx->stream));
+        GGC_CUDA_TRY(cudaMemcpyAsync(v, fv.data(), n * 4, cudaMemcpyDefault, m->ctx->stream));
+        GGC_TRY(ctx_sync(m->ctx));
     } else {
         GGC_TRY(kv_cache_to_rows(m, kd, k, len, 4));
         GGC_TRY(kv_cache_to_rows(m, vd, v, len, 4));

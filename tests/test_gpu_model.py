@@ -283,3 +283,27 @@ def test_chain_decode_matches_oracle(ggc, orc, ctx, monkeypatch, name, cfg, n_la
         pos += 1
     assert ids == want_ids
     m.close()
+
+
+# ---- models built back to back on one context ----
+# A model's buffers are zero-filled and its norm weights and biases uploaded on the
+# context stream, which does not synchronise with the legacy default stream: a fill
+# issued there could land after an upload and zero the weights of whichever model
+# reused the memory of the one before (seen as a layer's RMSNorm weight reading 0,
+# the layer's q/k/v then equal to their biases).  Several models of one shape, each
+# closed before the next is built, must all match the oracle on a multi-position
+# prompt (one position would not notice: its attention weight is 1).
+BACK_TO_BACK = [dict(MINI, ffn_dim=2048), dict(MINI, embed_dim=1024, n_heads=16, n_kv_heads=4)]
+
+
+@pytest.mark.parametrize("cfg", BACK_TO_BACK, ids=["ffn2048", "dim1024"])
+def test_models_built_back_to_back_keep_their_weights(ggc, orc, ctx, cfg):
+    hp, ts = synth.make_model(cfg, seed=0)
+    prompt = np.random.default_rng(9).integers(0, hp["vocab_size"], size=6).astype(np.uint32)
+    pos = np.arange(6, dtype=np.int64)
+    want = orc.Model(hp, ts).forward(prompt, pos)
+    for rep in range(6):
+        m = ggc.LlamaModel(hp, ts, max_ctx=256, ctx=ctx)
+        got = m.forward(prompt, pos)
+        m.close()
+        assert rel_l2(got, want) <= REL_L2, (rep, rel_l2(got, want))
