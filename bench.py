@@ -522,7 +522,9 @@ def run_ours(args, rank, world, local_rank):
     W, K, C = args.warmup, args.steps, args.ctx
     P = C - W - K
     assert P >= 1, "context too small for warmup + steps"
-    model = ggc.LlamaModel(hp, ts, max_ctx=C, ctx=ctx)
+    t_load = time.perf_counter()
+    model = ggc.LlamaModel(hp, ts, max_ctx=C, ctx=ctx)   # raw rows uploaded, split into planes on the GPU
+    t_load = time.perf_counter() - t_load
     allreduce = model.allreduce if tp else "none"
     w_bytes = synth.weight_bytes_per_token(ts)
     # prefill: P seeded K/V rows planted in every layer (a decode step's cost does
@@ -622,6 +624,10 @@ def run_ours(args, rank, world, local_rank):
                                "bytes_per_step_per_gpu": gpu_bytes, "achieved_gbs_per_gpu": model_gbs,
                                "frac": model_gbs / peak_gbs, "bound_tokens_s": peak_gbs * 1e9 / gpu_bytes * streams},
             "tp_parity": parity,
+            "load": {"s": t_load, "weight_bytes": int(sum(int(t["raw"].nbytes) for t in ts if t is not None
+                                                           and t.get("raw") is not None)),
+                     "what": "ggc_model_create wall time (rank 0): raw weight rows to HBM, plane split by "
+                             "k_repack on the GPU, prefill raw copies, KV cache and RoPE table"},
             "matvec": rl,
             "matvec_frac_summary": sweep_fracs,
             "prefill": prefill,

@@ -389,9 +389,40 @@ __device__ __forceinline__ void span_item_store(const float (&v)[16], uint32_t i
     }
 }
 
+// The RMSNorm weight of the one-item-per-thread prologue (x of at most one column
+// tile), read into registers before griddepcontrol.wait: the norm weight is a
+// model constant, so its load latency (HBM: the weight stream evicts it from L2
+// every step) overlaps the wait for the predecessor instead of following it.
+struct NormW {
+    float v[16];
+    bool ok;
+};
+template <int NWARPS = GS_WARPS>
+__device__ __forceinline__ NormW span_norm_preload(const SpanX a, uint32_t nct) {
+    NormW w;
+    const int tid = threadIdx.x;
+    const uint32_t items = nct * SPAN_LANES * 8;
+    w.ok = a.pro == PRO_RMSNORM && items <= (uint32_t)NWARPS * 32;
+    const uint32_t e0 = (tid >> 3) * SPAN + 16 * (tid & 7);
+    if (w.ok && (uint32_t)tid < items && e0 + 16 <= a.xcols) {
+        const float4* w4 = reinterpret_cast<const float4*>(a.x2 + e0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 v = __ldg(w4 + q);
+            w.v[4 * q] = v.x; w.v[4 * q + 1] = v.y; w.v[4 * q + 2] = v.z; w.v[4 * q + 3] = v.w;
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) w.v[e] = w.ok && (uint32_t)tid < items && e0 + e < a.xcols ? __ldg(a.x2 + e0 + e) : 0.f;
+    }
+    return w;
+}
+
 // Returns (thread 0) whether the RMSNorm sum of squares is NaN; the caller reports it.
+// `pre`: the norm weight already in registers (span_norm_preload), or none.
 template <int DT, int NWARPS = GS_WARPS>
-__device__ bool span_x_prologue(const SpanX a, uint32_t nct, uint32_t* xl, float* xfs, double* red, float* s_scale) {
+__device__ bool span_x_prologue(const SpanX a, uint32_t nct, uint32_t* xl, float* xfs, double* red, float* s_scale,
+                                const NormW* pre = nullptr) {
     constexpr uint32_t CT = NWARPS * 32;
     auto cbar = [] { asm volatile("bar.sync 1, %0;" ::"r"(CT) : "memory"); };
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -406,17 +437,24 @@ __device__ bool span_x_prologue(const SpanX a, uint32_t nct, uint32_t* xl, float
             const float4* w4 = reinterpret_cast<const float4*>(a.x2 + e0);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                const float4 v = __ldcg(x4 + q), w = __ldg(w4 + q);
+                const float4 v = __ldcg(x4 + q);
                 xv[4 * q] = v.x; xv[4 * q + 1] = v.y; xv[4 * q + 2] = v.z; xv[4 * q + 3] = v.w;
-                wv[4 * q] = w.x; wv[4 * q + 1] = w.y; wv[4 * q + 2] = w.z; wv[4 * q + 3] = w.w;
+                if (!pre) {
+                    const float4 w = __ldg(w4 + q);
+                    wv[4 * q] = w.x; wv[4 * q + 1] = w.y; wv[4 * q + 2] = w.z; wv[4 * q + 3] = w.w;
+                }
             }
         } else {
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
                 const bool in = (uint32_t)tid < items && e0 + e < a.xcols;
                 xv[e] = in ? __ldcg(a.x + e0 + e) : 0.f;
-                wv[e] = in ? __ldg(a.x2 + e0 + e) : 0.f;
+                if (!pre) wv[e] = in ? __ldg(a.x2 + e0 + e) : 0.f;
             }
+        }
+        if (pre) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) wv[e] = pre->v[e];
         }
         double ss = 0.0;
 #pragma unroll
@@ -566,6 +604,7 @@ __global__ void __launch_bounds__(GS_THREADS, 1) k_gemv_span(const GemvArgs a, c
     }
 
     // ---------------- consumer warps ----------------
+    const NormW normw = span_norm_preload(span_x_of(a), nct);
     pdl_wait();
     // the skip flags' loads are issued here and used after the x prologue, so
     // their latency overlaps it (the prologue only reads x, and its NaN report
@@ -573,7 +612,7 @@ __global__ void __launch_bounds__(GS_THREADS, 1) k_gemv_span(const GemvArgs a, c
     const bool skipping = skip();
     constexpr uint32_t CT = GS_WARPS * 32;
     auto cbar = [] { asm volatile("bar.sync 1, %0;" ::"r"(CT) : "memory"); };
-    const bool x_nan = span_x_prologue<DT>(span_x_of(a), nct, xl, xfs, red, &s_scale);
+    const bool x_nan = span_x_prologue<DT>(span_x_of(a), nct, xl, xfs, red, &s_scale, normw.ok ? &normw : nullptr);
     if (skipping) {   // drain the copies issued before the flag was seen
         const uint32_t n = ntiles < cfg.stages ? ntiles : cfg.stages;
         for (uint32_t i = 0; i < n; ++i) mbar_wait(&full[i], 0, a.errf);

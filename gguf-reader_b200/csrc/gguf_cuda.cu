@@ -24,6 +24,7 @@
 #include "common.cuh"
 #include "dequant.cuh"
 #include "planes.cuh"
+#include "repack.cuh"
 #include "gemv.cuh"
 #include "gemv_span.cuh"
 #include "chain.cuh"
@@ -543,7 +544,30 @@ void free_mat(DevMat& m) {
 
 int chunk_elems(int dt) { return plane_spec(dt).chunk_elems; }
 
-// Splits raw rows into planes on the host and uploads them.
+// Raw rows (in output order, contiguous) into the zeroed planes: one thread per
+// (row, unit) of the layout, the same per-unit split the host repack runs
+// (repack.cuh), so the planes are the host's byte for byte.
+__global__ void __launch_bounds__(256) k_repack(int dt, const uint8_t* __restrict__ raw, uint64_t rows, uint64_t cols,
+                                                uint64_t row_bytes, TileLayout L, uint8_t* p0, uint8_t* p1, uint8_t* p2,
+                                                uint8_t* p3) {
+    pdl_wait();
+    uint8_t* const planes[4] = {p0, p1, p2, p3};
+    const uint64_t upr = rp::units_per_row(dt, L, cols), n = rows * upr;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t r = i / upr, u = i % upr;
+        rp::repack_unit(dt, raw + r * row_bytes, r, u, cols, L, planes);
+    }
+}
+
+bool host_repack() {
+    const char* e = getenv("GGC_REPACK");
+    return e && strcmp(e, "host") == 0;
+}
+
+// Splits raw rows into planes and uploads them.  Default: the raw rows go to the
+// GPU (gathered in output order on the host when row_src selects or reorders
+// them) and k_repack splits them there; GGC_REPACK=host splits them on host
+// threads and uploads the planes.  `raw` is host memory.
 int upload_mat(ggc_ctx* ctx, const void* raw, uint64_t raw_bytes, int dt, uint64_t rows, uint64_t cols,
                const uint32_t* row_src, DevMat& out) {
     const int bs = block_size_of(dt), bb = block_bytes_of(dt);
@@ -568,10 +592,6 @@ int upload_mat(ggc_ctx* ctx, const void* raw, uint64_t raw_bytes, int dt, uint64
         off[p] = total;
         total += ((uint64_t)L.nrb * L.rb_bytes[p] + 255) / 256 * 256;
     }
-    std::vector<uint8_t> host(total, 0);
-    uint8_t* planes[4] = {nullptr, nullptr, nullptr, nullptr};
-    for (int p = 0; p < ps.n; ++p) planes[p] = host.data() + off[p];
-    repack_rows_host(dt, (const uint8_t*)raw, rows, cols, row_src, L, planes, host_threads());
     DevMat m;
     m.dtype = dt;
     m.rows = (uint32_t)rows;
@@ -579,8 +599,41 @@ int upload_mat(ggc_ctx* ctx, const void* raw, uint64_t raw_bytes, int dt, uint64
     m.xcols = (uint32_t)cols;
     m.bytes = total;
     GGC_CUDA_TRY(cudaMalloc(&m.base, total));
-    cudaError_t e = cudaMemcpyAsync(m.base, host.data(), total, cudaMemcpyHostToDevice, ctx->stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    cudaError_t e = cudaSuccess;
+    if (host_repack()) {
+        std::vector<uint8_t> host(total, 0);
+        uint8_t* planes[4] = {nullptr, nullptr, nullptr, nullptr};
+        for (int p = 0; p < ps.n; ++p) planes[p] = host.data() + off[p];
+        repack_rows_host(dt, (const uint8_t*)raw, rows, cols, row_src, L, planes, host_threads());
+        e = cudaMemcpyAsync(m.base, host.data(), total, cudaMemcpyHostToDevice, ctx->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    } else {
+        const uint8_t* src = (const uint8_t*)raw;
+        std::vector<uint8_t> gathered;
+        if (row_src) {
+            gathered.resize(rows * row_bytes);
+            for (uint64_t r = 0; r < rows; ++r)
+                memcpy(gathered.data() + r * row_bytes, src + (uint64_t)row_src[r] * row_bytes, row_bytes);
+            src = gathered.data();
+        }
+        uint8_t* draw = nullptr;
+        e = cudaMalloc(&draw, rows * row_bytes);
+        if (e == cudaSuccess) e = cudaMemsetAsync(m.base, 0, total, ctx->stream);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(draw, src, rows * row_bytes, cudaMemcpyHostToDevice, ctx->stream);
+        if (e == cudaSuccess) {
+            const uint64_t n = rows * rp::units_per_row(dt, L, cols);
+            const uint64_t grid = std::min<uint64_t>((n + 255) / 256, 148ull * 16);
+            uint8_t* pp[4];
+            for (int p = 0; p < 4; ++p) pp[p] = p < ps.n ? m.base + off[p] : nullptr;
+            e = launch(ctx, k_repack, dim3((unsigned)grid), dim3(256), 0, dt, (const uint8_t*)draw, rows, cols, row_bytes,
+                       L, pp[0], pp[1], pp[2], pp[3]);
+        }
+        if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+        if (draw) {
+            const cudaError_t f = cudaFree(draw);
+            if (e == cudaSuccess) e = f;
+        }
+    }
     if (e != cudaSuccess) {
         cudaFree(m.base);
         return set_error(GGC_ERR_CUDA, "upload: %s", cudaGetErrorString(e));

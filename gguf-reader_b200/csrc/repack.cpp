@@ -1,229 +1,22 @@
 // repack.cpp -- host-side split of raw GGUF rows into the plane layout
-// (see planes.cuh).  Runs once per weight at model load.
-#include <algorithm>
-#include <cstring>
+// (planes.cuh), on host threads with the same per-unit functions the device
+// repack (k_repack) runs (repack.cuh).  Used when GGC_REPACK=host.
 #include <thread>
 #include <vector>
 
-#include "planes.cuh"
+#include "repack.cuh"
 
 namespace ggc {
-namespace {
-
-inline uint32_t rd32(const uint8_t* p) {
-    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
-}
-inline void wr32(uint8_t* p, uint32_t v) {
-    p[0] = (uint8_t)v; p[1] = (uint8_t)(v >> 8); p[2] = (uint8_t)(v >> 16); p[3] = (uint8_t)(v >> 24);
-}
-
-// Q5_0 / Q5_1 qh: element i (i<16) uses bit i, element 16+i uses bit 16+i.
-// Plane bit 8k+w   <- qh bit 4w+k      (low nibbles of chunk word w, byte k)
-// Plane bit 8k+4+w <- qh bit 16+4w+k   (high nibbles of chunk word w, byte k)
-uint32_t permute_q5_qh(uint32_t qh) {
-    uint32_t o = 0;
-    for (int w = 0; w < 4; ++w)
-        for (int k = 0; k < 4; ++k) {
-            o |= ((qh >> (4 * w + k)) & 1u) << (8 * k + w);
-            o |= ((qh >> (16 + 4 * w + k)) & 1u) << (8 * k + 4 + w);
-        }
-    return o;
-}
-
-// quant.rs:116-124 k_scale_min_6bit for j = 0..7 -> sc[j] at out[j], mn[j] at out[8 + j]
-void unpack_scale_min(const uint8_t* q, uint8_t* out) {
-    for (int j = 0; j < 8; ++j) {
-        uint8_t sc, mn;
-        if (j < 4) {
-            sc = q[j] & 0x3F;
-            mn = q[j + 4] & 0x3F;
-        } else {
-            sc = (uint8_t)((q[j + 4] & 0x0F) | ((q[j - 4] >> 6) << 4));
-            mn = (uint8_t)((q[j + 4] >> 4) | ((q[j] >> 6) << 4));
-        }
-        out[j] = sc;
-        out[8 + j] = mn;
-    }
-}
-
-void repack_block(int dt, const uint8_t* b, uint64_t blk, uint8_t* const pl[4]) {
-    switch (dt) {
-        case GGC_Q4_0:
-            std::memcpy(pl[0] + blk * 16, b + 2, 16);
-            std::memcpy(pl[1] + blk * 2, b, 2);
-            break;
-        case GGC_Q4_1:
-            std::memcpy(pl[0] + blk * 16, b + 4, 16);
-            std::memcpy(pl[1] + blk * 4, b, 4);
-            break;
-        case GGC_Q5_0:
-            std::memcpy(pl[0] + blk * 16, b + 6, 16);
-            wr32(pl[1] + blk * 4, permute_q5_qh(rd32(b + 2)));
-            std::memcpy(pl[2] + blk * 2, b, 2);
-            break;
-        case GGC_Q5_1:
-            std::memcpy(pl[0] + blk * 16, b + 8, 16);
-            wr32(pl[1] + blk * 4, permute_q5_qh(rd32(b + 4)));
-            std::memcpy(pl[2] + blk * 4, b, 4);
-            break;
-        case GGC_Q8_0:
-            std::memcpy(pl[0] + blk * 32, b + 2, 32);
-            std::memcpy(pl[1] + blk * 2, b, 2);
-            break;
-        case GGC_Q2_K:
-            std::memcpy(pl[0] + blk * 64, b + 16, 64);
-            std::memcpy(pl[1] + blk * 16, b, 16);
-            std::memcpy(pl[2] + blk * 4, b + 80, 4);
-            break;
-        case GGC_Q3_K_S: case GGC_Q3_K_L: case GGC_Q3_K_M: {
-            std::memcpy(pl[0] + blk * 64, b + 32, 64);
-            // hmask: element e uses bit e%8 of byte e/8.  Chunk p covers elements
-            // 64p + 16w + 4k + s; plane word (2p + w/2), bit 8k + s + 4(w%2).
-            uint32_t words[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            for (int e = 0; e < 256; ++e) {
-                uint32_t bit = (b[e / 8] >> (e % 8)) & 1u;
-                int p = e / 64, r = e % 64, w = r / 16, k = (r % 16) / 4, s = r % 4;
-                words[2 * p + w / 2] |= bit << (8 * k + s + 4 * (w % 2));
-            }
-            for (int i = 0; i < 8; ++i) wr32(pl[1] + blk * 32 + 4 * i, words[i]);
-            std::memcpy(pl[2] + blk * 12, b + 96, 12);
-            std::memcpy(pl[3] + blk * 2, b + (dt == GGC_Q3_K_M ? 112 : 108), 2);
-            break;
-        }
-        case GGC_Q4_K:
-            std::memcpy(pl[0] + blk * 128, b + 16, 128);
-            std::memcpy(pl[1] + blk * 4, b, 4);
-            unpack_scale_min(b + 4, pl[2] + blk * 16);
-            break;
-        case GGC_Q5_K: {
-            std::memcpy(pl[0] + blk * 128, b + 48, 128);
-            // qs byte B (0..127) takes its 5th bit from bit B%8 of qh[B/8] (only
-            // qh[0..16) is read).  Chunk p = bytes 16p + 4w + k -> plane word p/2,
-            // bit 8k + w + 4(p%2).
-            uint32_t words[4] = {0, 0, 0, 0};
-            for (int B = 0; B < 128; ++B) {
-                uint32_t bit = (b[16 + B / 8] >> (B % 8)) & 1u;
-                int p = B / 16, i = B % 16, w = i / 4, k = i % 4;
-                words[p / 2] |= bit << (8 * k + w + 4 * (p % 2));
-            }
-            for (int i = 0; i < 4; ++i) wr32(pl[1] + blk * 16 + 4 * i, words[i]);
-            std::memcpy(pl[2] + blk * 4, b, 4);
-            unpack_scale_min(b + 4, pl[3] + blk * 16);
-            break;
-        }
-        case GGC_Q6_K:
-            std::memcpy(pl[0] + blk * 128, b, 128);
-            std::memcpy(pl[1] + blk * 64, b + 128, 64);
-            std::memcpy(pl[2] + blk * 16, b + 192, 16);
-            std::memcpy(pl[3] + blk * 2, b + 208, 2);
-            break;
-        case GGC_Q8_K:
-            std::memcpy(pl[0] + blk * 256, b + 4, 256);
-            std::memcpy(pl[1] + blk * 4, b, 4);
-            break;
-        case GGC_F16: case GGC_BF16:
-            std::memcpy(pl[0] + blk * 2, b, 2);
-            break;
-        case GGC_F32:
-            std::memcpy(pl[0] + blk * 4, b, 4);
-            break;
-        default:
-            break;
-    }
-}
-
-// One 128-element span (lane l of a column tile with nl lanes) of one row into
-// the span layout; row[p] is the plane's row base in the tile.  Blocks past the
-// row's end stay zero.
-void repack_span(int dt, const uint8_t* src, uint64_t nb, uint64_t sp, uint32_t l, uint32_t nl, uint8_t* const row[4]) {
-    auto unit = [&](int p, int k) { return row[p] + ((uint64_t)k * nl + l) * 16; };
-    switch (dt) {
-        case GGC_Q4_K: {   // span = half n of block sp / 2
-            const uint64_t b = sp / 2;
-            const int n = (int)(sp % 2);
-            if (b >= nb) return;
-            const uint8_t* blk = src + b * 144;
-            for (int k = 0; k < 4; ++k) std::memcpy(unit(0, k), blk + 16 + 64 * n + 16 * k, 16);
-            if (n == 0) std::memcpy(row[1] + (l / 2) * 4, blk, 4);
-            uint8_t scm[16];
-            unpack_scale_min(blk + 4, scm);
-            std::memcpy(row[2] + l * 8, scm + 4 * n, 4);
-            std::memcpy(row[2] + l * 8 + 4, scm + 8 + 4 * n, 4);
-            break;
-        }
-        case GGC_Q6_K: {
-            const uint64_t b = sp / 2;
-            const int n = (int)(sp % 2);
-            if (b >= nb) return;
-            const uint8_t* blk = src + b * 210;
-            for (int k = 0; k < 4; ++k) std::memcpy(unit(0, k), blk + 64 * n + 16 * k, 16);
-            for (int k = 0; k < 2; ++k) std::memcpy(unit(1, k), blk + 128 + 32 * n + 16 * k, 16);
-            std::memcpy(row[2] + l * 8, blk + 192 + 8 * n, 8);
-            if (n == 0) std::memcpy(row[3] + (l / 2) * 2, blk + 208, 2);
-            break;
-        }
-        case GGC_Q4_0:
-            for (int k = 0; k < 4; ++k) {
-                const uint64_t b = sp * 4 + k;
-                if (b >= nb) break;
-                std::memcpy(unit(0, k), src + b * 18 + 2, 16);
-                std::memcpy(row[1] + l * 8 + 2 * k, src + b * 18, 2);
-            }
-            break;
-        case GGC_Q8_0:
-            for (int k = 0; k < 4; ++k) {
-                const uint64_t b = sp * 4 + k;
-                if (b >= nb) break;
-                std::memcpy(unit(0, 2 * k), src + b * 34 + 2, 16);
-                std::memcpy(unit(0, 2 * k + 1), src + b * 34 + 18, 16);
-                std::memcpy(row[1] + l * 8 + 2 * k, src + b * 34, 2);
-            }
-            break;
-        default:
-            break;
-    }
-}
-
-}  // namespace
 
 void repack_rows_host(int dt, const uint8_t* raw, uint64_t rows, uint64_t cols, const uint32_t* row_src,
                       const TileLayout& L, uint8_t* const planes[4], int nthreads) {
-    const PlaneSpec s = plane_spec(dt);
     const uint64_t bs = (uint64_t)block_size_of(dt), bb = (uint64_t)block_bytes_of(dt);
-    const uint64_t nb = cols / bs, row_bytes = nb * bb;
-    const uint64_t blocks_per_tile = L.kc / bs;
+    const uint64_t row_bytes = cols / bs * bb;
+    const uint64_t upr = rp::units_per_row(dt, L, cols);
     auto work = [&](uint64_t r0, uint64_t r1) {
-        if (is_span_dt(dt)) {
-            const SpanSpec sp = span_spec(dt);
-            const uint64_t nsp = L.pcols / SPAN;
-            for (uint64_t r = r0; r < r1; ++r) {
-                const uint8_t* src = raw + (uint64_t)(row_src ? row_src[r] : r) * row_bytes;
-                const uint32_t rb = (uint32_t)(r / TILE_ROWS), rl = (uint32_t)(r % TILE_ROWS);
-                for (uint64_t q = 0; q < nsp; ++q) {
-                    const uint32_t ct = (uint32_t)(q / SPAN_LANES), l = (uint32_t)(q % SPAN_LANES);
-                    const uint32_t nl = ct + 1 == L.nct ? (uint32_t)(nsp - (uint64_t)ct * SPAN_LANES) : SPAN_LANES;
-                    uint8_t* row[4] = {nullptr, nullptr, nullptr, nullptr};
-                    for (int p = 0; p < sp.n; ++p)
-                        row[p] = planes[p] + tile_offset(L, p, rb, ct) + (uint64_t)rl * tile_pitch(L, p, ct);
-                    repack_span(dt, src, nb, q, l, nl, row);
-                }
-            }
-            return;
-        }
         for (uint64_t r = r0; r < r1; ++r) {
             const uint8_t* src = raw + (uint64_t)(row_src ? row_src[r] : r) * row_bytes;
-            const uint32_t rb = (uint32_t)(r / TILE_ROWS), rl = (uint32_t)(r % TILE_ROWS);
-            for (uint32_t ct = 0; ct < L.nct; ++ct) {
-                uint8_t* pl[4] = {nullptr, nullptr, nullptr, nullptr};
-                for (int p = 0; p < s.n; ++p)
-                    pl[p] = planes[p] + tile_offset(L, p, rb, ct) + (uint64_t)rl * tile_pitch(L, p, ct);
-                const uint64_t k0 = ct * blocks_per_tile, k1 = std::min<uint64_t>(nb, k0 + blocks_per_tile);
-                if (bs == 1) {   // float formats: one contiguous run per tile row
-                    if (k1 > k0) std::memcpy(pl[0], src + k0 * bb, (k1 - k0) * bb);
-                } else {
-                    for (uint64_t k = k0; k < k1; ++k) repack_block(dt, src + k * bb, k - k0, pl);
-                }
-            }
+            for (uint64_t u = 0; u < upr; ++u) rp::repack_unit(dt, src, r, u, cols, L, planes);
         }
     };
     if (nthreads <= 1 || rows < 64) {

@@ -307,3 +307,16 @@ def test_models_built_back_to_back_keep_their_weights(ggc, orc, ctx, cfg):
         got = m.forward(prompt, pos)
         m.close()
         assert rel_l2(got, want) <= REL_L2, (rep, rel_l2(got, want))
+
+
+def test_device_repack_model_matches_host_repack(ggc, ctx, monkeypatch):
+    """A model whose weights were split on the GPU at load (the default) and one split
+    on the host (GGC_REPACK=host) give bit-identical logits: the q/k RoPE row order and
+    the fused up/gate rows go through the device repack too."""
+    hp, ts = synth.make_model(MINI, seed=5)
+    toks, pos = [3, 17, 250, 9, 41], [0, 1, 2, 3, 4]
+    monkeypatch.delenv("GGC_REPACK", raising=False)
+    dev = ggc.LlamaModel(hp, ts, max_ctx=64, ctx=ctx).forward(toks, pos)
+    monkeypatch.setenv("GGC_REPACK", "host")
+    host = ggc.LlamaModel(hp, ts, max_ctx=64, ctx=ctx).forward(toks, pos)
+    assert np.array_equal(np.asarray(dev).view(np.uint32), np.asarray(host).view(np.uint32))
