@@ -1,5 +1,6 @@
-// gemv_span.cuh -- decode GEMV y = W x for the integer formats (Q4_K, Q6_K,
-// Q4_0, Q8_0) over the span layout (planes.cuh).
+// gemv_span.cuh -- decode GEMV y = W x for the block formats (Q4_0, Q4_1, Q5_0,
+// Q5_1, Q8_0, Q2_K, Q3_K_*, Q4_K, Q5_K, Q6_K, Q8_K) over the span layout
+// (planes.cuh).
 //
 // Work split.  One CTA per SM over a contiguous range of 16-row blocks; a
 // producer warp streams tiles (16 rows x 4096 columns, every plane: one bulk copy
@@ -245,6 +246,230 @@ template <> struct SpanFmt<GGC_Q8_0> {
             r = fmaf(d, comb(A), r);   // value = d q  (quant.rs:173-180)
         }
         return r * gs;
+    }
+};
+
+// Q4_1 (interleaved nibbles as Q4_0, value = d q + m, quant.rs:137-145): span = 4 blocks.
+template <> struct SpanFmt<GGC_Q4_1> {
+    __device__ static constexpr int elem(int s, int j) { return SpanFmt<GGC_Q4_0>::elem(s, j); }
+    __device__ static constexpr int step_of(int q, int t) { return SpanFmt<GGC_Q4_0>::step_of(q, t); }
+    __device__ static constexpr int qoff(int t, int j) { return SpanFmt<GGC_Q4_0>::qoff(t, j); }
+    __device__ static float dot(const SpanRow& R, int lane, const uint32_t* L, float gs, const float* xq) {
+        uint4 u[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) u[k] = lds128(R.p[0] + (k * R.nl + lane) * 16);
+        const uint4 dm = lds128(R.p[1] + lane * 16);   // d[4], m[4]
+        const float4 xs = xq_load(xq, 2);
+        float r = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            Acc3 lo, hi;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t q = wsel(u[k], i);
+                dp3u(q & 0x0F0F0F0Fu, L + 3 * (8 * k + 2 * i), lo);
+                dp3u(q & 0xF0F0F0F0u, L + 3 * (8 * k + 2 * i + 1), hi);   // 16 q
+            }
+            const float s16 = comb3(16 * lo.a0 + hi.a0, 16 * lo.a1 + hi.a1, 16 * lo.a2 + hi.a2);
+            const float d = h2f(((k < 2 ? dm.x : dm.y) >> (16 * (k & 1))) & 0xFFFFu);
+            const float m = h2f(((k < 2 ? dm.z : dm.w) >> (16 * (k & 1))) & 0xFFFFu);
+            r = fmaf(d, (gs * 0.0625f) * s16, fmaf(m, f4sel(xs, k), r));
+        }
+        return r;
+    }
+};
+
+// Q5_0 / Q5_1 (quant.rs:147-186: qs[i] low nibble = element i, high = element 16 + i,
+// the 5th bits from qh bits i and 16 + i): span = 4 blocks; block k's qh word is
+// permuted so bit 8 j + i / 8 j + 4 + i is the 5th bit of byte j's low / high
+// nibble in qs word i.  Value d (q - 16) (Q5_0) or d q + m (Q5_1).
+template <int DT> struct SpanQ5 {
+    __device__ static constexpr int elem(int s, int j) { return 32 * (s >> 3) + 16 * (s & 1) + 4 * ((s >> 1) & 3) + j; }
+    __device__ static constexpr int step_of(int q, int t) { return 8 * (q >> 1) + 2 * t + (q & 1); }
+    __device__ static constexpr int qoff(int t, int j) { return 4 * t + j; }
+    __device__ static float dot(const SpanRow& R, int lane, const uint32_t* L, float gs, const float* xq) {
+        uint4 u[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) u[k] = lds128(R.p[0] + (k * R.nl + lane) * 16);
+        const uint4 hq = lds128(R.p[1] + lane * 16);
+        uint4 dm;
+        if (DT == GGC_Q5_1) {
+            dm = lds128(R.p[2] + lane * 16);   // d[4], m[4]
+        } else {
+            const uint2 d2 = lds64(R.p[2] + lane * 8);
+            dm = make_uint4(d2.x, d2.y, 0u, 0u);
+        }
+        const float4 xs = xq_load(xq, 2);
+        float r = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t H = wsel(hq, k);
+            Acc3 A;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t q = wsel(u[k], i);
+                const uint32_t lo = (q & 0x0F0F0F0Fu) | (((H >> i) << 4) & 0x10101010u);
+                const uint32_t hi = ((q >> 4) & 0x0F0F0F0Fu) | ((H >> i) & 0x10101010u);
+                dp3u(lo, L + 3 * (8 * k + 2 * i), A);
+                dp3u(hi, L + 3 * (8 * k + 2 * i + 1), A);
+            }
+            const float d = h2f(((k < 2 ? dm.x : dm.y) >> (16 * (k & 1))) & 0xFFFFu);
+            if (DT == GGC_Q5_1) {
+                const float m = h2f(((k < 2 ? dm.z : dm.w) >> (16 * (k & 1))) & 0xFFFFu);
+                r = fmaf(d, gs * comb(A), fmaf(m, f4sel(xs, k), r));
+            } else {
+                r = fmaf(d, fmaf(gs, comb(A), -16.f * f4sel(xs, k)), r);
+            }
+        }
+        return r;
+    }
+};
+template <> struct SpanFmt<GGC_Q5_0> : SpanQ5<GGC_Q5_0> {};
+template <> struct SpanFmt<GGC_Q5_1> : SpanQ5<GGC_Q5_1> {};
+
+// Q2_K (quant.rs:190-205): span = half n of a block; qs byte m of the span holds
+// elements 4 m + t at bits 2 t, so qs word w gives, per shift t, the four elements
+// 16 w + 4 j + t of local sub-block w (16 elements, scale k_scale4(8 n + w)).
+// s < 8: value = d s q; else value = dmin ((2 s - 8) q + (s - 8)).
+template <> struct SpanFmt<GGC_Q2_K> {
+    __device__ static constexpr int elem(int s, int j) { return 16 * (s >> 2) + 4 * j + (s & 3); }
+    __device__ static constexpr int step_of(int q, int t) { return 4 * q + t; }
+    __device__ static constexpr int qoff(int t, int j) { return 4 * j + t; }
+    __device__ static float dot(const SpanRow& R, int lane, const uint32_t* L, float gs, const float* xq) {
+        uint4 u[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) u[k] = lds128(R.p[0] + (k * R.nl + lane) * 16);
+        const uint32_t sc4 = lds32(R.p[1] + lane * 4);
+        const uint32_t dd = lds32(R.p[2] + (lane >> 1) * 4);
+        int D0 = 0, D1 = 0, D2 = 0, M0 = 0, M1 = 0, M2 = 0;
+        float offm = 0.f;
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+            const float4 xs = xq_load(xq, p);   // sums of sub-blocks 4p .. 4p + 3
+            Acc3 A[4];
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+                const int w = 4 * p + v;
+                const uint32_t W = wsel(u[p], v);
+#pragma unroll
+                for (int t = 0; t < 4; ++t) dp3u((W >> (2 * t)) & 0x03030303u, L + 3 * (4 * w + t), A[v]);
+            }
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+                const int sv = (int)((sc4 >> (4 * (4 * p + v))) & 0xFu);
+                const int cd = sv < 8 ? sv : 0, cm = sv < 8 ? 0 : 2 * sv - 8;
+                D0 += cd * A[v].a0; D1 += cd * A[v].a1; D2 += cd * A[v].a2;
+                M0 += cm * A[v].a0; M1 += cm * A[v].a1; M2 += cm * A[v].a2;
+                offm = fmaf((float)(sv < 8 ? 0 : sv - 8), f4sel(xs, v), offm);
+            }
+        }
+        const float2 dm = h2f2(dd);
+        return fmaf(dm.x * gs, comb3(D0, D1, D2), dm.y * fmaf(gs, comb3(M0, M1, M2), offm));
+    }
+};
+
+// Q3_K (quant.rs:209-245): element layout as Q2_K; the span's qs and hmask are
+// stored inverted, so u = q + 3 = (ql ^ 3) | (h ^ 1) << 2 takes a shift and a mask
+// (the h bits of qs word w, shift t at bit t + 4 (w % 2) of hmask word w / 2);
+// value = d sc q with the int8 scale of local sub-block w.
+template <int DT> struct SpanQ3K {
+    __device__ static constexpr int elem(int s, int j) { return 16 * (s >> 2) + 4 * j + (s & 3); }
+    __device__ static constexpr int step_of(int q, int t) { return 4 * q + t; }
+    __device__ static constexpr int qoff(int t, int j) { return 4 * j + t; }
+    __device__ static float dot(const SpanRow& R, int lane, const uint32_t* L, float gs, const float* xq) {
+        uint4 u[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) u[k] = lds128(R.p[0] + (k * R.nl + lane) * 16);
+        const uint4 hm = lds128(R.p[1] + lane * 16);
+        const uint2 sc = lds64(R.p[2] + lane * 8);
+        const uint32_t d16 = lds16(R.p[3] + (lane >> 1) * 2);
+        int T0 = 0, T1 = 0, T2 = 0;
+        float off = 0.f;
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+            const float4 xs = xq_load(xq, p);
+            Acc3 A[4];
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+                const int w = 4 * p + v;
+                const uint32_t W = wsel(u[p], v), H = wsel(hm, w >> 1);
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const int sh = t + 4 * (w & 1);
+                    const uint32_t h4 = (sh >= 2 ? (H >> (sh - 2)) : (H << (2 - sh))) & 0x04040404u;
+                    dp3u(((W >> (2 * t)) & 0x03030303u) | h4, L + 3 * (4 * w + t), A[v]);
+                }
+            }
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+                const int c = (int)(int8_t)(((p == 0 ? sc.x : sc.y) >> (8 * v)) & 0xFFu);
+                T0 += c * A[v].a0; T1 += c * A[v].a1; T2 += c * A[v].a2;
+                off = fmaf((float)c, f4sel(xs, v), off);
+            }
+        }
+        return h2f(d16) * fmaf(gs, comb3(T0, T1, T2), -3.f * off);
+    }
+};
+template <> struct SpanFmt<GGC_Q3_K_S> : SpanQ3K<GGC_Q3_K_S> {};
+template <> struct SpanFmt<GGC_Q3_K_M> : SpanQ3K<GGC_Q3_K_M> {};
+template <> struct SpanFmt<GGC_Q3_K_L> : SpanQ3K<GGC_Q3_K_L> {};
+
+// Q5_K as the reference reads it (quant.rs:287-307): element k = nibble k % 2 of
+// qs[k / 2] with the 5th bit from qh bit k / 2 (both nibbles of a byte share it),
+// sub-blocks of 32 with the 6-bit (scale, min) pairs: span = half n of a block,
+// qs unit k = local sub-block k, element layout as Q4_0; the 5th bits of qs word w
+// at bit 8 j + w % 8 of qh word w / 8.  Value d sc q - dmin mn.
+template <> struct SpanFmt<GGC_Q5_K> {
+    __device__ static constexpr int elem(int s, int j) { return SpanFmt<GGC_Q4_0>::elem(s, j); }
+    __device__ static constexpr int step_of(int q, int t) { return SpanFmt<GGC_Q4_0>::step_of(q, t); }
+    __device__ static constexpr int qoff(int t, int j) { return SpanFmt<GGC_Q4_0>::qoff(t, j); }
+    __device__ static float dot(const SpanRow& R, int lane, const uint32_t* L, float gs, const float* xq) {
+        uint4 u[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) u[k] = lds128(R.p[0] + (k * R.nl + lane) * 16);
+        const uint32_t dd = lds32(R.p[1] + (lane >> 1) * 4);
+        const uint2 scm = lds64(R.p[2] + lane * 8);
+        const uint2 hw = lds64(R.p[3] + lane * 8);
+        int T0 = 0, T1 = 0, T2 = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            Acc3 A;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int w = 4 * k + i, b = w & 7;
+                const uint32_t q = wsel(u[k], i), H = w < 8 ? hw.x : hw.y;
+                const uint32_t h5 = (b <= 4 ? (H << (4 - b)) : (H >> (b - 4))) & 0x10101010u;
+                dp3u((q & 0x0F0F0F0Fu) | h5, L + 3 * (8 * k + 2 * i), A);
+                dp3u(((q >> 4) & 0x0F0F0F0Fu) | h5, L + 3 * (8 * k + 2 * i + 1), A);
+            }
+            const int c = (int)((scm.x >> (8 * k)) & 0xFFu);
+            T0 += c * A.a0; T1 += c * A.a1; T2 += c * A.a2;
+        }
+        const float4 xs = xq_load(xq, 2);
+        float mn = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) mn = fmaf((float)((scm.y >> (8 * k)) & 0xFFu), f4sel(xs, k), mn);
+        const float2 dm = h2f2(dd);
+        return fmaf(dm.x * gs, comb3(T0, T1, T2), -dm.y * mn);
+    }
+};
+
+// Q8_K (quant.rs:338-344): span = half a block of int8, one f32 d; element layout as Q8_0.
+template <> struct SpanFmt<GGC_Q8_K> {
+    __device__ static constexpr int elem(int s, int j) { return 4 * s + j; }
+    __device__ static constexpr int step_of(int q, int t) { return 4 * q + t; }
+    __device__ static constexpr int qoff(int t, int j) { return 4 * t + j; }
+    __device__ static float dot(const SpanRow& R, int lane, const uint32_t* L, float gs, const float* xq) {
+        uint4 u[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) u[k] = lds128(R.p[0] + (k * R.nl + lane) * 16);
+        const uint32_t dd = lds32(R.p[1] + (lane >> 1) * 4);
+        Acc3 A;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dp3s(wsel(u[k], i), L + 3 * (4 * k + i), A);
+        return __uint_as_float(dd) * (comb(A) * gs);
     }
 };
 

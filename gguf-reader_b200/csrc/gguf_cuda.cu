@@ -1600,7 +1600,7 @@ struct ChainBuilder {
         uint32_t xl = 0, part = 0, slot = 0;
         const uint32_t sms = (uint32_t)m->ctx->num_sms;
         for (auto& op : ops) {
-            if (!is_span_dt(op.first) || op.second.cols % SPAN) return false;
+            if (!chain_bit(op.first) || op.second.cols % SPAN) return false;   // Q4_K, Q6_K, Q4_0, Q8_0
             const TileLayout L = make_layout(op.first, TILE_ROWS, op.second.cols);
             const SpanSpec sp = span_spec(op.first);
             uint32_t sb = 0;

@@ -54,19 +54,21 @@ __host__ __device__ constexpr PlaneSpec plane_spec(int dt) {
          : PlaneSpec{0, {0, 0, 0, 0}, 0};
 }
 
-// Span layout (Q4_K, Q6_K, Q4_0, Q8_0: the formats of the integer GEMV).  A
-// column tile is 4096 columns = 32 lanes x one 128-element "span" per lane; the
-// bytes a lane reads for its span of a row are, per plane, either 16-byte units
-// interleaved by lane (unit k of lane l at (k * nl + l) * 16, nl = lanes of the
-// column tile) or a small per-lane record (at l * bps), or a per-block record
-// shared by a lane pair (Q4_K d|dmin, Q6_K d).  Rows are padded with zero bytes
-// to a multiple of 128 columns.
+// Span layout (every block format: the integer GEMV).  A column tile is 4096
+// columns = 32 lanes x one 128-element "span" per lane; the bytes a lane reads for
+// its span of a row are, per plane, either 16-byte units interleaved by lane
+// (unit k of lane l at (k * nl + l) * 16, nl = lanes of the column tile) or a
+// small per-lane record (at l * bps), or a per-block record shared by a lane pair
+// (256-element blocks: d|dmin, d).  Rows are padded with zero bytes to a multiple
+// of 128 columns.
 constexpr int SPAN = 128;
 constexpr int SPAN_LANES = 32;
 constexpr uint32_t SPAN_KC = SPAN * SPAN_LANES;
 
 __host__ __device__ constexpr bool is_span_dt(int dt) {
-    return dt == GGC_Q4_K || dt == GGC_Q6_K || dt == GGC_Q4_0 || dt == GGC_Q8_0;
+    return dt == GGC_Q4_0 || dt == GGC_Q4_1 || dt == GGC_Q5_0 || dt == GGC_Q5_1 || dt == GGC_Q8_0 || dt == GGC_Q2_K ||
+           dt == GGC_Q3_K_S || dt == GGC_Q3_K_M || dt == GGC_Q3_K_L || dt == GGC_Q4_K || dt == GGC_Q5_K ||
+           dt == GGC_Q6_K || dt == GGC_Q8_K;
 }
 struct SpanSpec {
     int n;          // planes
@@ -77,6 +79,14 @@ __host__ __device__ constexpr SpanSpec span_spec(int dt) {
          : dt == GGC_Q6_K ? SpanSpec{4, {64, 32, 8, 1}}    // ql units | qh units | sc[8] | d per block
          : dt == GGC_Q4_0 ? SpanSpec{2, {64, 8, 0, 0}}     // qs units (4 blocks) | d[4]
          : dt == GGC_Q8_0 ? SpanSpec{2, {128, 8, 0, 0}}    // qs units (4 blocks) | d[4]
+         : dt == GGC_Q4_1 ? SpanSpec{2, {64, 16, 0, 0}}    // qs units (4 blocks) | d[4] m[4]
+         : dt == GGC_Q5_0 ? SpanSpec{3, {64, 16, 8, 0}}    // qs units | permuted qh word per block | d[4]
+         : dt == GGC_Q5_1 ? SpanSpec{3, {64, 16, 16, 0}}   // qs units | permuted qh word per block | d[4] m[4]
+         : dt == GGC_Q2_K ? SpanSpec{3, {32, 4, 2, 0}}     // qs units | scale nibbles[8] | d,dmin per block
+         : (dt == GGC_Q3_K_S || dt == GGC_Q3_K_M || dt == GGC_Q3_K_L)
+             ? SpanSpec{4, {32, 16, 8, 1}}                 // inverted qs units | inverted hmask words[4] | sc[8] | d per block
+         : dt == GGC_Q5_K ? SpanSpec{4, {64, 2, 8, 8}}     // qs units | d,dmin per block | sc[4] mn[4] | qh words[2]
+         : dt == GGC_Q8_K ? SpanSpec{2, {128, 2, 0, 0}}    // qs units | f32 d per block
          : SpanSpec{0, {0, 0, 0, 0}};
 }
 

@@ -189,6 +189,112 @@ __host__ __device__ inline void repack_span(int dt, const uint8_t* src, uint64_t
                 cpy(row[1] + l * 8 + 2 * k, src + b * 34, 2);
             }
             break;
+        case GGC_Q4_1:   // d, m, qs[16] (quant.rs:137-145): qs unit per block, d[4] then m[4]
+            for (int k = 0; k < 4; ++k) {
+                const uint64_t b = sp * 4 + k;
+                if (b >= nb) break;
+                cpy(unit(0, k), src + b * 20 + 4, 16);
+                cpy(row[1] + l * 16 + 2 * k, src + b * 20, 2);
+                cpy(row[1] + l * 16 + 8 + 2 * k, src + b * 20 + 2, 2);
+            }
+            break;
+        case GGC_Q5_0: case GGC_Q5_1: {   // [d, (m,)] qh, qs[16] (quant.rs:147-186)
+            const int bb = dt == GGC_Q5_0 ? 22 : 24, qh = dt == GGC_Q5_0 ? 2 : 4;
+            for (int k = 0; k < 4; ++k) {
+                const uint64_t b = sp * 4 + k;
+                if (b >= nb) break;
+                const uint8_t* blk = src + b * bb;
+                cpy(unit(0, k), blk + qh + 4, 16);
+                wr32(row[1] + l * 16 + 4 * k, permute_q5_qh(rd32(blk + qh)));
+                if (dt == GGC_Q5_0) {
+                    cpy(row[2] + l * 8 + 2 * k, blk, 2);
+                } else {
+                    cpy(row[2] + l * 16 + 2 * k, blk, 2);
+                    cpy(row[2] + l * 16 + 8 + 2 * k, blk + 2, 2);
+                }
+            }
+            break;
+        }
+        case GGC_Q2_K: {   // scales[16], qs[64], d, dmin (quant.rs:190-205); span = half n of block sp / 2
+            const uint64_t b = sp / 2;
+            const int n = (int)(sp % 2);
+            if (b >= nb) return;
+            const uint8_t* blk = src + b * 84;
+            for (int k = 0; k < 2; ++k) cpy(unit(0, k), blk + 16 + 32 * n + 16 * k, 16);
+            // local sub-block w = sub-block j = 8n + w: k_scale4 (quant.rs:100-108), nibble w of the record
+            uint32_t sc = 0;
+            for (int w = 0; w < 8; ++w) {
+                const int j = 8 * n + w, byte = 15 - j / 2;
+                sc |= (uint32_t)((j % 2 == 0) ? (blk[byte] & 0xF) : ((blk[byte] >> 4) & 0xF)) << (4 * w);
+            }
+            wr32(row[1] + l * 4, sc);
+            if (n == 0) cpy(row[2] + (l / 2) * 4, blk + 80, 4);
+            break;
+        }
+        case GGC_Q3_K_S: case GGC_Q3_K_M: case GGC_Q3_K_L: {   // quant.rs:209-245
+            const uint64_t b = sp / 2;
+            const int n = (int)(sp % 2);
+            if (b >= nb) return;
+            const int bb = dt == GGC_Q3_K_M ? 114 : 110, doff = dt == GGC_Q3_K_M ? 112 : 108;
+            const uint8_t* blk = src + b * bb;
+            // qs stored inverted (2-bit code ql -> ql ^ 3), hmask inverted (h -> h ^ 1): the
+            // GEMV then reads u = q + 3 = (ql ^ 3) | (h ^ 1) << 2 with a shift and a mask
+            for (int k = 0; k < 2; ++k) {
+                uint8_t* d = unit(0, k);
+                const uint8_t* q = blk + 32 + 32 * n + 16 * k;
+                for (int i = 0; i < 16; ++i) d[i] = (uint8_t)~q[i];
+            }
+            // element e = 128 n + 16 w + 4 j + s (word w / 4 of unit w / 4, byte j, shift 2 s):
+            // inverted h at bit 8 j + s + 4 (w % 2) of hmask word w / 2
+            uint32_t hw[4] = {0, 0, 0, 0};
+            for (int w = 0; w < 8; ++w)
+                for (int j = 0; j < 4; ++j)
+                    for (int t = 0; t < 4; ++t) {
+                        const int e = 128 * n + 16 * w + 4 * j + t;
+                        const uint32_t h = ((blk[e / 8] >> (e % 8)) & 1u) ^ 1u;
+                        hw[w / 2] |= h << (8 * j + t + 4 * (w % 2));
+                    }
+            for (int i = 0; i < 4; ++i) wr32(row[1] + l * 16 + 4 * i, hw[i]);
+            for (int w = 0; w < 8; ++w) {   // scale of sub-block g = 8n + w, as int8 (lo | hi << 4) - 32
+                const int g = 8 * n + w;
+                const int lo = (blk[96 + g / 2] >> ((g % 2) * 4)) & 0xF, hi = (blk[104 + g / 4] >> ((g % 4) * 2)) & 3;
+                row[2][l * 8 + w] = (uint8_t)(int8_t)((lo | (hi << 4)) - 32);
+            }
+            if (n == 0) cpy(row[3] + (l / 2) * 2, blk + doff, 2);
+            break;
+        }
+        case GGC_Q5_K: {   // d, dmin, scales[12], qh[32], qs[128] (quant.rs:287-307)
+            const uint64_t b = sp / 2;
+            const int n = (int)(sp % 2);
+            if (b >= nb) return;
+            const uint8_t* blk = src + b * 176;
+            for (int k = 0; k < 4; ++k) cpy(unit(0, k), blk + 48 + 64 * n + 16 * k, 16);
+            if (n == 0) cpy(row[1] + (l / 2) * 4, blk, 4);
+            uint8_t scm[16];
+            unpack_scale_min(blk + 4, scm);
+            cpy(row[2] + l * 8, scm + 4 * n, 4);
+            cpy(row[2] + l * 8 + 4, scm + 8 + 4 * n, 4);
+            // qs byte B = 64n + 4w + j (both nibbles) takes its 5th bit from bit B % 8 of
+            // qh[B / 8]: stored at bit 8 j + w % 8 of word w / 8
+            uint32_t hw[2] = {0, 0};
+            for (int w = 0; w < 16; ++w)
+                for (int j = 0; j < 4; ++j) {
+                    const int B = 64 * n + 4 * w + j;
+                    hw[w / 8] |= (uint32_t)((blk[16 + B / 8] >> (B % 8)) & 1u) << (8 * j + w % 8);
+                }
+            wr32(row[3] + l * 8, hw[0]);
+            wr32(row[3] + l * 8 + 4, hw[1]);
+            break;
+        }
+        case GGC_Q8_K: {   // f32 d, qs[256], bsums (quant.rs:338-344)
+            const uint64_t b = sp / 2;
+            const int n = (int)(sp % 2);
+            if (b >= nb) return;
+            const uint8_t* blk = src + b * 292;
+            for (int k = 0; k < 8; ++k) cpy(unit(0, k), blk + 4 + 128 * n + 16 * k, 16);
+            if (n == 0) cpy(row[1] + (l / 2) * 4, blk, 4);
+            break;
+        }
         default:
             break;
     }
