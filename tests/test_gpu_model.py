@@ -69,6 +69,15 @@ CASES = [
     ("qwen2-0.5b-q8_0-2layers", "qwen2-0.5b-q8_0", 2, None),
     ("llama2-7b-q4_k_m-2layers", "llama2-7b-q4_k_m", 2, None),
     ("llama3-8b-q4_0-1layer", "llama3-8b-q4_0", 1, 32000),
+    # every other block format on the span GEMV, whole model
+    ("mini-q5_k", dict(MINI, weights=13), None, None),
+    ("mini-q3_k_m", dict(MINI, weights=112), None, None),
+    ("mini-q3_k_s", dict(MINI, weights=11, qkv_bias=False), None, None),
+    ("mini-q2_k", dict(MINI, weights=10), None, None),
+    ("mini-q4_1", dict(MINI, weights=3), None, None),
+    ("mini-q5_0", dict(MINI, weights=6, qkv_bias=False), None, None),
+    ("mini-q5_1", dict(MINI, weights=7), None, None),
+    ("mini-q8_k", dict(MINI, weights=15), None, None),
 ]
 
 
