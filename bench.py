@@ -229,8 +229,10 @@ def run_reference(args, rank, world):
 
 def config_block(args, allreduce=None):
     layers = "" if args.layers is None else f", first {args.layers} layers only (profiling case)"
-    return {"workload": f"{MODEL} decode, batch 1, context {args.ctx} (cache prefilled with planted K/V rows so the "
-                        f"timed steps end at {args.ctx}), f32 KV cache{layers}", "global_batch": 1, "seq_len": args.ctx,
+    return {"workload": f"{MODEL} decode, batch 1, context {args.ctx} (K/V rows planted at positions 0..P-1, one "
+                        f"token forwarded at position P, then warm-up and timed steps at positions P+1..{args.ctx - 1}, "
+                        f"each attending to every earlier row), f32 KV cache{layers}", "global_batch": 1,
+            "seq_len": args.ctx,
             "parallelism": parallelism(args, allreduce), "l2": "per-step traffic ~6 GB >> 126 MB L2 (no flush needed)"}
 
 

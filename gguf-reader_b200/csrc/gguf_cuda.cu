@@ -152,15 +152,17 @@ namespace {
 // communicator is aborted (its kernels in flight return; the fused all-reduce's
 // own waits are bounded) and the call fails with GGC_ERR_NCCL.  The context's
 // collectives fail from then on.
-int ctx_sync(ggc_ctx* ctx) {
+// Waits for the context stream, or with `ev` only for the work queued before that
+// event was recorded.
+int ctx_sync(ggc_ctx* ctx, cudaEvent_t ev = nullptr) {
     if (ctx->comm_failed) return set_error(GGC_ERR_NCCL, "communicator aborted earlier (a rank was lost)");
     if (!ctx->comm) {
-        GGC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+        GGC_CUDA_TRY(ev ? cudaEventSynchronize(ev) : cudaStreamSynchronize(ctx->stream));
         return GGC_OK;
     }
     const auto t0 = std::chrono::steady_clock::now();
     for (uint64_t it = 0;; ++it) {
-        const cudaError_t e = cudaStreamQuery(ctx->stream);
+        const cudaError_t e = ev ? cudaEventQuery(ev) : cudaStreamQuery(ctx->stream);
         if (e == cudaSuccess) return GGC_OK;
         if (e != cudaErrorNotReady) return set_error(GGC_ERR_CUDA, "stream: %s", cudaGetErrorString(e));
         ncclResult_t ar = ncclSuccess;
@@ -1428,6 +1430,7 @@ struct ggc_model {
         int errf[ERRF_COUNT];
         unsigned long long key;
     }* rb = nullptr;
+    cudaEvent_t ctl_done = nullptr;   // recorded after each copy of rb->ctl to the device
     // batched prefill (prefill.cuh): raw weights in the layers, activations for
     // PF_CHUNK tokens
     bool prefill = false;
@@ -1920,6 +1923,7 @@ void destroy_model(ggc_model* m) {
         for (void* p : m->ar_peer_maps) cudaIpcCloseMemHandle(p);
         for (void* p : m->allocs) cudaFree(p);
         if (m->rb) cudaFreeHost(m->rb);
+        if (m->ctl_done) cudaEventDestroy(m->ctl_done);
         if (m->logits_host) cudaFreeHost(m->logits_host);
     }
     delete m;
@@ -2195,6 +2199,7 @@ extern "C" int ggc_model_create(ggc_ctx* ctx, const ggc_hparams* hp_in, const gg
     GGC_TRY(dalloc(m.get(), &m->in_pos, hp.max_ctx));
     GGC_TRY(dalloc(m.get(), &m->out_ids, hp.max_ctx));
     GGC_CUDA_TRY(cudaMallocHost((void**)&m->rb, sizeof(*m->rb)));
+    GGC_CUDA_TRY(cudaEventCreateWithFlags(&m->ctl_done, cudaEventDisableTiming));
     GGC_CUDA_TRY(cudaMallocHost((void**)&m->logits_host, (size_t)hp.vocab_size * sizeof(float)));
     StepState s0{};
     s0.done = 1;
@@ -2226,12 +2231,21 @@ extern "C" int ggc_model_destroy(ggc_model* m) {
 namespace {
 
 // Runs `steps` graph replays after setting the control block, then reads back.
+// Queues the copy of the step control words to the device through the pinned
+// block, after the previous copy out of that block has landed (an event, not a
+// wait for the whole stream: a forward on an idle stream starts at once).
+int put_ctl(ggc_model* m, const int32_t (&ctl)[6]) {
+    GGC_TRY(ctx_sync(m->ctx, m->ctl_done));
+    memcpy(&m->rb->ctl, ctl, sizeof(ctl));
+    GGC_CUDA_TRY(cudaMemcpyAsync(m->st, &m->rb->ctl, sizeof(ctl), cudaMemcpyHostToDevice, m->ctx->stream));
+    GGC_CUDA_TRY(cudaEventRecord(m->ctl_done, m->ctx->stream));
+    return GGC_OK;
+}
+
 int run_steps(ggc_model* m, uint64_t n_in, uint64_t max_new, int64_t eos, uint64_t steps) {
     ggc_ctx* ctx = m->ctx;
     int32_t ctl[6] = {0, (int32_t)n_in, (int32_t)max_new, (int32_t)(eos < 0 ? -1 : eos), 0, 0};
-    GGC_TRY(ctx_sync(ctx));   // the pinned control block may still be in flight
-    memcpy(&m->rb->ctl, ctl, sizeof(ctl));
-    GGC_CUDA_TRY(cudaMemcpyAsync(m->st, &m->rb->ctl, sizeof(ctl), cudaMemcpyHostToDevice, ctx->stream));
+    GGC_TRY(put_ctl(m, ctl));
     for (uint64_t i = 0; i < steps; ++i) {
         GGC_CUDA_TRY(cudaGraphLaunch(m->graph, ctx->stream));
         ctx->launches += m->launches_per_step;
@@ -2522,9 +2536,7 @@ extern "C" int ggc_model_decode(ggc_model* m, uint64_t steps, int64_t eos, int s
     ggc_ctx* ctx = m->ctx;
     DeviceGuard g(ctx->device);
     int32_t ctl[6] = {0, 0, (int32_t)steps, (int32_t)(eos < 0 ? -1 : eos), 0, 0};
-    GGC_TRY(ctx_sync(ctx));   // the pinned control block may still be in flight
-    memcpy(&m->rb->ctl, ctl, sizeof(ctl));
-    GGC_CUDA_TRY(cudaMemcpyAsync(m->st, &m->rb->ctl, sizeof(ctl), cudaMemcpyHostToDevice, ctx->stream));
+    GGC_TRY(put_ctl(m, ctl));
     GGC_CUDA_TRY(launch(ctx, k_decode_start, dim3(1), dim3(32), 0, m->st, (const unsigned long long*)m->argmax_key,
                         m->out_ids, m->errf));
     for (uint64_t i = 0; i < steps; ++i) {
