@@ -1,28 +1,28 @@
-// planes.cuh -- the tiled "plane" layout of uploaded weight tensors.
+// planes.cuh -- the tiled layouts of uploaded weight tensors.
 //
 // A raw GGUF tensor stores each block's scale fields and quant bits together
-// (e.g. Q4_K: d, dmin, scales[12], qs[128] = 144 bytes).  At upload the host
-// splits every block into up to four planes:
+// (e.g. Q4_K: d, dmin, scales[12], qs[128] = 144 bytes).  At upload the raw rows
+// are split (on the GPU by k_repack, or on host threads; repack.cuh) into up to
+// four planes: the quant payload and the side data (scales, d, dmin, high bits).
 //
-//   plane 0  the quant payload (qs / ql), a multiple of 16 bytes per block, read
-//            by the GEMV as one 16-byte "chunk" per lane;
-//   plane 1+ the per-block side data (scales, d, dmin, high bits).
+// Each plane is stored tile by tile: a tile is TILE_ROWS (16) rows x one column
+// tile, and the bytes of one tile of one plane are contiguous in HBM (rows at a
+// 16-byte-aligned tile pitch).  The GEMV therefore moves a tile with one large
+// bulk copy per plane: bulk copies of 1 KB or less reach only ~3-4 TB/s on B200,
+// copies of >= 4 KB with >= 128 KB in flight per SM reach > 7 TB/s.
 //
-// Each plane is stored tile by tile: a tile is TILE_ROWS (16) rows x kc columns
-// (kc = 128 chunks of plane 0, the last column tile narrower), and the bytes of
-// one tile of one plane are contiguous in HBM (rows at a 16-byte-aligned tile
-// pitch).  The GEMV therefore moves a tile with one large bulk copy per plane:
-// bulk copies of 1 KB or less reach only ~3-4 TB/s on B200, copies of >= 4 KB
-// with >= 128 KB in flight per SM reach > 7 TB/s.
+// Block formats use the span layout below (k_gemv_span); F16 / BF16 / F32 use the
+// plane layout of plane_spec (k_gemv: 16-byte chunks, 128 per tile row).  The
+// plane_spec entries of the block formats describe the plane layout that k_gemv
+// (instantiated for every format) reads; uploads of block formats use spans.
 //
 // The split keeps every value the reference's dequantiser reads and drops the
 // bytes it never reads (Q3_K_M's 4 bytes at 108..111, Q5_K's qh[16..32), Q8_K's
 // bsums).  High-bit fields (Q5_0/Q5_1/Q5_K qh, Q3_K hmask) are bit-permuted so
-// that the four bits a lane needs for four consecutive bytes sit at bit k of
-// byte k of one 32-bit word (one shift + one mask).  The 12 packed bytes of the
-// Q4_K/Q5_K 6-bit (scale, min) pairs are unpacked with the reference's
-// k_scale_min_6bit (quant.rs:116-124) into sc[8], mn[8] bytes, so the GEMV reads
-// a scale with one byte extract.
+// that the bits a lane needs for four consecutive bytes sit one per byte of a
+// 32-bit word (one shift + one mask).  The 12 packed bytes of the Q4_K/Q5_K 6-bit
+// (scale, min) pairs are unpacked with the reference's k_scale_min_6bit
+// (quant.rs:116-124), so the GEMV reads a scale with one byte extract.
 #pragma once
 #include "common.cuh"
 
