@@ -208,6 +208,37 @@ def cpu_decode(hp, ts, ctx_len, tokens, warmup=1):
                        f"rms residual {resid * 1e3:.2f} ms")
 
 
+def cpu_matvec_sweep(dtypes, shapes, seed=77, reps=2):
+    """quant_matvec of the oracle (the reference's quant.rs:526-570 restated: block
+    dequant, then one serial multiply-add per element, rows split over the host
+    threads) for every format and sweep shape: the same seeded weights as the GPU
+    sweep, x ~ N(0, 1) seed 1, median of `reps` after a warm-up; GB/s of the same
+    algorithmic bytes (W + 4 cols + 4 rows)."""
+    from gguf_cuda import synth
+    from gguf_cuda._lib import DTYPE_NAMES
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+    oracle.build()
+    out = {}
+    t_all = time.perf_counter()
+    for dt in dtypes:
+        for rows, cols in shapes:
+            raw = synth.random_blocks(dt, rows * cols, synth.rng_for(seed, dt, rows, cols))
+            x = np.random.default_rng(1).normal(size=cols).astype(np.float32)
+            oracle.quant_matvec(raw, dt, rows, cols, x)
+            t = []
+            for _ in range(reps):
+                t0 = time.perf_counter()
+                oracle.quant_matvec(raw, dt, rows, cols, x)
+                t.append(time.perf_counter() - t0)
+            per = statistics.median(t)
+            alg = raw.nbytes + 4 * cols + 4 * rows
+            out[f"{DTYPE_NAMES[dt]}_{rows}x{cols}"] = {"ms": per * 1e3, "gbs": alg / per / 1e9}
+    return {"threads": oracle.get_threads(), "seconds": time.perf_counter() - t_all,
+            "what": "oracle quant_matvec (reference quant.rs:526-570 restated), all host threads, "
+                    f"median of {reps} after a warm-up, GB/s of W + 4 cols + 4 rows", "entries": out}
+
+
 def run_reference(args, rank, world):
     """The reference's CPU path (the oracle port; the Rust crate cannot be built
     here) on the host cores: W warm-up tokens, then K timed tokens, each one
@@ -286,7 +317,7 @@ def time_matvec(ggc, ctx, torch, stream, dt, rows, cols, peak_gbs, seed=77, min_
     del tensors
     return name, {"us_per_launch": per * 1e6, "algorithmic_bytes": alg, "gbs": alg / per / 1e9,
                   "frac_of_peak": alg / per / 1e9 / peak_gbs,
-                  "kernel": "k_gemv_span" if dt in (ggc.Q4_K, ggc.Q6_K, ggc.Q4_0, ggc.Q8_0) else "k_gemv"}
+                  "kernel": "k_gemv" if dt in (ggc.F16, ggc.BF16, ggc.F32) else "k_gemv_span"}
 
 
 SWEEP_SHAPES = [(4096, 4096), (11008, 4096), (4096, 11008)]
@@ -610,6 +641,8 @@ def run_ours(args, rank, world, local_rank):
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             cpu = cpu_decode(hp, ts, C, tokens=8, warmup=1)
+            if args.sweep:   # the format sweep on the host cores, beside the GPU's
+                cpu["matvec"] = cpu_matvec_sweep([d for d in ggc.ALL_DTYPES if d != ggc.F32], SWEEP_SHAPES)
         result = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": elapsed / K * 1e3, "higher_is_better": True, "scaling": "strong" if tp else "weak",
