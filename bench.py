@@ -295,7 +295,7 @@ def time_matvec(ggc, ctx, torch, stream, dt, rows, cols, peak_gbs, seed=77, min_
     wbytes = raw.nbytes
     copies = max(2, int(np.ceil(2 * 126e6 / wbytes)) + 1)
     tensors = [ggc.Tensor(raw, dt, (cols, rows), ctx=ctx) for _ in range(copies)]
-    x = torch.randn(cols, device="cuda", dtype=torch.float32)
+    x = torch.from_numpy(np.random.default_rng(1).normal(size=cols).astype(np.float32)).cuda()   # x ~ N(0, 1), seed 1
     y = torch.empty(rows, device="cuda", dtype=torch.float32)
     torch.cuda.synchronize()
     for t in tensors:
