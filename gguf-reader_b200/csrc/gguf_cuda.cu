@@ -569,7 +569,8 @@ bool host_repack() {
 // Splits raw rows into planes and uploads them.  Default: the raw rows go to the
 // GPU (gathered in output order on the host when row_src selects or reorders
 // them) and k_repack splits them there; GGC_REPACK=host splits them on host
-// threads and uploads the planes.  `raw` is host memory.
+// threads and uploads the planes.  `raw` is host memory, or device memory when
+// row_src is null and the split runs on the GPU.
 int upload_mat(ggc_ctx* ctx, const void* raw, uint64_t raw_bytes, int dt, uint64_t rows, uint64_t cols,
                const uint32_t* row_src, DevMat& out) {
     const int bs = block_size_of(dt), bb = block_bytes_of(dt);
@@ -621,10 +622,10 @@ int upload_mat(ggc_ctx* ctx, const void* raw, uint64_t raw_bytes, int dt, uint64
         uint8_t* draw = nullptr;
         e = cudaMalloc(&draw, rows * row_bytes);
         if (e == cudaSuccess) e = cudaMemsetAsync(m.base, 0, total, ctx->stream);
-        if (e == cudaSuccess) e = cudaMemcpyAsync(draw, src, rows * row_bytes, cudaMemcpyHostToDevice, ctx->stream);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(draw, src, rows * row_bytes, cudaMemcpyDefault, ctx->stream);
         if (e == cudaSuccess) {
             const uint64_t n = rows * rp::units_per_row(dt, L, cols);
-            const uint64_t grid = std::min<uint64_t>((n + 255) / 256, 148ull * 16);
+            const uint64_t grid = std::min<uint64_t>((n + 255) / 256, (uint64_t)ctx->num_sms * 16);
             uint8_t* pp[4];
             for (int p = 0; p < 4; ++p) pp[p] = p < ps.n ? m.base + off[p] : nullptr;
             e = launch(ctx, k_repack, dim3((unsigned)grid), dim3(256), 0, dt, (const uint8_t*)draw, rows, cols, row_bytes,

@@ -120,8 +120,10 @@ int ggc_quant_matvec_static(int dtype, const void* w, uint64_t w_len, uint64_t r
  *      src/infer/model/llama.rs:183-204; weights stay quantized in HBM) ------- */
 typedef struct ggc_tensor ggc_tensor;
 
-/* Uploads one GGUF tensor (ne[0] contiguous).  repack != 0 stores it in the
- * coalesced plane layout used by the decode kernels (a lossless byte permutation). */
+/* Uploads one GGUF tensor (ne[0] contiguous; raw in host or device memory).
+ * repack != 0 stores it in the tiled layout the decode GEMVs read (a lossless
+ * byte permutation, done on the GPU; with GGC_REPACK=host on host threads, which
+ * needs raw in host memory). */
 int ggc_tensor_upload(ggc_ctx* ctx, const void* raw, uint64_t bytes, int dtype, const uint64_t* ne,
                       int ndim, int repack, ggc_tensor** out);
 int ggc_tensor_free(ggc_tensor* t);

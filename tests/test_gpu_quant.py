@@ -186,3 +186,19 @@ def test_device_repack_matches_host_repack(ggc, orc, ctx, dt, monkeypatch):
         monkeypatch.delenv("GGC_REPACK")
         assert same_bits(dev, host), (DTYPE_NAMES[dt], rows, cols)
         assert rel_l2(dev, orc.quant_matvec(w, dt, rows, cols, x)) <= REL_L2
+
+
+@pytest.mark.parametrize("dt", [12, 112, 1], ids=["Q4_K", "Q3_K_M", "F16"])
+def test_repacked_upload_from_device_memory(ggc, ctx, dt):
+    """ggc_tensor_upload(repack=1) of raw bytes already in device memory gives the
+    same tensor as an upload from host memory (the split runs on the GPU either way)."""
+    import torch
+    rows, cols = 33, 4096 + 256
+    rng = synth.rng_for(24, dt)
+    w = synth.random_blocks(dt, rows * cols, rng)
+    x = rng.normal(0.0, 1.0, size=cols).astype(np.float32)
+    dw = torch.from_numpy(w.copy()).cuda()
+    torch.cuda.synchronize()
+    from_dev = ggc.Tensor(dw, dt, (cols, rows), repack=True, ctx=ctx).matvec(x)
+    from_host = ggc.Tensor(w, dt, (cols, rows), repack=True, ctx=ctx).matvec(x)
+    assert same_bits(from_dev, from_host)
