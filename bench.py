@@ -239,6 +239,12 @@ def cpu_matvec_sweep(dtypes, shapes, seed=77, reps=2):
                     f"median of {reps} after a warm-up, GB/s of W + 4 cols + 4 rows", "entries": out}
 
 
+def planted_rows(C, W, K):
+    """K/V rows planted before the decode timing: one forward at position P, then
+    max(W - 1, 0) warm-up steps and K timed steps end at context C."""
+    return C - max(W, 1) - K
+
+
 def run_reference(args, rank, world):
     """The reference's CPU path (the oracle port; the Rust crate cannot be built
     here) on the host cores: W warm-up tokens, then K timed tokens, each one
@@ -553,7 +559,7 @@ def run_ours(args, rank, world, local_rank):
 
     hp, ts = synth.make_model(MODEL, seed=0, n_layers=args.layers)
     W, K, C = args.warmup, args.steps, args.ctx
-    P = C - max(W, 1) - K   # planted rows; one forward + max(W - 1, 0) warm-up + K timed steps end at C
+    P = planted_rows(C, W, K)
     assert P >= 1, "context too small for warmup + steps"
     t_load = time.perf_counter()
     model = ggc.LlamaModel(hp, ts, max_ctx=C, ctx=ctx)   # raw rows uploaded, split into planes on the GPU
